@@ -1,0 +1,684 @@
+// LD_PRELOAD NCCL interposer for one process driving 1..8 GPUs.
+//
+// Exports the NCCL C ABI. Grouped AllReduce / AllGather / ReduceScatter /
+// Broadcast calls over a clique (communicators created together) are planned
+// and run by the sm_100a kernels; every other call, and every call the gates
+// reject, goes unchanged to the real libnccl.
+//
+// Error policy: a CUDA failure before a call's first copy or kernel falls
+// back to NCCL; a failure at or after it returns ncclUnhandledCudaError
+// (never an NCCL replay over half-written buffers), drains the clique's
+// devices and disables the custom paths for the process (poison).
+//
+// Parity: Layer 5 of the reference (shim/nccl_collectives_shim.cu:1196-1953):
+// symbol resolution, version gate, call model, group buffering, pair
+// registry, init interposers with prewarm, runtime checks, pair runner,
+// GroupEnd with device restore, and the passthrough wrappers.
+#include <dlfcn.h>
+
+#include <cstddef>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+#include "abi/runtime.h"
+#include "core/gate.h"
+#include "core/plan.h"
+#include "exec/calib.h"
+#include "exec/nvls.h"
+
+#ifndef NB_BUILD_ID
+#define NB_BUILD_ID "dev"
+#endif
+
+namespace nb {
+
+const char* build_id() { return NB_BUILD_ID; }
+
+namespace {
+
+struct ExitSummary {
+  ~ExitSummary() {
+    Runtime& r = rt();
+    if (!r.summary.enabled()) return;
+    for (const std::string& line : r.summary.render(build_id()))
+      std::fprintf(stderr, "[nccl-shim-summary] %s\n", line.c_str());
+  }
+};
+
+void* g_real_handle = nullptr;
+
+template <typename Fn>
+void resolve_one(const char* sym, Fn& fn, bool required) {
+  void* p = dlsym(RTLD_NEXT, sym);
+  if (!p) {
+    if (!g_real_handle) g_real_handle = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD | RTLD_GLOBAL);
+    if (!g_real_handle) {
+      const char* path = std::getenv("NCCL_B200_REAL_NCCL");
+      g_real_handle = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    }
+    if (g_real_handle) p = dlsym(g_real_handle, sym);
+  }
+  fn = reinterpret_cast<Fn>(p);
+  if (!fn && required) {
+    std::fprintf(stderr, "[nccl-b200] cannot resolve %s in the real libnccl: %s\n", sym, dlerror());
+    std::abort();
+  }
+}
+
+thread_local GroupState g_group;
+thread_local unsigned g_init_all_depth = 0;
+
+}  // namespace
+
+Runtime& rt() {
+  static Runtime* r = [] {
+    Runtime* x = new Runtime();
+    x->policy = policy_from_env([](const char* k) { return std::getenv(k); });
+    x->summary.set_enabled(x->policy.summary);
+    if (!x->fault.configure(x->policy.fault))
+      std::fprintf(stderr, "[nccl-b200] ignoring malformed NCCL_B200_FAULT=%s\n", x->policy.fault.c_str());
+    x->exec.set_policy(x->policy);
+    x->exec.set_summary(&x->summary);
+    return x;
+  }();
+  static ExitSummary exit_summary;
+  return *r;
+}
+
+void* real_symbol(const char* name) {
+  void* p = dlsym(RTLD_NEXT, name);
+  if (!p && g_real_handle) p = dlsym(g_real_handle, name);
+  return p;
+}
+
+void resolve_all() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    RealNccl& n = rt().real;
+    resolve_one("ncclGetVersion", n.GetVersion, true);
+    resolve_one("ncclCommGetAsyncError", n.CommGetAsyncError, true);
+    resolve_one("ncclAllReduce", n.AllReduce, true);
+    resolve_one("ncclAllGather", n.AllGather, true);
+    resolve_one("ncclReduceScatter", n.ReduceScatter, true);
+    resolve_one("ncclBroadcast", n.Broadcast, true);
+    resolve_one("ncclGroupStart", n.GroupStart, true);
+    resolve_one("ncclGroupEnd", n.GroupEnd, true);
+    resolve_one("ncclGroupSimulateEnd", n.GroupSimulateEnd, false);
+    resolve_one("ncclCommCuDevice", n.CommCuDevice, true);
+    resolve_one("ncclCommUserRank", n.CommUserRank, true);
+    resolve_one("ncclCommCount", n.CommCount, true);
+    resolve_one("ncclCommInitAll", n.CommInitAll, true);
+    resolve_one("ncclCommInitRank", n.CommInitRank, true);
+    resolve_one("ncclCommInitRankConfig", n.CommInitRankConfig, true);
+    resolve_one("ncclCommDestroy", n.CommDestroy, true);
+    int version = 0;
+    Runtime& r = rt();
+    r.nccl_version = n.GetVersion(&version) == ncclSuccess ? version : 0;
+    r.nccl_supported = r.nccl_version >= r.policy.min_nccl_version &&
+                       r.nccl_version <= r.policy.max_nccl_version;
+  });
+}
+
+Shares shares_for(Algo a, int n, const CallDesc& c) {
+  Runtime& r = rt();
+  Shares s = r.calibrated_done ? shares_from(last_calibration(), a, n) : Shares{};
+  if (r.policy.host_share_ppm >= 0) s.host_ppm = r.policy.host_share_ppm;
+  if (r.policy.ce_share_ppm >= 0) s.ce_ppm = r.policy.ce_share_ppm;
+  if (n <= 1 || a == Algo::ArNvls) s.host_ppm = s.ce_ppm = 0;
+  // Device-resident PreMulSum scalars cannot be applied by the host fold.
+  if (c.op == RedOp::PreMulSum && c.scalar_residence == 0) s.host_ppm = 0;
+  if (a == Algo::RsPull || a == Algo::BcScatter) s.ce_ppm = 0;
+  return s;
+}
+
+void prewarm(const int* devices, int n) {
+  Runtime& r = rt();
+  std::lock_guard<std::mutex> lk(r.exec_mu);
+  std::string why;
+  if (!r.exec.setup(devices, n, &why)) {
+    cudaGetLastError();
+    if (r.summary.enabled()) r.summary.note("prewarm_failed " + why);
+    return;
+  }
+  if (!r.calibrated_done && r.policy.calibrate && n > 1) {
+    r.calibrated = calibrate_shares(devices, n, r.policy, &r.summary);
+    r.calibrated_done = true;
+  }
+  Shares s = r.calibrated;
+  if (r.policy.host_share_ppm >= 0) s.host_ppm = r.policy.host_share_ppm;
+  const bool nvls = r.policy.nvls != NvlsMode::Off && nvls_supported(devices, n);
+  const Needs needs = prewarm_needs(n, r.policy, s, nvls);
+  if (!r.exec.ensure(needs, devices, n, &why)) {
+    cudaGetLastError();
+    if (r.summary.enabled()) r.summary.note("prewarm_failed " + why);
+  }
+  r.exec.drain(devices, n);
+}
+
+namespace {
+
+// The GroupBackend the group state machine drives in the library.
+class RealBackend final : public GroupBackend {
+ public:
+  int real_group_start() override { return rt().real.GroupStart(); }
+  int real_group_end() override { return rt().real.GroupEnd(); }
+  int real_simulate_end(void* info) override {
+    auto fn = rt().real.GroupSimulateEnd;
+    return fn ? fn(static_cast<ncclSimInfo_t*>(info)) : ncclInvalidUsage;
+  }
+  int forward(const Call& c, Reason reason) override {
+    const RealNccl& n = rt().real;
+    rt().summary.count_fallback(reason);
+    const auto dt = static_cast<ncclDataType_t>(c.nccl_dtype);
+    const auto op = static_cast<ncclRedOp_t>(c.nccl_op);
+    const auto comm = static_cast<ncclComm_t>(c.comm);
+    const auto stream = static_cast<cudaStream_t>(c.stream);
+    switch (c.desc.kind) {
+      case Kind::AllGather: return n.AllGather(c.sendbuff, c.recvbuff, c.desc.count, dt, comm, stream);
+      case Kind::ReduceScatter:
+        return n.ReduceScatter(c.sendbuff, c.recvbuff, c.desc.count, dt, op, comm, stream);
+      case Kind::Broadcast:
+        return n.Broadcast(c.sendbuff, c.recvbuff, c.desc.count, dt, c.desc.root, comm, stream);
+      default: return n.AllReduce(c.sendbuff, c.recvbuff, c.desc.count, dt, op, comm, stream);
+    }
+  }
+  bool query(Call& c) override {
+    const RealNccl& n = rt().real;
+    const auto comm = static_cast<ncclComm_t>(c.comm);
+    return n.CommCuDevice(comm, &c.desc.device) == ncclSuccess &&
+           n.CommUserRank(comm, &c.desc.rank) == ncclSuccess &&
+           n.CommCount(comm, &c.desc.nranks) == ncclSuccess;
+  }
+  const Policy& policy() override { return rt().policy; }
+  Outcome run(std::vector<Call>& calls, Reason& reason) override;
+};
+
+RealBackend g_backend;
+GroupMachine g_machine(g_backend);
+
+bool runtime_checks(Runtime& r, const std::vector<Call>& calls, const CliqueInfo& info) {
+  for (const Call& c : calls) {
+    ncclResult_t async = ncclSuccess;
+    if (r.real.CommGetAsyncError(static_cast<ncclComm_t>(c.comm), &async) != ncclSuccess ||
+        async != ncclSuccess) {
+      r.cliques.forget(c.comm);
+      return false;
+    }
+    const int dev = c.desc.device;
+    int stream_dev = -1;
+    if (cudaSetDevice(dev) != cudaSuccess ||
+        cudaStreamGetDevice(static_cast<cudaStream_t>(c.stream), &stream_dev) != cudaSuccess ||
+        stream_dev != dev) {
+      cudaGetLastError();
+      return false;
+    }
+    if (!supported_buffer(c.recvbuff, recv_extent(c.desc), dev, info.devices, info.nranks)) return false;
+    const bool bcast_nonroot = c.desc.kind == Kind::Broadcast && c.desc.rank != c.desc.root;
+    if (!bcast_nonroot &&
+        !supported_buffer(c.sendbuff, send_extent(c.desc), dev, info.devices, info.nranks))
+      return false;
+  }
+  return true;
+}
+
+Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
+  Runtime& r = rt();
+  std::lock_guard<std::mutex> lk(r.exec_mu);
+  CliqueState st;
+  st.poisoned = r.poisoned;
+  st.nccl_supported = r.nccl_supported;
+  st.first_pass_done = r.first_pass_done;
+  std::vector<void*> comms;
+  std::vector<CallDesc> descs;
+  for (const Call& c : calls) {
+    comms.push_back(c.comm);
+    descs.push_back(c.desc);
+  }
+  CliqueInfo info;
+  st.known_clique = r.cliques.same_clique(comms, &info);
+  if (st.known_clique) {
+    // The registered devices must be the ones the communicators report.
+    for (const Call& c : calls)
+      if (c.desc.rank < 0 || c.desc.rank >= info.nranks || info.devices[c.desc.rank] != c.desc.device ||
+          info.comms[c.desc.rank] != c.comm)
+        st.known_clique = false;
+  }
+  if (st.known_clique) {
+    for (const Call& c : calls)
+      if (stream_capturing(static_cast<cudaStream_t>(c.stream), c.desc.device)) st.capturing = true;
+    st.nvls_available = r.policy.nvls != NvlsMode::Off && nvls_supported(info.devices, info.nranks);
+  }
+  const CliqueDecision d = gate_clique(descs, st, r.policy);
+  reason = d.reason;
+  if (d.reason == Reason::FirstPass) r.first_pass_done = true;
+  if (d.algo == Algo::Fallback) return Outcome::Fallback;
+  reason = Reason::RuntimeUnsupported;
+  if (!runtime_checks(r, calls, info)) return Outcome::Fallback;
+
+  const int n = info.nranks;
+  Binding b;
+  b.nranks = n;
+  const Call* by_rank[kMaxRanks] = {};
+  for (const Call& c : calls) by_rank[c.desc.rank] = &c;
+  b.fold.dtype = descs[0].dtype;
+  b.fold.op = descs[0].op;
+  b.fold.nranks = n;
+  for (int q = 0; q < n; ++q) {
+    const Call& c = *by_rank[q];
+    b.device[q] = c.desc.device;
+    b.stream[q] = static_cast<cudaStream_t>(c.stream);
+    b.send[q] = c.sendbuff;
+    b.recv[q] = c.recvbuff;
+    b.fold.scalars[q] = c.desc.scalar;
+    b.dev_scalar[q] = c.desc.op == RedOp::PreMulSum && c.desc.scalar_residence == 0
+                          ? reinterpret_cast<const void*>(c.desc.scalar_ptr)
+                          : nullptr;
+  }
+  // A Broadcast non-root's send pointer is never read.
+  const Shares shares = shares_for(d.algo, n, descs[0]);
+  Plan plan;
+  build_plan(d.algo, describe_clique(descs), r.policy, shares, plan);
+
+  std::string why;
+  if (r.fault.fail_setup() || !r.exec.ensure(plan.needs, info.devices, n, &why)) {
+    cudaGetLastError();
+    reason = Reason::SetupFailed;
+    return Outcome::Fallback;
+  }
+  cudaError_t error = cudaSuccess;
+  const ExecStatus status = r.exec.execute(plan, b, &error, &r.fault);
+  if (status == ExecStatus::Failed) {
+    r.poisoned = true;
+    std::fprintf(stderr,
+                 "[nccl-b200] %s: CUDA error after custom work was enqueued (%s); returning "
+                 "ncclUnhandledCudaError, custom paths disabled for this process\n",
+                 kind_name(descs[0].kind), cudaGetErrorString(error));
+    r.exec.drain(info.devices, n);
+    cudaGetLastError();
+    return Outcome::Error;
+  }
+  if (status == ExecStatus::Ok) {
+    r.summary.count_custom(d.algo, logical_bytes(descs[0]), n, plan.sm_bytes, plan.ce_bytes,
+                           plan.host_bytes);
+    return Outcome::Handled;
+  }
+  cudaGetLastError();  // consumed here; NCCL must not see it
+  reason = Reason::SubmitFailedEarly;
+  return Outcome::Fallback;
+}
+
+RedOp to_op(int op, void* comm, CallDesc& d) {
+  if (op >= 0 && op < nccl::NumOps) return RedOp(op);  // Sum Prod Max Min Avg
+  PreMulScalar s;
+  if (rt().cliques.find_premul(comm, op, &s) && s.dtype == d.dtype) {
+    d.scalar_residence = s.residence;
+    d.scalar = s.value;
+    d.scalar_ptr = s.device_ptr;
+    return RedOp::PreMulSum;
+  }
+  return RedOp::Unsupported;
+}
+
+Call make_call(Kind kind, const void* sendbuff, void* recvbuff, size_t count, ncclDataType_t dt,
+               ncclRedOp_t op, int root, ncclComm_t comm, cudaStream_t stream) {
+  Call c;
+  c.sendbuff = sendbuff;
+  c.recvbuff = recvbuff;
+  c.nccl_dtype = int(dt);
+  c.nccl_op = int(op);
+  c.comm = comm;
+  c.stream = stream;
+  c.desc.kind = kind;
+  c.desc.dtype = dtype_from_nccl(int(dt));
+  c.desc.op = reduces(kind) ? to_op(int(op), comm, c.desc) : RedOp::Sum;
+  c.desc.count = count;
+  c.desc.send = reinterpret_cast<uintptr_t>(sendbuff);
+  c.desc.recv = reinterpret_cast<uintptr_t>(recvbuff);
+  c.desc.root = root;
+  return c;
+}
+
+bool blocking_configuration(const ncclConfig_t* config) {
+  const char* env = std::getenv("NCCL_COMM_BLOCKING");
+  if (env && std::strcmp(env, "1") != 0) return false;
+  if (!config) return true;
+  const Policy& p = rt().policy;
+  return config->size >= offsetof(ncclConfig_t, blocking) + sizeof(config->blocking) &&
+         config->magic == 0xcafebeef && int(config->version) >= p.min_nccl_version &&
+         int(config->version) <= p.max_nccl_version &&
+         (config->blocking == 1 || config->blocking == NCCL_CONFIG_UNDEF_INT);
+}
+
+bool distinct_devices(const int* devs, int n) {
+  for (int i = 0; i < n; ++i) {
+    if (devs[i] < 0) return false;
+    for (int j = 0; j < i; ++j)
+      if (devs[i] == devs[j]) return false;
+  }
+  return true;
+}
+
+// Register a clique from communicators, checking each one's device, rank and
+// async state with libnccl.
+bool register_clique(ncclComm_t* comms_by_rank, int n) {
+  Runtime& r = rt();
+  int devices[kMaxRanks];
+  void* comms[kMaxRanks];
+  for (int i = 0; i < n; ++i) {
+    int rank = -1, count = -1;
+    ncclResult_t async = ncclSuccess;
+    if (!comms_by_rank[i] || r.real.CommCuDevice(comms_by_rank[i], &devices[i]) != ncclSuccess ||
+        r.real.CommUserRank(comms_by_rank[i], &rank) != ncclSuccess || rank != i ||
+        r.real.CommCount(comms_by_rank[i], &count) != ncclSuccess || count != n ||
+        r.real.CommGetAsyncError(comms_by_rank[i], &async) != ncclSuccess || async != ncclSuccess)
+      return false;
+    comms[i] = comms_by_rank[i];
+  }
+  if (!distinct_devices(devices, n)) return false;
+  if (r.cliques.add(comms, devices, n) < 0) return false;
+  r.summary.note_clique(n, devices);
+  return true;
+}
+
+void note_initialization(ncclResult_t result, ncclComm_t* output, int nranks, ncclUniqueId id,
+                         int rank, bool blocking) {
+  if (g_init_all_depth) return;
+  Runtime& r = rt();
+  if (g_group.depth == 0) {
+    // An ungrouped one-rank communicator is a clique of one.
+    if (result == ncclSuccess && r.nccl_supported && blocking && output && nranks == 1 && rank == 0 &&
+        register_clique(output, 1)) {
+      int dev = -1;
+      int caller = -1;
+      if (r.real.CommCuDevice(*output, &dev) == ncclSuccess && cudaGetDevice(&caller) == cudaSuccess) {
+        prewarm(&dev, 1);
+        cudaSetDevice(caller);
+      }
+    }
+    return;
+  }
+  if (!r.nccl_supported || result != ncclSuccess || !blocking || !output || nranks < 1 ||
+      nranks > kMaxRanks || rank < 0 || rank >= nranks) {
+    g_group.init_only = false;
+    return;
+  }
+  // Grouped init may defer writing *output until the outer native GroupEnd.
+  PendingInit p;
+  p.output = reinterpret_cast<void**>(output);
+  std::memcpy(p.id, id.internal, sizeof(p.id));
+  p.rank = rank;
+  p.nranks = nranks;
+  g_group.inits.push_back(p);
+}
+
+void register_initializations() {
+  Runtime& r = rt();
+  if (!r.nccl_supported || !g_group.init_only || !inits_form_clique(g_group.inits)) return;
+  const int n = int(g_group.inits.size());
+  ncclComm_t by_rank[kMaxRanks] = {};
+  for (const PendingInit& p : g_group.inits) by_rank[p.rank] = static_cast<ncclComm_t>(*p.output);
+  if (!register_clique(by_rank, n)) return;
+  CliqueInfo info;
+  int caller = -1;
+  if (r.cliques.lookup(by_rank[0], &info) && cudaGetDevice(&caller) == cudaSuccess) {
+    prewarm(info.devices, n);
+    cudaSetDevice(caller);
+  }
+}
+
+int force_passthrough(bool initialization = false) {
+  return g_machine.force_passthrough(g_group, initialization);
+}
+
+template <typename Fn>
+Fn real_fn(const char* name) {
+  resolve_all();
+  return reinterpret_cast<Fn>(real_symbol(name));
+}
+
+}  // namespace
+}  // namespace nb
+
+using namespace nb;
+
+extern "C" {
+
+ncclResult_t ncclGroupStart() {
+  resolve_all();
+  return ncclResult_t(g_machine.group_start(g_group));
+}
+
+ncclResult_t ncclGroupEnd() {
+  resolve_all();
+  int caller = -1;
+  const cudaError_t get_error = cudaGetDevice(&caller);
+  const bool outer = g_group.depth == 1;
+  const int result = g_machine.group_end(g_group);
+  const cudaError_t restore = get_error == cudaSuccess ? cudaSetDevice(caller) : get_error;
+  if (outer) {
+    if (result == ncclSuccess && restore == cudaSuccess) register_initializations();
+    g_group.inits.clear();
+  }
+  if (restore != cudaSuccess) return result == ncclSuccess ? ncclUnhandledCudaError : ncclResult_t(result);
+  return ncclResult_t(result);
+}
+
+ncclResult_t ncclGroupSimulateEnd(ncclSimInfo_t* info) {
+  resolve_all();
+  return ncclResult_t(g_machine.simulate_end(g_group, info));
+}
+
+ncclResult_t ncclCommInitAll(ncclComm_t* comms, int ndev, const int* devlist) {
+  resolve_all();
+  Runtime& r = rt();
+  const bool outer = g_group.depth == 0;
+  const int prefix = force_passthrough();
+  if (prefix != ncclSuccess) return ncclResult_t(prefix);
+  int devs[kMaxRanks] = {};
+  bool clique = outer && r.nccl_supported && blocking_configuration(nullptr) && ndev >= 1 &&
+                ndev <= kMaxRanks;
+  if (clique) {
+    for (int i = 0; i < ndev; ++i) devs[i] = devlist ? devlist[i] : i;
+    clique = distinct_devices(devs, ndev);
+  }
+  bool restored = true;
+  if (clique) {
+    int caller = -1;
+    if (cudaGetDevice(&caller) == cudaSuccess) {
+      prewarm(devs, ndev);
+      restored = cudaSetDevice(caller) == cudaSuccess;
+    }
+  }
+  ++g_init_all_depth;
+  const ncclResult_t res = r.real.CommInitAll(comms, ndev, devlist);
+  --g_init_all_depth;
+  if (res == ncclSuccess && clique && restored && comms) register_clique(comms, ndev);
+  if (res == ncclSuccess && !restored) return ncclUnhandledCudaError;
+  return res;
+}
+
+ncclResult_t ncclCommInitRank(ncclComm_t* comm, int nranks, ncclUniqueId commId, int rank) {
+  resolve_all();
+  const int prefix = force_passthrough(true);
+  if (prefix != ncclSuccess) return ncclResult_t(prefix);
+  const ncclResult_t res = rt().real.CommInitRank(comm, nranks, commId, rank);
+  note_initialization(res, comm, nranks, commId, rank, blocking_configuration(nullptr));
+  return res;
+}
+
+ncclResult_t ncclCommInitRankConfig(ncclComm_t* comm, int nranks, ncclUniqueId commId, int rank,
+                                    ncclConfig_t* config) {
+  resolve_all();
+  const int prefix = force_passthrough(true);
+  if (prefix != ncclSuccess) return ncclResult_t(prefix);
+  const ncclResult_t res = rt().real.CommInitRankConfig(comm, nranks, commId, rank, config);
+  note_initialization(res, comm, nranks, commId, rank, blocking_configuration(config));
+  return res;
+}
+
+ncclResult_t ncclCommDestroy(ncclComm_t comm) {
+  resolve_all();
+  const int prefix = force_passthrough();
+  rt().cliques.forget(comm);
+  return prefix != ncclSuccess ? ncclResult_t(prefix) : rt().real.CommDestroy(comm);
+}
+
+ncclResult_t ncclAllReduce(const void* sendbuff, void* recvbuff, size_t count,
+                           ncclDataType_t datatype, ncclRedOp_t op, ncclComm_t comm,
+                           cudaStream_t stream) {
+  resolve_all();
+  return ncclResult_t(g_machine.enqueue(
+      g_group, make_call(Kind::AllReduce, sendbuff, recvbuff, count, datatype, op, -1, comm, stream)));
+}
+
+ncclResult_t ncclAllGather(const void* sendbuff, void* recvbuff, size_t sendcount,
+                           ncclDataType_t datatype, ncclComm_t comm, cudaStream_t stream) {
+  resolve_all();
+  return ncclResult_t(g_machine.enqueue(
+      g_group, make_call(Kind::AllGather, sendbuff, recvbuff, sendcount, datatype, ncclSum, -1, comm, stream)));
+}
+
+ncclResult_t ncclReduceScatter(const void* sendbuff, void* recvbuff, size_t recvcount,
+                               ncclDataType_t datatype, ncclRedOp_t op, ncclComm_t comm,
+                               cudaStream_t stream) {
+  resolve_all();
+  return ncclResult_t(g_machine.enqueue(
+      g_group, make_call(Kind::ReduceScatter, sendbuff, recvbuff, recvcount, datatype, op, -1, comm, stream)));
+}
+
+ncclResult_t ncclBroadcast(const void* sendbuff, void* recvbuff, size_t count,
+                           ncclDataType_t datatype, int root, ncclComm_t comm, cudaStream_t stream) {
+  resolve_all();
+  return ncclResult_t(g_machine.enqueue(
+      g_group, make_call(Kind::Broadcast, sendbuff, recvbuff, count, datatype, ncclSum, root, comm, stream)));
+}
+
+// Legacy in-place broadcast, interposed so a buffered clique set cannot be
+// reordered around it.
+ncclResult_t ncclBcast(void* buff, size_t count, ncclDataType_t datatype, int root, ncclComm_t comm,
+                       cudaStream_t stream) {
+  return ncclBroadcast(buff, buff, count, datatype, root, comm, stream);
+}
+
+// ---- Unsupported operations: visible to the group state machine ----------
+
+#define NB_PASSTHROUGH(ret_expr_name, sig, args)                                        \
+  ncclResult_t ret_expr_name sig {                                                      \
+    using Fn = decltype(&::ret_expr_name);                                              \
+    static const Fn real = real_fn<Fn>(#ret_expr_name);                                 \
+    const int prefix = force_passthrough();                                             \
+    if (prefix != ncclSuccess) return ncclResult_t(prefix);                             \
+    return real ? real args : ncclInvalidUsage;                                         \
+  }
+
+#define NB_LIFECYCLE(ret_expr_name, sig, comm_arg, args)                                \
+  ncclResult_t ret_expr_name sig {                                                      \
+    using Fn = decltype(&::ret_expr_name);                                              \
+    static const Fn real = real_fn<Fn>(#ret_expr_name);                                 \
+    const int prefix = force_passthrough();                                             \
+    rt().cliques.forget(comm_arg);                                                      \
+    if (prefix != ncclSuccess) return ncclResult_t(prefix);                             \
+    return real ? real args : ncclInvalidUsage;                                         \
+  }
+
+NB_PASSTHROUGH(ncclReduce, (const void* s, void* r, size_t n, ncclDataType_t t, ncclRedOp_t o, int root,
+                            ncclComm_t c, cudaStream_t st), (s, r, n, t, o, root, c, st))
+NB_PASSTHROUGH(ncclSend, (const void* s, size_t n, ncclDataType_t t, int peer, ncclComm_t c,
+                          cudaStream_t st), (s, n, t, peer, c, st))
+NB_PASSTHROUGH(ncclRecv, (void* r, size_t n, ncclDataType_t t, int peer, ncclComm_t c, cudaStream_t st),
+               (r, n, t, peer, c, st))
+NB_PASSTHROUGH(ncclAlltoAll, (const void* s, void* r, size_t n, ncclDataType_t t, ncclComm_t c,
+                              cudaStream_t st), (s, r, n, t, c, st))
+NB_PASSTHROUGH(ncclGather, (const void* s, void* r, size_t n, ncclDataType_t t, int root, ncclComm_t c,
+                            cudaStream_t st), (s, r, n, t, root, c, st))
+NB_PASSTHROUGH(ncclScatter, (const void* s, void* r, size_t n, ncclDataType_t t, int root, ncclComm_t c,
+                             cudaStream_t st), (s, r, n, t, root, c, st))
+NB_PASSTHROUGH(ncclCommInitRankScalable, (ncclComm_t* out, int nranks, int rank, int nid,
+                                          ncclUniqueId* ids, ncclConfig_t* cfg),
+               (out, nranks, rank, nid, ids, cfg))
+
+NB_LIFECYCLE(ncclCommFinalize, (ncclComm_t comm), comm, (comm))
+NB_LIFECYCLE(ncclCommAbort, (ncclComm_t comm), comm, (comm))
+NB_LIFECYCLE(ncclCommSplit, (ncclComm_t comm, int color, int key, ncclComm_t* out, ncclConfig_t* cfg),
+             comm, (comm, color, key, out, cfg))
+NB_LIFECYCLE(ncclCommShrink, (ncclComm_t comm, int* excluded, int count, ncclComm_t* out,
+                              ncclConfig_t* cfg, int flags), comm, (comm, excluded, count, out, cfg, flags))
+NB_LIFECYCLE(ncclCommRegister, (const ncclComm_t comm, void* buff, size_t size, void** handle), comm,
+             (comm, buff, size, handle))
+NB_LIFECYCLE(ncclCommDeregister, (const ncclComm_t comm, void* handle), comm, (comm, handle))
+NB_LIFECYCLE(ncclCommWindowRegister, (ncclComm_t comm, void* buff, size_t size, ncclWindow_t* win,
+                                      int flags), comm, (comm, buff, size, win, flags))
+NB_LIFECYCLE(ncclCommWindowDeregister, (ncclComm_t comm, ncclWindow_t win), comm, (comm, win))
+
+// PreMulSum: forwarded so NCCL can still run the op on fallback, and
+// recorded so the kernels can apply the same per-rank scalar.
+ncclResult_t ncclRedOpCreatePreMulSum(ncclRedOp_t* op, void* scalar, ncclDataType_t datatype,
+                                      ncclScalarResidence_t residence, ncclComm_t comm) {
+  using Fn = decltype(&::ncclRedOpCreatePreMulSum);
+  static const Fn real = real_fn<Fn>("ncclRedOpCreatePreMulSum");
+  const int prefix = force_passthrough();
+  if (prefix != ncclSuccess) return ncclResult_t(prefix);
+  if (!real) return ncclInvalidUsage;
+  const ncclResult_t res = real(op, scalar, datatype, residence, comm);
+  if (res == ncclSuccess && op && scalar) {
+    PreMulScalar s;
+    s.dtype = dtype_from_nccl(int(datatype));
+    s.residence = residence == ncclScalarHostImmediate ? 1 : 0;
+    if (s.residence) {
+      switch (s.dtype) {
+        case DType::F32: s.value = *static_cast<const float*>(scalar); break;
+        case DType::F64: s.value = *static_cast<const double*>(scalar); break;
+        case DType::F16: s.value = half_to_float(*static_cast<const uint16_t*>(scalar)); break;
+        case DType::BF16: s.value = bf16_to_float(*static_cast<const uint16_t*>(scalar)); break;
+        default: s.dtype = DType::Unsupported; break;
+      }
+    } else {
+      s.device_ptr = reinterpret_cast<uintptr_t>(scalar);
+    }
+    if (s.dtype != DType::Unsupported) rt().cliques.add_premul(comm, int(*op), s);
+  }
+  return res;
+}
+
+ncclResult_t ncclRedOpDestroy(ncclRedOp_t op, ncclComm_t comm) {
+  using Fn = decltype(&::ncclRedOpDestroy);
+  static const Fn real = real_fn<Fn>("ncclRedOpDestroy");
+  const int prefix = force_passthrough();
+  rt().cliques.drop_premul(comm, int(op));
+  if (prefix != ncclSuccess) return ncclResult_t(prefix);
+  return real ? real(op, comm) : ncclInvalidUsage;
+}
+
+// ---- Introspection for tests and the benchmark (not NCCL ABI) -------------
+
+int nb_custom_calls(int algo) {
+  return algo >= 0 && algo < int(Algo::Count) ? int(rt().summary.custom_calls(Algo(algo))) : -1;
+}
+int nb_fallbacks(int reason) {
+  return reason >= 0 && reason < int(Reason::Count) ? int(rt().summary.fallbacks(Reason(reason))) : -1;
+}
+int nb_poisoned() { return rt().poisoned ? 1 : 0; }
+uint64_t nb_kernel_launches() { return rt().exec.kernel_launches(); }
+const char* nb_build_id() { return build_id(); }
+int nb_nccl_version() {
+  resolve_all();
+  return rt().nccl_version;
+}
+// Copies the summary lines, newline-separated, into buf; returns the length.
+size_t nb_summary_text(char* buf, size_t cap) {
+  std::string all;
+  for (const std::string& s : rt().summary.render(build_id())) all += s + "\n";
+  if (buf && cap) {
+    const size_t n = all.size() < cap - 1 ? all.size() : cap - 1;
+    std::memcpy(buf, all.data(), n);
+    buf[n] = 0;
+  }
+  return all.size();
+}
+void nb_shares(int* host_ppm, int* ce_ppm) {
+  *host_ppm = rt().calibrated.host_ppm;
+  *ce_ppm = rt().calibrated.ce_ppm;
+}
+
+}  // extern "C"

@@ -1,0 +1,89 @@
+#include "core/calib_model.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+namespace nb {
+
+Shares shares_from(const CalibResult& c, Algo a, int n) {
+  Shares s;
+  if (!c.valid || n < 2 || c.nvlink_sm_gbs <= 0) return s;
+  const double N = double(n);
+  const double bnv = c.nvlink_sm_gbs;
+  const double bp = std::min(c.pcie_d2h_gbs, c.pcie_h2d_gbs);
+  const double bf = c.fold_gbs;
+  // NVLink seconds per byte of this GPU's share, and host seconds per byte.
+  double nv = 0, host = 0;
+  switch (a) {
+    case Algo::ArTwoShot:
+      nv = 2.0 * (N - 1.0) / N / bnv;
+      host = std::max(bp > 0 ? 1.0 / bp : 1e30, bf > 0 ? N / bf : 1e30);
+      break;
+    case Algo::RsPull:
+      nv = (N - 1.0) / bnv;
+      host = std::max(bp > 0 ? N / bp : 1e30, bf > 0 ? N * N / bf : 1e30);
+      break;
+    case Algo::AgPull:
+      nv = (N - 1.0) / bnv;
+      host = bp > 0 ? (N - 1.0) / bp : 1e30;
+      break;
+    case Algo::BcPull: case Algo::BcScatter:
+      nv = 1.0 / bnv;
+      host = bp > 0 ? 1.0 / bp : 1e30;
+      break;
+    default:
+      return s;
+  }
+  double h = nv / (nv + host);
+  if (h < 0.03) h = 0;  // the predicted gain is about h: not worth the lanes
+  h = std::min(h, 0.25);
+  s.host_ppm = int(h * 10000.0);
+  const bool ce_algo = a == Algo::ArTwoShot || a == Algo::AgPull || a == Algo::BcPull;
+  if (ce_algo && c.nvlink_mix_gbs > 1.03 * bnv && c.mix_ce_fraction > 0)
+    s.ce_ppm = int(std::min(0.5, c.mix_ce_fraction) * 10000.0);
+  return s;
+}
+
+std::string calib_to_json(const CalibResult& c, const std::string& key) {
+  char buf[1024];
+  std::snprintf(buf, sizeof buf,
+                "{\"key\": \"%s\", \"nvlink_sm_gbs\": %.3f, \"nvlink_ce_gbs\": %.3f, "
+                "\"nvlink_mix_gbs\": %.3f, \"mix_ce_fraction\": %.5f, \"pcie_d2h_gbs\": %.3f, "
+                "\"pcie_h2d_gbs\": %.3f, \"fold_gbs\": %.3f}\n",
+                key.c_str(), c.nvlink_sm_gbs, c.nvlink_ce_gbs, c.nvlink_mix_gbs, c.mix_ce_fraction,
+                c.pcie_d2h_gbs, c.pcie_h2d_gbs, c.fold_gbs);
+  return buf;
+}
+
+static bool json_number(const std::string& text, const char* name, double* out) {
+  const std::string pat = std::string("\"") + name + "\":";
+  const size_t p = text.find(pat);
+  if (p == std::string::npos) return false;
+  const char* s = text.c_str() + p + pat.size();
+  char* end = nullptr;
+  const double v = std::strtod(s, &end);
+  if (end == s) return false;
+  *out = v;
+  return true;
+}
+
+bool calib_from_json(const std::string& text, const std::string& key, CalibResult* out) {
+  const std::string pat = "\"key\": \"" + key + "\"";
+  if (text.find(pat) == std::string::npos) return false;
+  CalibResult c;
+  bool ok = json_number(text, "nvlink_sm_gbs", &c.nvlink_sm_gbs) &&
+            json_number(text, "nvlink_ce_gbs", &c.nvlink_ce_gbs) &&
+            json_number(text, "nvlink_mix_gbs", &c.nvlink_mix_gbs) &&
+            json_number(text, "mix_ce_fraction", &c.mix_ce_fraction) &&
+            json_number(text, "pcie_d2h_gbs", &c.pcie_d2h_gbs) &&
+            json_number(text, "pcie_h2d_gbs", &c.pcie_h2d_gbs) &&
+            json_number(text, "fold_gbs", &c.fold_gbs);
+  if (!ok) return false;
+  c.valid = true;
+  *out = c;
+  return true;
+}
+
+}  // namespace nb

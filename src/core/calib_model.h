@@ -1,0 +1,37 @@
+// Pure part of path calibration: the measured rates, the share model that
+// turns them into per-algorithm byte splits, and the JSON cache format.
+//
+// Share model. For each algorithm, per GPU, the SM/NVLink part carries
+// c_nv bytes of NVLink traffic per byte of its share at B_nv, the host part
+// carries c_h bytes of PCIe traffic per byte at B_pcie (plus, for reductions,
+// N bytes of host-fold input per byte at B_fold, over all GPUs at once); the
+// host share h balances the two times, and is dropped when the predicted gain
+// is under 3 %. The copy-engine share is the CE part of the measured mixed
+// SM+CE rate, used only when the mix beats SM pulls alone by 3 % or more.
+//
+// Parity: replaces the reference's constant divisors 7/7/7/7/6 and piece
+// sizes (shim/nccl_collectives_shim.cu:51-91).
+#pragma once
+
+#include <string>
+
+#include "core/plan.h"
+
+namespace nb {
+
+struct CalibResult {
+  bool valid = false;
+  double nvlink_sm_gbs = 0;   // per-GPU inbound, SM pulls, all GPUs pulling
+  double nvlink_ce_gbs = 0;   // per-GPU inbound, copy engine alone
+  double nvlink_mix_gbs = 0;  // per-GPU inbound, SM + CE together
+  double mix_ce_fraction = 0; // CE's part of the mixed rate
+  double pcie_d2h_gbs = 0;    // per GPU, every GPU at once, D2H and H2D together
+  double pcie_h2d_gbs = 0;
+  double fold_gbs = 0;        // host fold input throughput (all threads)
+};
+
+Shares shares_from(const CalibResult& c, Algo a, int n);
+std::string calib_to_json(const CalibResult& c, const std::string& key);
+bool calib_from_json(const std::string& text, const std::string& key, CalibResult* out);
+
+}  // namespace nb

@@ -1,0 +1,547 @@
+#include "core/plan.h"
+
+#include <algorithm>
+
+namespace nb {
+
+bool operator==(StreamId a, StreamId b) {
+  return a.kind == b.kind && a.dev == b.dev && a.lane == b.lane;
+}
+bool operator==(EventId a, EventId b) {
+  return a.kind == b.kind && a.dev == b.dev && a.lane == b.lane && a.index == b.index;
+}
+
+void Needs::merge(const Needs& o) {
+  lanes = std::max(lanes, o.lanes);
+  bounce_bytes = std::max(bounce_bytes, o.bounce_bytes);
+  phase_events = std::max(phase_events, o.phase_events);
+  nvls_bytes = std::max(nvls_bytes, o.nvls_bytes);
+}
+
+void slice_of(size_t bytes, int parts, int i, size_t* off, size_t* len) {
+  const size_t base = (bytes / size_t(parts)) & ~size_t(15);
+  *off = base * size_t(i);
+  *len = i == parts - 1 ? bytes - *off : base;
+}
+
+size_t host_share(size_t len, int ppm, const Policy& p) {
+  if (ppm <= 0 || len == 0) return 0;
+  const size_t h = (size_t((unsigned __int128)len * unsigned(ppm) / 10000) / 16) * 16;
+  return h >= p.min_host_bytes ? h : 0;
+}
+
+size_t ce_share(size_t len, int ppm) {
+  if (ppm <= 0 || len == 0) return 0;
+  return (size_t((unsigned __int128)len * unsigned(ppm) / 10000) / 16) * 16;
+}
+
+namespace {
+
+StreamId caller(int r) { return {Strm::Caller, uint8_t(r), 0}; }
+StreamId d2h(int r, int lane) { return {Strm::D2H, uint8_t(r), uint8_t(lane)}; }
+StreamId h2d(int r, int lane) { return {Strm::H2D, uint8_t(r), uint8_t(lane)}; }
+StreamId host(int lane) { return {Strm::Host, 0, uint8_t(lane)}; }
+EventId input_ready(int r) { return {Ev::InputReady, uint8_t(r), 0, 0}; }
+EventId join_done(int r) { return {Ev::Join, uint8_t(r), 0, 0}; }
+EventId done(StreamId s) { return {Ev::Done, s.dev, s.lane, uint16_t(s.kind)}; }
+EventId d2h_done(int r, int lane) { return {Ev::D2HDone, uint8_t(r), uint8_t(lane), 0}; }
+EventId h2d_done(int r, int lane) { return {Ev::H2DDone, uint8_t(r), uint8_t(lane), 0}; }
+EventId host_done(int lane) { return {Ev::HostDone, 0, uint8_t(lane), 0}; }
+EventId lane_free(int lane) { return {Ev::LaneFree, 0, uint8_t(lane), 0}; }
+
+// Appends ops and tracks, per stream, which ranks' InputReady it has already
+// waited for, and which internal streams each rank used (for the join).
+class Builder {
+ public:
+  Builder(Plan& plan, Algo algo, const CliqueDesc& d, const Policy& p) : p_(plan), pol_(p) {
+    p_.algo = algo;
+    p_.desc = d;
+    p_.ops.clear();
+    p_.needs = Needs{};
+    p_.sm_bytes = p_.ce_bytes = p_.host_bytes = 0;
+    n_ = d.nranks;
+  }
+  int n() const { return n_; }
+  const Policy& policy() const { return pol_; }
+  Plan& plan() { return p_; }
+
+  void record(EventId e, StreamId s) {
+    if (e.kind == Ev::Phase) p_.needs.phase_events = std::max<uint16_t>(p_.needs.phase_events, uint16_t(e.index + 1));
+    PlanOp op;
+    op.kind = OpKind::Record;
+    op.stream = s;
+    op.event = e;
+    p_.ops.push_back(op);
+  }
+  void wait(StreamId s, EventId e) {
+    PlanOp op;
+    op.kind = OpKind::Wait;
+    op.stream = s;
+    op.event = e;
+    p_.ops.push_back(op);
+  }
+  // `s` is about to touch rank r's buffers: make it wait r's InputReady once.
+  void touch(StreamId s, int r) {
+    if (s.kind == Strm::Caller && s.dev == r) return;  // stream order
+    for (const auto& t : touched_)
+      if (t.first == s && t.second == r) return;
+    touched_.push_back({s, r});
+    wait(s, input_ready(r));
+    use(s);
+  }
+  void use(StreamId s) {
+    if (s.kind == Strm::Caller || s.kind == Strm::Host) return;
+    for (const auto& u : used_)
+      if (u == s) return;
+    used_.push_back(s);
+  }
+  void ce_copy(StreamId s, Loc dst, Loc src, size_t bytes) {
+    if (!bytes) return;
+    PlanOp op;
+    op.kind = OpKind::CeCopy;
+    op.stream = s;
+    op.nsrc = op.ndst = 1;
+    op.src[0] = src;
+    op.dst[0] = dst;
+    op.len[0] = op.bytes = bytes;
+    p_.ops.push_back(op);
+    use(s);
+  }
+  void sm_copy(StreamId s, const Loc* dst, const Loc* src, const size_t* len, int nseg) {
+    PlanOp op;
+    op.kind = OpKind::SmCopy;
+    op.stream = s;
+    for (int i = 0; i < nseg; ++i) {
+      if (!len[i]) continue;
+      op.src[op.nsrc] = src[i];
+      op.dst[op.ndst] = dst[i];
+      op.len[op.nsrc] = len[i];
+      op.bytes += len[i];
+      ++op.nsrc;
+      ++op.ndst;
+    }
+    if (!op.nsrc) return;
+    p_.ops.push_back(op);
+    use(s);
+  }
+  void sm_reduce(StreamId s, const Loc* src, int nsrc, const Loc* dst, int ndst, size_t bytes) {
+    if (!bytes) return;
+    PlanOp op;
+    op.kind = OpKind::SmReduce;
+    op.stream = s;
+    op.nsrc = uint8_t(nsrc);
+    op.ndst = uint8_t(ndst);
+    for (int i = 0; i < nsrc; ++i) op.src[i] = src[i];
+    for (int i = 0; i < ndst; ++i) op.dst[i] = dst[i];
+    op.len[0] = op.bytes = bytes;
+    p_.ops.push_back(op);
+    use(s);
+  }
+  void host_reduce(StreamId s, const Loc* src, int nsrc, Loc dst, size_t bytes) {
+    PlanOp op;
+    op.kind = OpKind::HostReduce;
+    op.stream = s;
+    op.nsrc = uint8_t(nsrc);
+    op.ndst = 1;
+    for (int i = 0; i < nsrc; ++i) op.src[i] = src[i];
+    op.dst[0] = dst;
+    op.len[0] = op.bytes = bytes;
+    p_.ops.push_back(op);
+  }
+  void nvls(StreamId s, int r, size_t bytes) {
+    PlanOp op;
+    op.kind = OpKind::NvlsReduce;
+    op.stream = s;
+    op.nsrc = op.ndst = 1;
+    op.src[0] = send_at(r, 0);
+    op.dst[0] = recv_at(r, 0);
+    op.len[0] = op.bytes = bytes;
+    p_.ops.push_back(op);
+    use(s);
+  }
+
+  void prologue() {
+    for (int r = 0; r < n_; ++r) record(input_ready(r), caller(r));
+  }
+  // Every rank's caller stream waits for its own internal streams, then for
+  // every peer's join, so no rank returns while a peer still reads its send
+  // buffer or writes its receive buffer.
+  void join() {
+    for (int r = 0; r < n_; ++r) {
+      for (const StreamId& s : used_) {
+        if (s.dev != r) continue;
+        record(done(s), s);
+        wait(caller(r), done(s));
+      }
+      record(join_done(r), caller(r));
+    }
+    for (int r = 0; r < n_; ++r)
+      for (int q = 0; q < n_; ++q)
+        if (q != r) wait(caller(r), join_done(q));
+  }
+
+  // Stage `bytes` through the pinned-host lanes in pieces, round-robin over
+  // lanes. For each piece: every source rank's D2H lands in its bounce
+  // buffer; with `reduce` the host folds them (rank order) into HostOut;
+  // every destination rank's H2D then copies the result (or, without
+  // `reduce`, the single source's bounce) into its buffer. A lane is reused
+  // only after all H2Ds of its previous piece completed (LaneFree), which is
+  // the HostLaneReuse invariant.
+  // srcs[i] / dsts[j] locate offset 0 of this staged range.
+  void host_stage(const int* src_ranks, const Loc* srcs, int nsrc, const int* dst_ranks,
+                  const Loc* dsts, int ndst, size_t bytes, bool reduce) {
+    const size_t piece = pol_.host_piece;
+    const int lanes = pol_.lanes;
+    for (size_t rel = 0; rel < bytes; rel += piece) {
+      const size_t cb = std::min(piece, bytes - rel);
+      const int lane = int(pieces_++ % size_t(lanes));
+      p_.needs.lanes = std::max(p_.needs.lanes, lane + 1);
+      p_.needs.bounce_bytes = std::max(p_.needs.bounce_bytes, cb);
+      Loc bounce[kMaxRanks];
+      for (int i = 0; i < nsrc; ++i) {
+        const int q = src_ranks[i];
+        const StreamId s = d2h(q, lane);
+        touch(s, q);
+        wait(s, lane_free(lane));
+        bounce[i] = bounce_at(q, lane);
+        ce_copy(s, bounce[i], at(srcs[i], rel), cb);
+        record(d2h_done(q, lane), s);
+      }
+      Loc out = bounce[0];
+      if (reduce) {
+        for (int i = 0; i < nsrc; ++i) wait(host(lane), d2h_done(src_ranks[i], lane));
+        out = hostout_at(lane);
+        host_reduce(host(lane), bounce, nsrc, out, cb);
+        record(host_done(lane), host(lane));
+      }
+      for (int j = 0; j < ndst; ++j) {
+        const int r = dst_ranks[j];
+        const StreamId s = h2d(r, lane);
+        touch(s, r);
+        wait(s, reduce ? host_done(lane) : d2h_done(src_ranks[0], lane));
+        ce_copy(s, at(dsts[j], rel), out, cb);
+        record(h2d_done(r, lane), s);
+      }
+      for (int j = 0; j < ndst; ++j) wait(host(lane), h2d_done(dst_ranks[j], lane));
+      if (!reduce)
+        for (int i = 0; i < nsrc; ++i) wait(host(lane), d2h_done(src_ranks[i], lane));
+      record(lane_free(lane), host(lane));
+      p_.host_bytes += cb * size_t(nsrc + ndst);
+    }
+  }
+
+ private:
+  Plan& p_;
+  const Policy& pol_;
+  int n_ = 0;
+  size_t pieces_ = 0;
+  std::vector<std::pair<StreamId, int>> touched_;
+  std::vector<StreamId> used_;
+};
+
+void all_ranks(int n, int* ranks) {
+  for (int i = 0; i < n; ++i) ranks[i] = i;
+}
+
+// AllReduce two-shot: rank r owns slice r. Its kernel reads slice r of every
+// rank's input (fixed rank order), reduces in fp32 (fp64 for doubles) and
+// stores the result into slice r of every rank's output: the reduce-scatter
+// and all-gather halves of the ring, fused into one pass with no scratch.
+// Optional copy-engine share: a middle part of each slice is reduced into the
+// owner's output only, then pushed to the peers by the owner's copy engine.
+// Optional host share: the slice's suffix goes through the host lanes.
+void plan_ar_twoshot(Builder& b, const CliqueDesc& d, const Shares& s) {
+  const int n = b.n();
+  b.prologue();
+  int ranks[kMaxRanks];
+  all_ranks(n, ranks);
+  size_t off[kMaxRanks], len[kMaxRanks], host[kMaxRanks], ce[kMaxRanks];
+  for (int r = 0; r < n; ++r) {
+    slice_of(d.bytes, n, r, &off[r], &len[r]);
+    host[r] = n > 1 ? host_share(len[r], s.host_ppm, b.policy()) : 0;
+    ce[r] = n > 1 ? ce_share(len[r] - host[r], s.ce_ppm) : 0;
+  }
+  for (int r = 0; r < n; ++r) {
+    const size_t sm = len[r] - host[r] - ce[r];
+    Loc src[kMaxRanks], dst[kMaxRanks];
+    for (int q = 0; q < n; ++q) {
+      b.touch({Strm::Caller, uint8_t(r), 0}, q);
+      src[q] = send_at(q, off[r]);
+      dst[q] = recv_at(q, off[r]);
+    }
+    b.sm_reduce({Strm::Caller, uint8_t(r), 0}, src, n, dst, n, sm);
+    b.plan().sm_bytes += sm * size_t(2 * (n - 1));
+    if (ce[r]) {
+      // Reduce the copy-engine part into this rank's output only, in
+      // pieces, and push each piece to every peer from this GPU.
+      const size_t piece = b.policy().sm_chunk;
+      int k = 0;
+      for (size_t rel = 0; rel < ce[r]; rel += piece, ++k) {
+        const size_t cb = std::min(piece, ce[r] - rel);
+        Loc src2[kMaxRanks];
+        for (int q = 0; q < n; ++q) src2[q] = send_at(q, off[r] + sm + rel);
+        Loc own = recv_at(r, off[r] + sm + rel);
+        b.sm_reduce({Strm::Caller, uint8_t(r), 0}, src2, n, &own, 1, cb);
+        b.record({Ev::Phase, uint8_t(r), 0, uint16_t(k)}, {Strm::Caller, uint8_t(r), 0});
+        const StreamId cs{Strm::Copy, uint8_t(r), 0};
+        b.wait(cs, {Ev::Phase, uint8_t(r), 0, uint16_t(k)});
+        for (int q = 0; q < n; ++q) {
+          if (q == r) continue;
+          b.touch(cs, q);
+          b.ce_copy(cs, recv_at(q, off[r] + sm + rel), own, cb);
+        }
+      }
+      b.plan().sm_bytes += ce[r] * size_t(n - 1);
+      b.plan().ce_bytes += ce[r] * size_t(n - 1);
+    }
+  }
+  for (int r = 0; r < n; ++r) {
+    if (!host[r]) continue;
+    const size_t base = off[r] + len[r] - host[r];
+    Loc src[kMaxRanks], dst[kMaxRanks];
+    for (int q = 0; q < n; ++q) {
+      src[q] = send_at(q, base);
+      dst[q] = recv_at(q, base);
+    }
+    b.host_stage(ranks, src, n, ranks, dst, n, host[r], true);
+  }
+  b.join();
+}
+
+// ReduceScatter: rank r reduces slot r of every rank's input into its output.
+void plan_rs_pull(Builder& b, const CliqueDesc& d, const Shares& s) {
+  const int n = b.n();
+  b.prologue();
+  int ranks[kMaxRanks];
+  all_ranks(n, ranks);
+  const size_t slot = d.bytes;
+  const size_t host = n > 1 ? host_share(slot, s.host_ppm, b.policy()) : 0;
+  const size_t sm = slot - host;
+  for (int r = 0; r < n; ++r) {
+    Loc src[kMaxRanks];
+    for (int q = 0; q < n; ++q) {
+      b.touch({Strm::Caller, uint8_t(r), 0}, q);
+      src[q] = send_at(q, size_t(r) * slot);
+    }
+    Loc dst = recv_at(r, 0);
+    b.sm_reduce({Strm::Caller, uint8_t(r), 0}, src, n, &dst, 1, sm);
+    b.plan().sm_bytes += sm * size_t(n - 1);
+  }
+  if (host)
+    for (int r = 0; r < n; ++r) {
+      Loc src[kMaxRanks];
+      for (int q = 0; q < n; ++q) src[q] = send_at(q, size_t(r) * slot + sm);
+      Loc dst = recv_at(r, sm);
+      b.host_stage(ranks, src, n, &ranks[r], &dst, 1, host, true);
+    }
+  b.join();
+}
+
+// AllGather: rank r pulls every rank's slot into slot q of its output (its
+// own slot too, unless in place). Optional copy-engine and host shares take
+// the middle and the suffix of each peer slot.
+void plan_ag_pull(Builder& b, const CliqueDesc& d, const Shares& s) {
+  const int n = b.n();
+  b.prologue();
+  const size_t slot = d.bytes;
+  const size_t host = n > 1 ? host_share(slot, s.host_ppm, b.policy()) : 0;
+  const size_t ce = n > 1 ? ce_share(slot - host, s.ce_ppm) : 0;
+  const size_t sm = slot - host - ce;
+  for (int r = 0; r < n; ++r) {
+    Loc dst[kMaxRanks], src[kMaxRanks];
+    size_t len[kMaxRanks];
+    int k = 0;
+    for (int q = 0; q < n; ++q) {
+      if (q == r && d.in_place[r]) continue;
+      b.touch({Strm::Caller, uint8_t(r), 0}, q);
+      dst[k] = recv_at(r, size_t(q) * slot);
+      src[k] = send_at(q, 0);
+      // The own slot is a local copy: all of it goes through the SM kernel.
+      len[k] = q == r ? slot : sm;
+      ++k;
+    }
+    b.sm_copy({Strm::Caller, uint8_t(r), 0}, dst, src, len, k);
+    b.plan().sm_bytes += sm * size_t(n - 1);
+    if (ce) {
+      const StreamId cs{Strm::Copy, uint8_t(r), 0};
+      for (int q = 0; q < n; ++q) {
+        if (q == r) continue;
+        b.touch(cs, r);
+        b.touch(cs, q);
+        b.ce_copy(cs, recv_at(r, size_t(q) * slot + sm), send_at(q, sm), ce);
+      }
+      b.plan().ce_bytes += ce * size_t(n - 1);
+    }
+  }
+  if (host)
+    for (int q = 0; q < n; ++q) {
+      int dst_ranks[kMaxRanks];
+      Loc dsts[kMaxRanks];
+      int k = 0;
+      for (int r = 0; r < n; ++r) {
+        if (r == q) continue;
+        dst_ranks[k] = r;
+        dsts[k++] = recv_at(r, size_t(q) * slot + sm + ce);
+      }
+      Loc src = send_at(q, sm + ce);
+      b.host_stage(&q, &src, 1, dst_ranks, dsts, k, host, false);
+    }
+  b.join();
+}
+
+// Broadcast by pulls: every non-root pulls the root's buffer; the root copies
+// its own buffer locally when out of place.
+void plan_bc_pull(Builder& b, const CliqueDesc& d, const Shares& s) {
+  const int n = b.n();
+  const int root = d.root;
+  b.prologue();
+  const size_t bytes = d.bytes;
+  const size_t host = n > 1 ? host_share(bytes, s.host_ppm, b.policy()) : 0;
+  const size_t ce = n > 1 ? ce_share(bytes - host, s.ce_ppm) : 0;
+  const size_t sm = bytes - host - ce;
+  if (!d.in_place[root]) {
+    Loc dst = recv_at(root, 0), src = send_at(root, 0);
+    b.sm_copy({Strm::Caller, uint8_t(root), 0}, &dst, &src, &bytes, 1);
+  }
+  for (int r = 0; r < n; ++r) {
+    if (r == root) continue;
+    b.touch({Strm::Caller, uint8_t(r), 0}, root);
+    Loc dst = recv_at(r, 0), src = send_at(root, 0);
+    b.sm_copy({Strm::Caller, uint8_t(r), 0}, &dst, &src, &sm, 1);
+    b.plan().sm_bytes += sm;
+    if (ce) {
+      const StreamId cs{Strm::Copy, uint8_t(r), 0};
+      b.touch(cs, r);
+      b.touch(cs, root);
+      b.ce_copy(cs, recv_at(r, sm), send_at(root, sm), ce);
+      b.plan().ce_bytes += ce;
+    }
+  }
+  if (host) {
+    int dst_ranks[kMaxRanks];
+    Loc dsts[kMaxRanks];
+    int k = 0;
+    for (int r = 0; r < n; ++r) {
+      if (r == root) continue;
+      dst_ranks[k] = r;
+      dsts[k++] = recv_at(r, sm + ce);
+    }
+    Loc src = send_at(root, sm + ce);
+    b.host_stage(&root, &src, 1, dst_ranks, dsts, k, host, false);
+  }
+  b.join();
+}
+
+// Broadcast by scatter + all-gather over the N-1 non-roots, in pipelined
+// pieces. Phase 1 (caller stream): non-root j pulls its slice of the piece
+// from the root. Phase 2 (aux stream): after every other non-root's phase 1
+// of that piece, non-root j pulls the other slices from their owners. The
+// root sends each byte once and every non-root receives each byte once.
+void plan_bc_scatter(Builder& b, const CliqueDesc& d, const Shares& s) {
+  const int n = b.n();
+  const int root = d.root;
+  b.prologue();
+  const size_t bytes = d.bytes;
+  const size_t host = host_share(bytes, s.host_ppm, b.policy());
+  const size_t body = bytes - host;
+  int nonroot[kMaxRanks];
+  int m = 0;
+  for (int r = 0; r < n; ++r)
+    if (r != root) nonroot[m++] = r;
+  const size_t min_piece = 16 * kMiB;
+  int pieces = std::max(1, b.policy().bc_pieces);
+  while (pieces > 1 && body / size_t(pieces) < min_piece) --pieces;
+  if (!d.in_place[root]) {
+    const StreamId as{Strm::Aux, uint8_t(root), 0};
+    b.touch(as, root);
+    Loc dst = recv_at(root, 0), src = send_at(root, 0);
+    b.sm_copy(as, &dst, &src, &bytes, 1);
+  }
+  for (int k = 0; k < pieces; ++k) {
+    size_t poff, plen;
+    slice_of(body, pieces, k, &poff, &plen);
+    for (int j = 0; j < m; ++j) {
+      size_t soff, slen;
+      slice_of(plen, m, j, &soff, &slen);
+      const int r = nonroot[j];
+      b.touch({Strm::Caller, uint8_t(r), 0}, root);
+      Loc dst = recv_at(r, poff + soff), src = send_at(root, poff + soff);
+      b.sm_copy({Strm::Caller, uint8_t(r), 0}, &dst, &src, &slen, 1);
+      b.record({Ev::Phase, uint8_t(r), 0, uint16_t(k)}, {Strm::Caller, uint8_t(r), 0});
+      b.plan().sm_bytes += slen;
+    }
+    for (int j = 0; j < m; ++j) {
+      const int r = nonroot[j];
+      const StreamId as{Strm::Aux, uint8_t(r), 0};
+      b.touch(as, r);
+      Loc dst[kMaxRanks], src[kMaxRanks];
+      size_t len[kMaxRanks];
+      int c = 0;
+      for (int i = 0; i < m; ++i) {
+        if (i == j) continue;
+        const int q = nonroot[i];
+        b.wait(as, {Ev::Phase, uint8_t(q), 0, uint16_t(k)});
+        size_t soff, slen;
+        slice_of(plen, m, i, &soff, &slen);
+        dst[c] = recv_at(r, poff + soff);
+        src[c] = recv_at(q, poff + soff);
+        len[c++] = slen;
+        b.plan().sm_bytes += slen;
+      }
+      b.sm_copy(as, dst, src, len, c);
+    }
+  }
+  if (host) {
+    Loc dsts[kMaxRanks];
+    for (int j = 0; j < m; ++j) dsts[j] = recv_at(nonroot[j], body);
+    Loc src = send_at(root, body);
+    b.host_stage(&root, &src, 1, nonroot, dsts, m, host, false);
+  }
+  b.join();
+}
+
+// NVLS AllReduce: one gang op per rank on its aux stream, after every rank's
+// input is ready. Inside, rank r copies its input into its multicast-bound
+// scratch, then reduces slice r through the switch (multimem.ld_reduce) and
+// multicasts the result (multimem.st), then copies its output out, with
+// bounded in-kernel barriers between the phases.
+void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p) {
+  const int n = b.n();
+  b.prologue();
+  for (int r = 0; r < n; ++r) {
+    const StreamId as{Strm::Aux, uint8_t(r), 0};
+    for (int q = 0; q < n; ++q) b.touch(as, q);
+    b.nvls(as, r, d.bytes);
+  }
+  b.plan().needs.nvls_bytes = p.nvls_round_bytes;
+  b.plan().sm_bytes += d.bytes * size_t(n);  // ~S in and S out per GPU via the switch
+  b.join();
+}
+
+}  // namespace
+
+void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s, Plan& out) {
+  Builder b(out, algo, d, p);
+  switch (algo) {
+    case Algo::ArTwoShot: plan_ar_twoshot(b, d, s); break;
+    case Algo::ArNvls: plan_ar_nvls(b, d, p); break;
+    case Algo::RsPull: plan_rs_pull(b, d, s); break;
+    case Algo::AgPull: plan_ag_pull(b, d, s); break;
+    case Algo::BcPull: plan_bc_pull(b, d, s); break;
+    case Algo::BcScatter: plan_bc_scatter(b, d, s); break;
+    default: break;
+  }
+}
+
+Needs prewarm_needs(int nranks, const Policy& p, const Shares& s, bool nvls) {
+  Needs needs;
+  if (s.host_ppm > 0) {
+    needs.lanes = p.lanes;
+    needs.bounce_bytes = p.host_piece;
+  }
+  needs.phase_events = uint16_t(std::max(64, p.bc_pieces));
+  if (nvls && nranks >= 2) needs.nvls_bytes = p.nvls_round_bytes;
+  return needs;
+}
+
+}  // namespace nb

@@ -1,0 +1,125 @@
+// Pure schedule IR and the per-algorithm planners.
+//
+// A Plan is an ordered list of ops on logical streams (per rank: the
+// caller's stream, an auxiliary SM stream, a copy-engine stream, per-lane
+// D2H/H2D streams; per lane: a host-reduction stream), ordered across streams
+// by logical events. The executor binds streams, events and buffers and
+// submits the ops in order; the CPU simulator (plan_sim.h) runs the same
+// plans on host memory and checks every conflicting access pair for a
+// happens-before edge.
+//
+// Parity: the reference's Layer-3 IR (shim/nccl_collectives_shim.cu:292-418:
+// Record/Wait/Copy/Reduce on Caller/Copy/HostReduce/Side/D2H/H2D streams) and
+// its route builders (:420-714). Differences: N ranks instead of a device
+// pair; a data op is a fused multi-source reduce or multi-segment copy that
+// one sm_100a kernel performs while moving the bytes over NVLink (no Temp
+// scratch round-trip); the host lane reduces on the CPU.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <vector>
+
+#include "core/gate.h"
+#include "core/policy.h"
+#include "core/types.h"
+
+namespace nb {
+
+// Logical streams. `dev` is a rank index of the clique. D2H and H2D lanes
+// live on rank `dev`'s GPU; Host(lane) lives on rank 0's GPU and only waits,
+// records and runs the CPU reduction.
+enum class Strm : uint8_t { Caller, Aux, Copy, D2H, H2D, Host, Count };
+struct StreamId {
+  Strm kind = Strm::Caller;
+  uint8_t dev = 0;
+  uint8_t lane = 0;
+};
+bool operator==(StreamId a, StreamId b);
+inline bool operator!=(StreamId a, StreamId b) { return !(a == b); }
+
+// Logical events, each recorded on one stream. Done(stream) marks the end of
+// an internal stream's work in this plan (index = stream kind).
+enum class Ev : uint8_t { InputReady, Join, Phase, Done, D2HDone, H2DDone, HostDone, LaneFree, Count };
+struct EventId {
+  Ev kind = Ev::InputReady;
+  uint8_t dev = 0;
+  uint8_t lane = 0;
+  uint16_t index = 0;
+};
+bool operator==(EventId a, EventId b);
+
+// Buffers. Send/Recv are the caller's (per rank); Bounce(dev, lane) is the
+// pinned-host staging buffer a rank's D2H fills; HostOut(lane) holds the
+// host reduction's result.
+enum class Buf : uint8_t { None, Send, Recv, Bounce, HostOut };
+struct Loc {
+  Buf buf = Buf::None;
+  uint8_t dev = 0;
+  uint8_t lane = 0;
+  size_t off = 0;
+};
+inline Loc at(Loc l, size_t by) { l.off += by; return l; }
+inline Loc send_at(int r, size_t off) { return {Buf::Send, uint8_t(r), 0, off}; }
+inline Loc recv_at(int r, size_t off) { return {Buf::Recv, uint8_t(r), 0, off}; }
+inline Loc bounce_at(int r, int lane) { return {Buf::Bounce, uint8_t(r), uint8_t(lane), 0}; }
+inline Loc hostout_at(int lane) { return {Buf::HostOut, 0, uint8_t(lane), 0}; }
+
+// Record: event := current position of stream.   Wait: stream waits event.
+// CeCopy: dst[0,bytes) := src[0,bytes) by a copy engine.
+// SmCopy: for each segment i, dst[i][0,len[i]) := src[i][0,len[i]), one kernel.
+// SmReduce: v := op-fold of src[0..nsrc) in index order; every dst[j] := v.
+// HostReduce: the same fold on the CPU over pinned-host buffers.
+// NvlsReduce: one rank's share of an NVLS AllReduce; the N NvlsReduce ops
+// of a plan form a gang that synchronizes inside the kernel.
+enum class OpKind : uint8_t { Record, Wait, CeCopy, SmCopy, SmReduce, HostReduce, NvlsReduce };
+struct PlanOp {
+  OpKind kind = OpKind::Record;
+  StreamId stream;
+  EventId event;
+  uint8_t nsrc = 0, ndst = 0;
+  Loc src[kMaxRanks];
+  Loc dst[kMaxRanks];
+  size_t len[kMaxRanks] = {};
+  size_t bytes = 0;
+};
+
+// Resources a plan needs; the executor allocates them before submitting.
+struct Needs {
+  int lanes = 0;               // host lanes used
+  size_t bounce_bytes = 0;     // per rank per lane, and per HostOut lane
+  uint16_t phase_events = 0;   // Phase(dev, index) indices per rank
+  size_t nvls_bytes = 0;       // multicast scratch per GPU
+  void merge(const Needs& o);
+};
+
+// Per-path shares in parts per 10000 of the bytes a rank receives.
+struct Shares {
+  int host_ppm = 0;
+  int ce_ppm = 0;
+};
+
+struct Plan {
+  Algo algo = Algo::Fallback;
+  CliqueDesc desc;
+  std::vector<PlanOp> ops;
+  Needs needs;
+  // Byte accounting per path (summed over ranks): what crossed NVLink by SM
+  // kernels, by copy engines, and through pinned host memory.
+  size_t sm_bytes = 0, ce_bytes = 0, host_bytes = 0;
+};
+
+// 16-byte-aligned split of `bytes` into `parts` consecutive slices; the last
+// slice takes the remainder.
+void slice_of(size_t bytes, int parts, int i, size_t* off, size_t* len);
+// Host-lane share of `len` bytes at `ppm`: a whole number of 16-byte units,
+// zero below the policy minimum.
+size_t host_share(size_t len, int ppm, const Policy& p);
+size_t ce_share(size_t len, int ppm);
+
+void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s, Plan& out);
+
+// Resources for the largest call the prewarm covers (at InitAll).
+Needs prewarm_needs(int nranks, const Policy& p, const Shares& s, bool nvls);
+
+}  // namespace nb

@@ -1,0 +1,65 @@
+// Routing policy: compile-time defaults plus a small set of runtime overrides
+// under one prefix (NCCL_B200_*). Bandwidth shares come from calibration
+// (measured at init) unless an override pins them.
+//
+// Parity: the reference freezes every threshold, chunk size and host-share
+// divisor in a constexpr `Tuning` (shim/nccl_collectives_shim.cu:47-105) and
+// reads only NCCL_SHIM_SUMMARY and NCCL_COMM_BLOCKING at run time.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <functional>
+#include <string>
+
+#include "core/types.h"
+
+namespace nb {
+
+enum class NvlsMode : uint8_t { Off, Auto, On };
+
+struct Policy {
+  bool enabled = true;              // NCCL_B200_DISABLE=1 forwards everything
+  bool kind_enabled[size_t(Kind::Count)] = {true, true, true, true};
+  // Logical-size thresholds (nccl-tests "size": N slots for AG/RS).
+  size_t min_bytes[size_t(Kind::Count)] = {32 * kMiB, 32 * kMiB, 32 * kMiB, 32 * kMiB};
+  size_t max_message_bytes = size_t(8) << 30;  // enforced logical message cap
+  bool first_pass = true;           // first eligible clique call runs on NCCL
+  NvlsMode nvls = NvlsMode::Auto;
+  int nvls_min_ranks = 4;           // NVLS AllReduce only pays off from 4 ranks
+  size_t nvls_round_bytes = 256 * kMiB;  // multicast scratch per GPU (one round)
+  Algo force_algo[size_t(Kind::Count)] = {Algo::Fallback, Algo::Fallback, Algo::Fallback,
+                                          Algo::Fallback};  // Fallback = choose
+  // Shares in parts per 10000 of the bytes each GPU receives. Negative =
+  // take the calibrated value.
+  int host_share_ppm = -1;          // pinned-host PCIe lane
+  int ce_share_ppm = -1;            // copy-engine peer copies (pure-copy shares)
+  int lanes = 4;                    // reusable pinned-host lanes per GPU
+  size_t host_piece = 16 * kMiB;    // host-lane staging piece (16-byte multiple)
+  size_t min_host_bytes = 64 * kMiB;  // below this per GPU, no host share
+  int host_threads = 8;             // CPU threads of the host reduction
+  size_t sm_chunk = 512 * kMiB;     // pipelining piece of the SM share
+  int blocks_per_sm = 2;
+  int threads = 512;
+  int bc_pieces = 4;                // scatter/all-gather broadcast pipeline depth
+  bool calibrate = true;            // measure path bandwidths at init
+  std::string calib_cache;          // JSON cache path ("" = none)
+  uint64_t device_timeout_ns = 2000000000ull;  // bound of every in-kernel wait
+  bool summary = false;             // NCCL_SHIM_SUMMARY=1 or NCCL_B200_SUMMARY=1
+  int min_nccl_version = 21900;     // supported libnccl range (ncclConfig_t layout)
+  int max_nccl_version = 22999;
+  std::string fault;                // host-side fault injector spec ("" = off)
+};
+
+using EnvLookup = std::function<const char*(const char*)>;
+
+// Defaults overridden from the environment. `lookup` is getenv in the
+// library and a map in the unit tests.
+Policy policy_from_env(const EnvLookup& lookup);
+Policy default_policy();
+
+// Parse helpers (exposed for tests): sizes accept K/M/G suffixes.
+bool parse_size(const char* s, size_t* out);
+bool parse_algo(const char* s, Kind* kind, Algo* algo);
+
+}  // namespace nb

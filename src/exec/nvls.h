@@ -1,0 +1,34 @@
+// NVLS (NVLink SHARP) support: multicast objects over the clique's GPUs and
+// the multimem AllReduce gang kernel.
+//
+// User cudaMalloc buffers cannot be bound to a multicast object, so every
+// GPU owns a multicast-bound scratch region (physical memory from
+// cuMemCreate, bound into one multicast object that spans every clique
+// device). The gang kernel copies its input into its own scratch, reduces its
+// slice through the switch with multimem.ld_reduce, multicasts the result
+// with multimem.st and copies its output out, in rounds, with bounded
+// in-kernel barriers (multimem.red on a multicast flag word per block) between
+// the phases. No TMA multicast is used anywhere.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "core/plan.h"
+#include "exec/executor.h"
+
+namespace nb {
+
+// True when every device supports multicast objects and the driver entry
+// points exist. Cheap after the first call per device set.
+bool nvls_supported(const int* devices, int n);
+// Create (or grow) the multicast scratch for this device set.
+bool nvls_ensure(const int* devices, int n, size_t bytes, std::string* why);
+cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, const Policy& p,
+                        cudaStream_t s, int dev);
+// Device-side status of the last NVLS gang on this device set: 0 ok,
+// nonzero = a bounded wait expired. Reading it synchronizes nothing.
+unsigned nvls_status(const int* devices, int n);
+
+}  // namespace nb

@@ -1,0 +1,345 @@
+// sm_100a collective kernels: fused multi-source reduce-and-push and
+// multi-segment pull copies over NVLink peer memory.
+//
+// Reduce kernel: thread i folds 16-byte vector i of every source in source
+// (= rank) order, accumulating in fp32 for fp16/bf16/fp32 (fp64 for doubles,
+// the type's own width with wrap-around for integers), applies the op's
+// finalization (average, pre-multiplied scalars) and stores the converted
+// result to every destination. Sources and destinations are plain global
+// pointers: local HBM or a peer GPU's HBM through NVLink/NVSwitch. Each
+// thread keeps ~8 independent 16-byte loads in flight to cover the NVLink
+// round trip. The per-element arithmetic is exactly the host fold's
+// (hostreduce.cc), so the host oracle is bit-exact.
+//
+// Copy kernel: a flat tile space over up to 8 (src, dst, len) segments;
+// every block takes 64 KiB tiles round-robin, so pulls from different peers
+// proceed concurrently.
+//
+// Parity: replaces the reference's shim_reduce_write_vector /
+// shim_reduce_write_tail (shim/nccl_collectives_shim.cu:772-851) and its
+// copy-engine peer copies (:1156).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "kernels/kernels.h"
+
+namespace nb {
+namespace {
+
+struct KReduceArgs {
+  const void* src[kMaxRanks];
+  void* dst[kMaxRanks];
+  const void* dev_scalar[kMaxRanks];
+  double scale[kMaxRanks];
+  unsigned long long nvec;       // whole 16-byte vectors
+  unsigned long long tail_elems; // trailing elements after the vectors
+  int ndst;
+  int op;
+  int nranks;
+};
+
+struct KCopyArgs {
+  const void* src[kMaxRanks];
+  void* dst[kMaxRanks];
+  unsigned long long len[kMaxRanks];
+  unsigned long long tile_start[kMaxRanks + 1];  // prefix sums of tiles per segment
+  int nseg;
+};
+
+constexpr int kTileBytes = 64 * 1024;
+
+template <typename T>
+struct Acc {
+  using type = T;
+};
+template <> struct Acc<__half> { using type = float; };
+template <> struct Acc<__nv_bfloat16> { using type = float; };
+template <> struct Acc<float> { using type = float; };
+template <> struct Acc<double> { using type = double; };
+
+template <typename T> __device__ __forceinline__ typename Acc<T>::type to_acc(T v) { return v; }
+template <> __device__ __forceinline__ float to_acc<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_acc<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_acc(typename Acc<T>::type v) { return T(v); }
+template <> __device__ __forceinline__ __half from_acc<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_acc<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+template <typename T> struct IsFloat { static constexpr bool value = false; };
+template <> struct IsFloat<__half> { static constexpr bool value = true; };
+template <> struct IsFloat<__nv_bfloat16> { static constexpr bool value = true; };
+template <> struct IsFloat<float> { static constexpr bool value = true; };
+template <> struct IsFloat<double> { static constexpr bool value = true; };
+
+template <typename T> struct Unsigned { using type = T; };
+template <> struct Unsigned<int8_t> { using type = uint8_t; };
+template <> struct Unsigned<int32_t> { using type = uint32_t; };
+template <> struct Unsigned<int64_t> { using type = unsigned long long; };
+template <> struct Unsigned<uint64_t> { using type = unsigned long long; };
+
+// Same ordering rules as the host fold (hostreduce.cc fold_max/fold_min).
+template <typename A>
+__device__ __forceinline__ A fmax_ord(A a, A b) {
+  if (a != a) return b;
+  if (b != b) return a;
+  if (a == b) return signbit(a) ? b : a;
+  return a > b ? a : b;
+}
+template <typename A>
+__device__ __forceinline__ A fmin_ord(A a, A b) {
+  if (a != a) return b;
+  if (b != b) return a;
+  if (a == b) return signbit(a) ? a : b;
+  return a < b ? a : b;
+}
+
+__device__ __forceinline__ float fma_rn(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ double fma_rn(double a, double b, double c) { return __fma_rn(a, b, c); }
+
+template <typename T>
+__device__ __forceinline__ typename Acc<T>::type combine(typename Acc<T>::type acc, T xv, int op,
+                                                         typename Acc<T>::type s) {
+  using A = typename Acc<T>::type;
+  const A x = to_acc<T>(xv);
+  if constexpr (IsFloat<T>::value) {
+    switch (op) {
+      case int(RedOp::Prod): return acc * x;
+      case int(RedOp::Max): return fmax_ord(acc, x);
+      case int(RedOp::Min): return fmin_ord(acc, x);
+      case int(RedOp::PreMulSum): return fma_rn(x, s, acc);
+      default: return acc + x;
+    }
+  } else {
+    using U = typename Unsigned<T>::type;
+    switch (op) {
+      case int(RedOp::Prod): return T(U(acc) * U(x));
+      case int(RedOp::Max): return acc > x ? acc : x;
+      case int(RedOp::Min): return acc < x ? acc : x;
+      default: return T(U(acc) + U(x));
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ T finish(typename Acc<T>::type acc, int op, int nranks) {
+  using A = typename Acc<T>::type;
+  if (op == int(RedOp::Avg)) {
+    if constexpr (IsFloat<T>::value) acc = acc / A(nranks);
+    else acc = T(T(acc) / T(nranks));
+  }
+  return from_acc<T>(acc);
+}
+
+template <typename T>
+__device__ __forceinline__ typename Acc<T>::type first(T xv, int op, typename Acc<T>::type s) {
+  using A = typename Acc<T>::type;
+  A x = to_acc<T>(xv);
+  if constexpr (IsFloat<T>::value) {
+    if (op == int(RedOp::PreMulSum)) x = x * s;
+  }
+  return x;
+}
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+  __stcs(reinterpret_cast<uint4*>(p), v);
+}
+
+template <typename T>
+__device__ __forceinline__ typename Acc<T>::type load_scale(const KReduceArgs& a, int s) {
+  using A = typename Acc<T>::type;
+  if (a.dev_scalar[s]) return to_acc<T>(*reinterpret_cast<const T*>(a.dev_scalar[s]));
+  return A(a.scale[s]);
+}
+
+// One 16-byte vector of every source -> folded vector.
+template <typename T, int NSRC>
+__device__ __forceinline__ uint4 fold_vec(const uint4 (&v)[NSRC], int op, int nranks,
+                                          const typename Acc<T>::type (&s)[NSRC]) {
+  using A = typename Acc<T>::type;
+  constexpr int E = 16 / sizeof(T);
+  uint4 out;
+  const T* in0 = reinterpret_cast<const T*>(&v[0]);
+  T* o = reinterpret_cast<T*>(&out);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    A acc = first<T>(in0[e], op, s[0]);
+#pragma unroll
+    for (int k = 1; k < NSRC; ++k) acc = combine<T>(acc, reinterpret_cast<const T*>(&v[k])[e], op, s[k]);
+    o[e] = finish<T>(acc, op, nranks);
+  }
+  return out;
+}
+
+template <typename T, int NSRC>
+__global__ void __launch_bounds__(512, 2) reduce_kernel(const __grid_constant__ KReduceArgs a) {
+  using A = typename Acc<T>::type;
+  constexpr int U = (8 / NSRC) > 0 ? (8 / NSRC) : 1;
+  A s[NSRC];
+#pragma unroll
+  for (int k = 0; k < NSRC; ++k) s[k] = load_scale<T>(a, k);
+  const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+  const unsigned long long tid = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (unsigned long long base = tid; base < a.nvec; base += stride * U) {
+    uint4 v[U][NSRC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const unsigned long long idx = base + u * stride;
+      if (idx < a.nvec) {
+#pragma unroll
+        for (int k = 0; k < NSRC; ++k)
+          v[u][k] = ld_stream(static_cast<const uint4*>(a.src[k]) + idx);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const unsigned long long idx = base + u * stride;
+      if (idx < a.nvec) {
+        const uint4 out = fold_vec<T, NSRC>(v[u], a.op, a.nranks, s);
+        for (int d = 0; d < a.ndst; ++d) st_stream(static_cast<uint4*>(a.dst[d]) + idx, out);
+      }
+    }
+  }
+  // Trailing elements that do not fill a 16-byte vector.
+  if (blockIdx.x == 0 && threadIdx.x < a.tail_elems) {
+    const unsigned long long e = a.nvec * (16 / sizeof(T)) + threadIdx.x;
+    A acc = first<T>(static_cast<const T*>(a.src[0])[e], a.op, s[0]);
+#pragma unroll
+    for (int k = 1; k < NSRC; ++k) acc = combine<T>(acc, static_cast<const T*>(a.src[k])[e], a.op, s[k]);
+    const T out = finish<T>(acc, a.op, a.nranks);
+    for (int d = 0; d < a.ndst; ++d) static_cast<T*>(a.dst[d])[e] = out;
+  }
+}
+
+__global__ void __launch_bounds__(512) copy_kernel(const __grid_constant__ KCopyArgs a) {
+  const unsigned long long tiles = a.tile_start[a.nseg];
+  for (unsigned long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+    int s = 0;
+    while (s + 1 < a.nseg && t >= a.tile_start[s + 1]) ++s;
+    const unsigned long long lo = (t - a.tile_start[s]) * kTileBytes;
+    const unsigned long long hi = min(lo + (unsigned long long)kTileBytes, a.len[s]);
+    const char* src = static_cast<const char*>(a.src[s]) + lo;
+    char* dst = static_cast<char*>(a.dst[s]) + lo;
+    const unsigned long long n = hi - lo;
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+      const unsigned long long nvec = n / 16;
+      constexpr int U = 8;
+      for (unsigned long long base = threadIdx.x; base < nvec; base += blockDim.x * U) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const unsigned long long i = base + u * blockDim.x;
+          if (i < nvec) v[u] = ld_stream(reinterpret_cast<const uint4*>(src) + i);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const unsigned long long i = base + u * blockDim.x;
+          if (i < nvec) st_stream(reinterpret_cast<uint4*>(dst) + i, v[u]);
+        }
+      }
+      for (unsigned long long i = nvec * 16 + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    } else if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | n) & 3) == 0) {
+      const unsigned long long nw = n / 4;
+      for (unsigned long long i = threadIdx.x; i < nw; i += blockDim.x)
+        reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
+    } else {
+      for (unsigned long long i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    }
+  }
+}
+
+using ReduceFn = void (*)(KReduceArgs);
+
+template <typename T>
+ReduceFn reduce_for(int nsrc) {
+  switch (nsrc) {
+    case 1: return reduce_kernel<T, 1>;
+    case 2: return reduce_kernel<T, 2>;
+    case 3: return reduce_kernel<T, 3>;
+    case 4: return reduce_kernel<T, 4>;
+    case 5: return reduce_kernel<T, 5>;
+    case 6: return reduce_kernel<T, 6>;
+    case 7: return reduce_kernel<T, 7>;
+    case 8: return reduce_kernel<T, 8>;
+    default: return nullptr;
+  }
+}
+
+ReduceFn pick_reduce(DType t, int nsrc) {
+  switch (t) {
+    case DType::F32: return reduce_for<float>(nsrc);
+    case DType::F16: return reduce_for<__half>(nsrc);
+    case DType::BF16: return reduce_for<__nv_bfloat16>(nsrc);
+    case DType::F64: return reduce_for<double>(nsrc);
+    case DType::I8: return reduce_for<int8_t>(nsrc);
+    case DType::U8: return reduce_for<uint8_t>(nsrc);
+    case DType::I32: return reduce_for<int32_t>(nsrc);
+    case DType::U32: return reduce_for<uint32_t>(nsrc);
+    case DType::I64: return reduce_for<int64_t>(nsrc);
+    case DType::U64: return reduce_for<uint64_t>(nsrc);
+    default: return nullptr;
+  }
+}
+
+}  // namespace
+
+LaunchShape shape_for(size_t bytes, int sm_count, int blocks_per_sm, int threads) {
+  LaunchShape s;
+  s.threads = threads;
+  const size_t per_block = size_t(threads) * 16 * 8;
+  const size_t want = (bytes + per_block - 1) / per_block;
+  const size_t cap = size_t(std::max(1, sm_count) * std::max(1, blocks_per_sm));
+  s.blocks = int(std::max<size_t>(1, std::min(want, cap)));
+  return s;
+}
+
+cudaError_t launch_reduce(const ReduceLaunch& r, LaunchShape shape, cudaStream_t stream) {
+  const size_t es = elem_size(r.fold.dtype);
+  if (!es || r.nsrc < 1 || r.nsrc > kMaxRanks || r.ndst < 1 || r.ndst > kMaxRanks ||
+      r.bytes % es)
+    return cudaErrorInvalidValue;
+  const ReduceFn fn = pick_reduce(r.fold.dtype, r.nsrc);
+  if (!fn) return cudaErrorInvalidValue;
+  if (r.bytes == 0) return cudaSuccess;
+  KReduceArgs k{};
+  for (int i = 0; i < r.nsrc; ++i) {
+    k.src[i] = r.src[i];
+    k.dev_scalar[i] = r.dev_scalar[i];
+    k.scale[i] = r.fold.scalars[i];
+  }
+  for (int i = 0; i < r.ndst; ++i) k.dst[i] = r.dst[i];
+  k.nvec = r.bytes / 16;
+  k.tail_elems = (r.bytes - k.nvec * 16) / es;
+  k.ndst = r.ndst;
+  k.op = int(r.fold.op);
+  k.nranks = r.fold.nranks;
+  void* argv[] = {&k};
+  return cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3(unsigned(shape.blocks)),
+                          dim3(unsigned(shape.threads)), argv, 0, stream);
+}
+
+cudaError_t launch_copy(const CopyLaunch& c, LaunchShape shape, cudaStream_t stream) {
+  if (c.nseg < 1 || c.nseg > kMaxRanks) return cudaErrorInvalidValue;
+  KCopyArgs k{};
+  k.nseg = c.nseg;
+  unsigned long long tiles = 0;
+  for (int i = 0; i < c.nseg; ++i) {
+    k.src[i] = c.src[i];
+    k.dst[i] = c.dst[i];
+    k.len[i] = c.len[i];
+    k.tile_start[i] = tiles;
+    tiles += (c.len[i] + kTileBytes - 1) / kTileBytes;
+  }
+  k.tile_start[c.nseg] = tiles;
+  if (!tiles) return cudaSuccess;
+  const unsigned blocks = unsigned(std::min<unsigned long long>(tiles, (unsigned long long)shape.blocks));
+  void* argv[] = {&k};
+  return cudaLaunchKernel(reinterpret_cast<const void*>(copy_kernel), dim3(blocks),
+                          dim3(unsigned(shape.threads)), argv, 0, stream);
+}
+
+}  // namespace nb
