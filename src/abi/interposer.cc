@@ -122,13 +122,13 @@ void resolve_all() {
 
 Shares shares_for(Algo a, int n, const CallDesc& c) {
   Runtime& r = rt();
-  Shares s = r.calibrated_done ? shares_from(last_calibration(), a, n) : Shares{};
+  Shares s = n >= 1 && n <= kMaxRanks && r.calib[n].valid ? shares_from(r.calib[n], a, n) : Shares{};
   if (r.policy.host_share_ppm >= 0) s.host_ppm = r.policy.host_share_ppm;
   if (r.policy.ce_share_ppm >= 0) s.ce_ppm = r.policy.ce_share_ppm;
   if (n <= 1 || a == Algo::ArNvls) s.host_ppm = s.ce_ppm = 0;
   // Device-resident PreMulSum scalars cannot be applied by the host fold.
   if (c.op == RedOp::PreMulSum && c.scalar_residence == 0) s.host_ppm = 0;
-  if (a == Algo::RsPull || a == Algo::BcScatter) s.ce_ppm = 0;
+  if (a == Algo::RsPull || a == Algo::RsStaged || a == Algo::ArStaged) s.ce_ppm = 0;
   return s;
 }
 
@@ -141,14 +141,34 @@ void prewarm(const int* devices, int n) {
     if (r.summary.enabled()) r.summary.note("prewarm_failed " + why);
     return;
   }
-  if (!r.calibrated_done && r.policy.calibrate && n > 1) {
-    r.calibrated = calibrate_shares(devices, n, r.policy, &r.summary);
-    r.calibrated_done = true;
+  if (r.policy.calibrate && n > 1 && !r.calib_tried[n]) {
+    r.calib_tried[n] = true;
+    const std::string key = calib_cache_key(devices, n);
+    CalibResult c;
+    if (calib_load(r.policy.calib_cache, key, &c)) {
+      r.summary.note("calibration loaded from " + r.policy.calib_cache);
+    } else {
+      c = calibrate(devices, n, r.policy, &r.summary);
+      if (c.valid && r.policy.tune) tune_routes(devices, n, r.policy.tune_bytes, &c);
+      calib_save(r.policy.calib_cache, key, c);
+    }
+    r.calib[n] = c;
+    if (c.valid) {
+      char line[200];
+      std::snprintf(line, sizeof line, "routes n=%d allreduce=%s allgather=%s(ce=%d) reducescatter=%s "
+                    "broadcast=%s(ce=%d)", n, algo_name(Algo(c.preferred[0])),
+                    algo_name(Algo(c.preferred[1])), c.ce_ppm[1], algo_name(Algo(c.preferred[2])),
+                    algo_name(Algo(c.preferred[3])), c.ce_ppm[3]);
+      r.summary.note(line);
+    }
   }
-  Shares s = r.calibrated;
-  if (r.policy.host_share_ppm >= 0) s.host_ppm = r.policy.host_share_ppm;
+  Shares s = shares_for(Algo::ArTwoShot, n, CallDesc{});
   const bool nvls = r.policy.nvls != NvlsMode::Off && nvls_supported(devices, n);
-  const Needs needs = prewarm_needs(n, r.policy, s, nvls);
+  Needs needs = prewarm_needs(n, r.policy, s, nvls);
+  // Scratch of the staged routes, sized for the tuned choice.
+  if (n > 1 && (r.calib[n].preferred[0] == int(Algo::ArStaged) ||
+                r.calib[n].preferred[2] == int(Algo::RsStaged)))
+    needs.temp_bytes = size_t(r.policy.stage_depth) * size_t(n - 1) * r.policy.stage_piece;
   if (!r.exec.ensure(needs, devices, n, &why)) {
     cudaGetLastError();
     if (r.summary.enabled()) r.summary.note("prewarm_failed " + why);
@@ -248,6 +268,8 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
     for (const Call& c : calls)
       if (stream_capturing(static_cast<cudaStream_t>(c.stream), c.desc.device)) st.capturing = true;
     st.nvls_available = r.policy.nvls != NvlsMode::Off && nvls_supported(info.devices, info.nranks);
+    if (r.calib[info.nranks].valid)
+      for (int k = 0; k < int(Kind::Count); ++k) st.preferred[k] = Algo(r.calib[info.nranks].preferred[k]);
   }
   const CliqueDecision d = gate_clique(descs, st, r.policy);
   reason = d.reason;
@@ -676,9 +698,10 @@ size_t nb_summary_text(char* buf, size_t cap) {
   }
   return all.size();
 }
-void nb_shares(int* host_ppm, int* ce_ppm) {
-  *host_ppm = rt().calibrated.host_ppm;
-  *ce_ppm = rt().calibrated.ce_ppm;
+// The tuned route of a collective kind on cliques of n ranks (-1 untuned).
+int nb_route(int n, int kind) {
+  if (n < 1 || n > kMaxRanks || kind < 0 || kind >= int(Kind::Count) || !rt().calib[n].valid) return -1;
+  return rt().calib[n].preferred[kind];
 }
 
 }  // extern "C"

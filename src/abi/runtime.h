@@ -7,6 +7,7 @@
 #include <mutex>
 #include <string>
 
+#include "core/calib_model.h"
 #include "core/clique.h"
 #include "core/fault.h"
 #include "core/group.h"
@@ -47,9 +48,15 @@ struct Runtime {
   bool first_pass_done = false;
   bool nccl_supported = false;
   int nccl_version = 0;
-  Shares calibrated;  // measured at the first prewarm (zero until then)
-  bool calibrated_done = false;
+  // Path rates and tuned routes per clique size (measured at the first
+  // prewarm of a clique of that size, or loaded from the cache).
+  CalibResult calib[kMaxRanks + 1];
+  bool calib_tried[kMaxRanks + 1] = {};
 };
+
+// Time every candidate route on the clique's GPUs at `bytes` and record the
+// fastest per collective kind (abi/tune.cc).
+void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out);
 
 Runtime& rt();
 // Resolve the real libnccl once (dlsym RTLD_NEXT, then the loaded

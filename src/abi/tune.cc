@@ -1,0 +1,161 @@
+// Init-time route tuning: every candidate route of each collective runs on
+// the clique's own GPUs (one warm-up and three timed runs on scratch
+// buffers, CUDA events on every GPU, max over GPUs) and the fastest one is
+// kept per collective kind. Candidates: AllReduce fused two-shot / staged /
+// NVLS; ReduceScatter fused pull / staged; AllGather and Broadcast with SM or
+// copy-engine data movement.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "abi/runtime.h"
+#include "core/plan.h"
+#include "exec/nvls.h"
+
+namespace nb {
+
+namespace {
+
+struct Candidate {
+  Algo algo;
+  int ce_ppm;
+};
+
+std::vector<Candidate> candidates(Kind k, int n, bool nvls) {
+  switch (k) {
+    case Kind::AllReduce: {
+      std::vector<Candidate> v{{Algo::ArTwoShot, 0}, {Algo::ArStaged, 0}};
+      if (nvls && n >= 2) v.push_back({Algo::ArNvls, 0});
+      return v;
+    }
+    case Kind::ReduceScatter: return {{Algo::RsPull, 0}, {Algo::RsStaged, 0}};
+    case Kind::AllGather: return {{Algo::AgPull, 0}, {Algo::AgPull, 10000}};
+    case Kind::Broadcast:
+      if (n >= 3) return {{Algo::BcScatter, 0}, {Algo::BcScatter, 10000}, {Algo::BcPull, 10000}};
+      return {{Algo::BcPull, 0}, {Algo::BcPull, 10000}};
+    default: return {};
+  }
+}
+
+double busbw_factor(Kind k, int n) {
+  if (n <= 1) return 1.0;
+  if (k == Kind::AllReduce) return 2.0 * (n - 1) / n;
+  if (k == Kind::AllGather || k == Kind::ReduceScatter) return double(n - 1) / n;
+  return 1.0;
+}
+
+}  // namespace
+
+void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
+  Runtime& r = rt();
+  if (n < 2) return;
+  bytes = (bytes / (size_t(n) * 256)) * size_t(n) * 256;
+  std::vector<void*> send(size_t(n), nullptr), recv(size_t(n), nullptr);
+  std::vector<cudaStream_t> streams(size_t(n), nullptr);
+  std::vector<cudaEvent_t> e0(size_t(n), nullptr), e1(size_t(n), nullptr);
+  bool ok = true;
+  for (int i = 0; i < n && ok; ++i) {
+    ok = cudaSetDevice(devices[i]) == cudaSuccess && cudaMalloc(&send[size_t(i)], bytes) == cudaSuccess &&
+         cudaMalloc(&recv[size_t(i)], bytes) == cudaSuccess &&
+         cudaMemset(send[size_t(i)], 0, bytes) == cudaSuccess &&
+         cudaStreamCreateWithFlags(&streams[size_t(i)], cudaStreamNonBlocking) == cudaSuccess &&
+         cudaEventCreate(&e0[size_t(i)]) == cudaSuccess && cudaEventCreate(&e1[size_t(i)]) == cudaSuccess;
+  }
+  const bool nvls = r.policy.nvls != NvlsMode::Off && nvls_supported(devices, n);
+  for (int kk = 0; ok && kk < int(Kind::Count); ++kk) {
+    const Kind kind = Kind(kk);
+    CliqueDesc d;
+    d.kind = kind;
+    d.dtype = DType::F32;
+    d.op = RedOp::Sum;
+    d.nranks = n;
+    d.bytes = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? bytes / size_t(n) : bytes;
+    d.count = d.bytes / 4;
+    d.root = 0;
+    Binding b;
+    b.nranks = n;
+    b.fold.dtype = DType::F32;
+    b.fold.op = RedOp::Sum;
+    b.fold.nranks = n;
+    for (int i = 0; i < n; ++i) {
+      b.device[i] = devices[i];
+      b.stream[i] = streams[size_t(i)];
+      b.send[i] = send[size_t(i)];
+      b.recv[i] = recv[size_t(i)];
+    }
+    double best_ms = 1e30;
+    Candidate best{Algo::Fallback, -1};
+    for (const Candidate& c : candidates(kind, n, nvls)) {
+      Shares s;
+      s.ce_ppm = c.ce_ppm;
+      Plan plan;
+      build_plan(c.algo, d, r.policy, s, plan);
+      std::string why;
+      if (!r.exec.ensure(plan.needs, devices, n, &why)) {
+        cudaGetLastError();
+        continue;
+      }
+      bool good = true;
+      float ms = 0;
+      for (int rep = 0; rep < 2 && good; ++rep) {  // rep 0 warms up
+        for (int i = 0; i < n; ++i) {
+          cudaSetDevice(devices[i]);
+          cudaEventRecord(e0[size_t(i)], streams[size_t(i)]);
+        }
+        const int runs = rep ? 3 : 1;
+        for (int k = 0; k < runs && good; ++k) {
+          cudaError_t err = cudaSuccess;
+          good = r.exec.execute(plan, b, &err, nullptr) == ExecStatus::Ok;
+        }
+        float worst = 0;
+        for (int i = 0; i < n && good; ++i) {
+          cudaSetDevice(devices[i]);
+          cudaEventRecord(e1[size_t(i)], streams[size_t(i)]);
+        }
+        for (int i = 0; i < n && good; ++i) {
+          cudaSetDevice(devices[i]);
+          float t = 0;
+          good = cudaEventSynchronize(e1[size_t(i)]) == cudaSuccess &&
+                 cudaEventElapsedTime(&t, e0[size_t(i)], e1[size_t(i)]) == cudaSuccess;
+          worst = t > worst ? t : worst;
+        }
+        ms = worst / float(runs);
+      }
+      if (!good) {
+        cudaGetLastError();
+        r.exec.drain(devices, n);
+        continue;
+      }
+      char line[160];
+      const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? bytes : d.bytes;
+      std::snprintf(line, sizeof line, "tune %s n=%d %s ce_ppm=%d busbw_gbs=%.1f",
+                    kind_name(kind), n, algo_name(c.algo), c.ce_ppm,
+                    logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
+      r.summary.note(line);
+      if (ms < best_ms) {
+        best_ms = ms;
+        best = c;
+      }
+    }
+    if (best.algo != Algo::Fallback) {
+      out->preferred[kk] = int(best.algo);
+      out->ce_ppm[kk] = best.ce_ppm;
+      const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? bytes : d.bytes;
+      out->route_gbs[kk] = logical / (best_ms * 1e-3) / 1e9 * busbw_factor(kind, n);
+    }
+  }
+  for (int i = 0; i < n; ++i) {
+    cudaSetDevice(devices[i]);
+    cudaDeviceSynchronize();
+    if (send[size_t(i)]) cudaFree(send[size_t(i)]);
+    if (recv[size_t(i)]) cudaFree(recv[size_t(i)]);
+    if (streams[size_t(i)]) cudaStreamDestroy(streams[size_t(i)]);
+    if (e0[size_t(i)]) cudaEventDestroy(e0[size_t(i)]);
+    if (e1[size_t(i)]) cudaEventDestroy(e1[size_t(i)]);
+  }
+  cudaGetLastError();
+}
+
+}  // namespace nb

@@ -40,20 +40,27 @@ Shares shares_from(const CalibResult& c, Algo a, int n) {
   if (h < 0.03) h = 0;  // the predicted gain is about h: not worth the lanes
   h = std::min(h, 0.25);
   s.host_ppm = int(h * 10000.0);
-  const bool ce_algo = a == Algo::ArTwoShot || a == Algo::AgPull || a == Algo::BcPull;
+  const bool ce_algo = a == Algo::ArTwoShot || a == Algo::AgPull || a == Algo::BcPull ||
+                       a == Algo::BcScatter;
   if (ce_algo && c.nvlink_mix_gbs > 1.03 * bnv && c.mix_ce_fraction > 0)
     s.ce_ppm = int(std::min(0.5, c.mix_ce_fraction) * 10000.0);
+  // A measured route choice overrides the model's copy-engine share.
+  for (int k = 0; k < 4; ++k)
+    if (c.preferred[k] == int(a) && c.ce_ppm[k] >= 0) s.ce_ppm = c.ce_ppm[k];
   return s;
 }
 
 std::string calib_to_json(const CalibResult& c, const std::string& key) {
-  char buf[1024];
+  char buf[1536];
   std::snprintf(buf, sizeof buf,
                 "{\"key\": \"%s\", \"nvlink_sm_gbs\": %.3f, \"nvlink_ce_gbs\": %.3f, "
                 "\"nvlink_mix_gbs\": %.3f, \"mix_ce_fraction\": %.5f, \"pcie_d2h_gbs\": %.3f, "
-                "\"pcie_h2d_gbs\": %.3f, \"fold_gbs\": %.3f}\n",
+                "\"pcie_h2d_gbs\": %.3f, \"fold_gbs\": %.3f, "
+                "\"pref0\": %d, \"pref1\": %d, \"pref2\": %d, \"pref3\": %d, "
+                "\"ce0\": %d, \"ce1\": %d, \"ce2\": %d, \"ce3\": %d}\n",
                 key.c_str(), c.nvlink_sm_gbs, c.nvlink_ce_gbs, c.nvlink_mix_gbs, c.mix_ce_fraction,
-                c.pcie_d2h_gbs, c.pcie_h2d_gbs, c.fold_gbs);
+                c.pcie_d2h_gbs, c.pcie_h2d_gbs, c.fold_gbs, c.preferred[0], c.preferred[1],
+                c.preferred[2], c.preferred[3], c.ce_ppm[0], c.ce_ppm[1], c.ce_ppm[2], c.ce_ppm[3]);
   return buf;
 }
 
@@ -81,6 +88,12 @@ bool calib_from_json(const std::string& text, const std::string& key, CalibResul
             json_number(text, "pcie_h2d_gbs", &c.pcie_h2d_gbs) &&
             json_number(text, "fold_gbs", &c.fold_gbs);
   if (!ok) return false;
+  for (int k = 0; k < 4; ++k) {
+    double v = 0;
+    const std::string pn = "pref" + std::to_string(k), cn = "ce" + std::to_string(k);
+    if (json_number(text, pn.c_str(), &v)) c.preferred[k] = int(v);
+    if (json_number(text, cn.c_str(), &v)) c.ce_ppm[k] = int(v);
+  }
   c.valid = true;
   *out = c;
   return true;

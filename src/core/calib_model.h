@@ -28,6 +28,11 @@ struct CalibResult {
   double pcie_d2h_gbs = 0;    // per GPU, every GPU at once, D2H and H2D together
   double pcie_h2d_gbs = 0;
   double fold_gbs = 0;        // host fold input throughput (all threads)
+  // Route tuning: the fastest measured algorithm per collective kind and
+  // its copy-engine share (parts per 10000), -1 / Fallback when untuned.
+  int preferred[4] = {0, 0, 0, 0};
+  int ce_ppm[4] = {-1, -1, -1, -1};
+  double route_gbs[4] = {0, 0, 0, 0};  // busbw of the chosen route at the tuning size
 };
 
 Shares shares_from(const CalibResult& c, Algo a, int n);

@@ -260,6 +260,39 @@ int nb_plan_simulate(int algo, int kind, int dtype, int op, int nranks, uint64_t
   return 0;
 }
 
+// Checker self-test: build a plan, delete its `drop`-th Wait op, and report
+// whether the happens-before checker rejects the mutated plan (1), accepts
+// it (0), or the plan has fewer waits (-1). A checker that accepts plans
+// with missing waits would let real ordering bugs through.
+int nb_plan_mutation(int algo, int kind, int nranks, uint64_t count, int host_ppm, int ce_ppm,
+                     const char* env, int drop, char* err, size_t errcap) {
+  const Policy p = EnvMap(env).policy();
+  CliqueDesc d;
+  d.kind = Kind(kind);
+  d.dtype = DType::F32;
+  d.op = RedOp::Sum;
+  d.nranks = nranks;
+  d.count = size_t(count);
+  d.bytes = d.count * 4;
+  d.root = 0;
+  Shares s;
+  s.host_ppm = host_ppm;
+  s.ce_ppm = ce_ppm;
+  Plan plan;
+  build_plan(Algo(algo), d, p, s, plan);
+  int seen = 0;
+  for (size_t i = 0; i < plan.ops.size(); ++i) {
+    if (plan.ops[i].kind != OpKind::Wait) continue;
+    if (seen++ == drop) {
+      plan.ops.erase(plan.ops.begin() + long(i));
+      const std::string r = check_plan(plan, layout_for(d));
+      copy_out(r, err, errcap);
+      return r.empty() ? 0 : 1;
+    }
+  }
+  return -1;
+}
+
 // Host fold exposed directly (tests compare it with numpy / serial sums).
 void nb_host_fold(int dtype, int op, int nranks, const void* const* srcs, int nsrc, void* dst,
                   uint64_t bytes, const double* scalars, int threads) {
@@ -363,6 +396,15 @@ class FakeBackend final : public GroupBackend {
   }
   const Policy& policy() override { return policy_; }
   Outcome run(std::vector<Call>& calls, Reason& reason) override {
+    // Like the real clique gate: one call per rank, all of one kind.
+    unsigned ranks = 0;
+    for (const Call& c : calls) {
+      if ((ranks >> c.desc.rank) & 1u || c.desc.kind != calls[0].desc.kind) {
+        reason = Reason::NotClique;
+        return Outcome::Fallback;
+      }
+      ranks |= 1u << c.desc.rank;
+    }
     reason = Reason::None;
     if (run_result_ == 1) return Outcome::Fallback;
     if (run_result_ == 2) return Outcome::Error;

@@ -65,14 +65,20 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
     case Algo::AgPull: return k == Kind::AllGather;
     case Algo::BcPull: return k == Kind::Broadcast;
     case Algo::BcScatter: return k == Kind::Broadcast && nranks >= 3;
+    case Algo::ArStaged: return k == Kind::AllReduce;
+    case Algo::RsStaged: return k == Kind::ReduceScatter;
     default: return false;
   }
 }
 
-Algo choose_algo(const CallDesc& c, int nranks, bool nvls_available, const Policy& p) {
+Algo choose_algo(const CallDesc& c, int nranks, bool nvls_available, const Policy& p,
+                 Algo preferred) {
   const Algo forced = p.force_algo[size_t(c.kind)];
   if (forced != Algo::Fallback && algo_valid(forced, c.kind, nranks, c.dtype, c.op, nvls_available))
     return forced;
+  if (preferred != Algo::Fallback &&
+      algo_valid(preferred, c.kind, nranks, c.dtype, c.op, nvls_available))
+    return preferred;
   switch (c.kind) {
     case Kind::AllReduce: {
       const bool nvls = p.nvls != NvlsMode::Off &&
@@ -118,7 +124,7 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
   }
   if (s.capturing) return fallback(Reason::Capturing);
   if (p.first_pass && !s.first_pass_done) return fallback(Reason::FirstPass);
-  const Algo algo = choose_algo(a, n, s.nvls_available, p);
+  const Algo algo = choose_algo(a, n, s.nvls_available, p, s.preferred[size_t(a.kind)]);
   if (algo == Algo::Fallback) return fallback(Reason::PolicyFallback);
   return {algo, Reason::None};
 }

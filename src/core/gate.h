@@ -29,6 +29,10 @@ struct CliqueState {
   bool poisoned = false;
   bool nccl_supported = true;  // libnccl inside the supported version range
   bool nvls_available = false; // multicast objects usable on this clique
+  // Per-kind algorithm the init-time calibration measured fastest on this
+  // clique (Fallback = no preference).
+  Algo preferred[size_t(Kind::Count)] = {Algo::Fallback, Algo::Fallback, Algo::Fallback,
+                                         Algo::Fallback};
 };
 
 struct CliqueDecision {
@@ -41,7 +45,8 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
                            const Policy& p);
 
 // Algorithm choice for an eligible clique call.
-Algo choose_algo(const CallDesc& c, int nranks, bool nvls_available, const Policy& p);
+Algo choose_algo(const CallDesc& c, int nranks, bool nvls_available, const Policy& p,
+                 Algo preferred = Algo::Fallback);
 bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_available);
 
 // A gated clique as the planner sees it: no pointers, everything indexed by

@@ -16,6 +16,7 @@ void Needs::merge(const Needs& o) {
   bounce_bytes = std::max(bounce_bytes, o.bounce_bytes);
   phase_events = std::max(phase_events, o.phase_events);
   nvls_bytes = std::max(nvls_bytes, o.nvls_bytes);
+  temp_bytes = std::max(temp_bytes, o.temp_bytes);
 }
 
 void slice_of(size_t bytes, int parts, int i, size_t* off, size_t* len) {
@@ -262,15 +263,11 @@ void plan_ar_twoshot(Builder& b, const CliqueDesc& d, const Shares& s) {
     ce[r] = n > 1 ? ce_share(len[r] - host[r], s.ce_ppm) : 0;
   }
   for (int r = 0; r < n; ++r) {
+    // Slice layout [copy-engine part | host part | SM part]: the first two
+    // are whole 16-byte units, so every part starts 16-byte aligned and only
+    // the SM part (last) can end in a partial vector.
     const size_t sm = len[r] - host[r] - ce[r];
-    Loc src[kMaxRanks], dst[kMaxRanks];
-    for (int q = 0; q < n; ++q) {
-      b.touch({Strm::Caller, uint8_t(r), 0}, q);
-      src[q] = send_at(q, off[r]);
-      dst[q] = recv_at(q, off[r]);
-    }
-    b.sm_reduce({Strm::Caller, uint8_t(r), 0}, src, n, dst, n, sm);
-    b.plan().sm_bytes += sm * size_t(2 * (n - 1));
+    for (int q = 0; q < n; ++q) b.touch({Strm::Caller, uint8_t(r), 0}, q);
     if (ce[r]) {
       // Reduce the copy-engine part into this rank's output only, in
       // pieces, and push each piece to every peer from this GPU.
@@ -279,8 +276,8 @@ void plan_ar_twoshot(Builder& b, const CliqueDesc& d, const Shares& s) {
       for (size_t rel = 0; rel < ce[r]; rel += piece, ++k) {
         const size_t cb = std::min(piece, ce[r] - rel);
         Loc src2[kMaxRanks];
-        for (int q = 0; q < n; ++q) src2[q] = send_at(q, off[r] + sm + rel);
-        Loc own = recv_at(r, off[r] + sm + rel);
+        for (int q = 0; q < n; ++q) src2[q] = send_at(q, off[r] + rel);
+        Loc own = recv_at(r, off[r] + rel);
         b.sm_reduce({Strm::Caller, uint8_t(r), 0}, src2, n, &own, 1, cb);
         b.record({Ev::Phase, uint8_t(r), 0, uint16_t(k)}, {Strm::Caller, uint8_t(r), 0});
         const StreamId cs{Strm::Copy, uint8_t(r), 0};
@@ -288,16 +285,23 @@ void plan_ar_twoshot(Builder& b, const CliqueDesc& d, const Shares& s) {
         for (int q = 0; q < n; ++q) {
           if (q == r) continue;
           b.touch(cs, q);
-          b.ce_copy(cs, recv_at(q, off[r] + sm + rel), own, cb);
+          b.ce_copy(cs, recv_at(q, off[r] + rel), own, cb);
         }
       }
       b.plan().sm_bytes += ce[r] * size_t(n - 1);
       b.plan().ce_bytes += ce[r] * size_t(n - 1);
     }
+    Loc src[kMaxRanks], dst[kMaxRanks];
+    for (int q = 0; q < n; ++q) {
+      src[q] = send_at(q, off[r] + ce[r] + host[r]);
+      dst[q] = recv_at(q, off[r] + ce[r] + host[r]);
+    }
+    b.sm_reduce({Strm::Caller, uint8_t(r), 0}, src, n, dst, n, sm);
+    b.plan().sm_bytes += sm * size_t(2 * (n - 1));
   }
   for (int r = 0; r < n; ++r) {
     if (!host[r]) continue;
-    const size_t base = off[r] + len[r] - host[r];
+    const size_t base = off[r] + ce[r];
     Loc src[kMaxRanks], dst[kMaxRanks];
     for (int q = 0; q < n; ++q) {
       src[q] = send_at(q, base);
@@ -337,6 +341,100 @@ void plan_rs_pull(Builder& b, const CliqueDesc& d, const Shares& s) {
   b.join();
 }
 
+// Copy-engine staged AllReduce / ReduceScatter. Rank r owns slice r (AR) or
+// slot r (RS). For each piece of it, rank r's copy engine pulls that piece of
+// every peer's input into r's scratch (Copy stream); the caller stream folds
+// the local input and the staged peer pieces, in rank order, into r's output
+// with one local kernel (HBM-bound, fp32 accumulation); for AllReduce the
+// Push stream's copy engine then writes the reduced piece into every peer's
+// output. Scratch holds `stage_depth` pieces per peer; a piece's scratch is
+// refilled only after its fold, and a call's first fill waits for the
+// previous staged call's last fold (TempFree). Every NVLink byte moves by
+// copy engine, which keeps the link at its bidirectional copy rate.
+// Optional host share: the first part of each slice through the host lanes.
+void plan_staged(Builder& b, const CliqueDesc& d, const Shares& s, bool allreduce) {
+  const int n = b.n();
+  b.prologue();
+  const Policy& p = b.policy();
+  const size_t piece = p.stage_piece;
+  const int depth = p.stage_depth;
+  int ranks[kMaxRanks];
+  all_ranks(n, ranks);
+  if (n > 1) b.plan().needs.temp_bytes = size_t(depth) * size_t(n - 1) * piece;
+  for (int r = 0; r < n; ++r) {
+    size_t off, len;
+    if (allreduce) {
+      slice_of(d.bytes, n, r, &off, &len);
+    } else {
+      off = size_t(r) * d.bytes;  // source offset of slot r
+      len = d.bytes;
+    }
+    const size_t host = n > 1 ? host_share(len, s.host_ppm, p) : 0;
+    const size_t dst_base = allreduce ? off : 0;
+    const StreamId cl{Strm::Caller, uint8_t(r), 0};
+    const StreamId cs{Strm::Copy, uint8_t(r), 0};
+    const StreamId ps{Strm::Push, uint8_t(r), 0};
+    int peer_index[kMaxRanks];
+    for (int q = 0, j = 0; q < n; ++q) peer_index[q] = q == r ? -1 : j++;
+    // The caller stream touches only this rank's buffers and the scratch.
+    // The pull stream waits for every peer's input; the push stream's
+    // writes into peer outputs are ordered after those waits through the
+    // fold it waits for.
+    for (int q = 0; q < n; ++q)
+      if (q != r) b.touch(cs, q);
+    if (allreduce) b.use(ps);
+    const size_t staged = len - host;
+    int k = 0;
+    for (size_t rel = 0; rel < staged; rel += piece, ++k) {
+      const size_t cb = std::min(piece, staged - rel);
+      const size_t slot = size_t(k % depth) * size_t(n - 1) * piece;
+      const size_t src = off + host + rel;
+      if (n > 1) {
+        if (k >= depth) b.wait(cs, {Ev::Phase, uint8_t(r), 0, uint16_t(2 * (k - depth) + 1)});
+        else if (k == 0) b.wait(cs, {Ev::TempFree, uint8_t(r), 0, 0});
+        for (int q = 0; q < n; ++q)
+          if (q != r) b.ce_copy(cs, temp_at(r, slot + size_t(peer_index[q]) * piece), send_at(q, src), cb);
+        b.record({Ev::Phase, uint8_t(r), 0, uint16_t(2 * k)}, cs);
+        b.wait(cl, {Ev::Phase, uint8_t(r), 0, uint16_t(2 * k)});
+      }
+      Loc srcs[kMaxRanks];
+      for (int q = 0; q < n; ++q)
+        srcs[q] = q == r ? send_at(r, src) : temp_at(r, slot + size_t(peer_index[q]) * piece);
+      const Loc dst = recv_at(r, dst_base + host + rel);
+      b.sm_reduce(cl, srcs, n, &dst, 1, cb);
+      b.record({Ev::Phase, uint8_t(r), 0, uint16_t(2 * k + 1)}, cl);
+      if (allreduce && n > 1) {
+        b.wait(ps, {Ev::Phase, uint8_t(r), 0, uint16_t(2 * k + 1)});
+        for (int q = 0; q < n; ++q)
+          if (q != r) b.ce_copy(ps, recv_at(q, dst_base + host + rel), dst, cb);
+      }
+    }
+    if (n > 1) b.record({Ev::TempFree, uint8_t(r), 0, 0}, cl);
+    b.plan().ce_bytes += staged * size_t(n - 1) * (allreduce ? 2 : 1);
+  }
+  for (int r = 0; r < n; ++r) {
+    size_t off, len;
+    if (allreduce) {
+      slice_of(d.bytes, n, r, &off, &len);
+    } else {
+      off = size_t(r) * d.bytes;
+      len = d.bytes;
+    }
+    const size_t host = n > 1 ? host_share(len, s.host_ppm, p) : 0;
+    if (!host) continue;
+    Loc src[kMaxRanks], dst[kMaxRanks];
+    for (int q = 0; q < n; ++q) src[q] = send_at(q, off);
+    if (allreduce) {
+      for (int q = 0; q < n; ++q) dst[q] = recv_at(q, off);
+      b.host_stage(ranks, src, n, ranks, dst, n, host, true);
+    } else {
+      dst[0] = recv_at(r, 0);
+      b.host_stage(ranks, src, n, &ranks[r], dst, 1, host, true);
+    }
+  }
+  b.join();
+}
+
 // AllGather: rank r pulls every rank's slot into slot q of its output (its
 // own slot too, unless in place). Optional copy-engine and host shares take
 // the middle and the suffix of each peer slot.
@@ -363,9 +461,12 @@ void plan_ag_pull(Builder& b, const CliqueDesc& d, const Shares& s) {
     b.sm_copy({Strm::Caller, uint8_t(r), 0}, dst, src, len, k);
     b.plan().sm_bytes += sm * size_t(n - 1);
     if (ce) {
-      const StreamId cs{Strm::Copy, uint8_t(r), 0};
+      // Peers alternate between the two copy-engine streams so that two
+      // engines pull concurrently.
+      int e = 0;
       for (int q = 0; q < n; ++q) {
         if (q == r) continue;
+        const StreamId cs{(e++ % 2) ? Strm::Push : Strm::Copy, uint8_t(r), 0};
         b.touch(cs, r);
         b.touch(cs, q);
         b.ce_copy(cs, recv_at(r, size_t(q) * slot + sm), send_at(q, sm), ce);
@@ -451,11 +552,19 @@ void plan_bc_scatter(Builder& b, const CliqueDesc& d, const Shares& s) {
   const size_t min_piece = 16 * kMiB;
   int pieces = std::max(1, b.policy().bc_pieces);
   while (pieces > 1 && body / size_t(pieces) < min_piece) --pieces;
+  // With a copy-engine share every byte moves by copy engine: phase 1 on the
+  // Copy stream, phase 2 on the Push stream; otherwise by SM copy kernels on
+  // the caller and aux streams.
+  const bool ce = s.ce_ppm >= 5000;
+  auto phase1 = [&](int r) -> StreamId { return {ce ? Strm::Copy : Strm::Caller, uint8_t(r), 0}; };
+  auto phase2 = [&](int r) -> StreamId { return {ce ? Strm::Push : Strm::Aux, uint8_t(r), 0}; };
+  size_t& moved = ce ? b.plan().ce_bytes : b.plan().sm_bytes;
   if (!d.in_place[root]) {
-    const StreamId as{Strm::Aux, uint8_t(root), 0};
+    const StreamId as = phase2(root);
     b.touch(as, root);
     Loc dst = recv_at(root, 0), src = send_at(root, 0);
-    b.sm_copy(as, &dst, &src, &bytes, 1);
+    if (ce) b.ce_copy(as, dst, src, bytes);
+    else b.sm_copy(as, &dst, &src, &bytes, 1);
   }
   for (int k = 0; k < pieces; ++k) {
     size_t poff, plen;
@@ -464,15 +573,18 @@ void plan_bc_scatter(Builder& b, const CliqueDesc& d, const Shares& s) {
       size_t soff, slen;
       slice_of(plen, m, j, &soff, &slen);
       const int r = nonroot[j];
-      b.touch({Strm::Caller, uint8_t(r), 0}, root);
+      const StreamId s1 = phase1(r);
+      b.touch(s1, root);
+      b.touch(s1, r);
       Loc dst = recv_at(r, poff + soff), src = send_at(root, poff + soff);
-      b.sm_copy({Strm::Caller, uint8_t(r), 0}, &dst, &src, &slen, 1);
-      b.record({Ev::Phase, uint8_t(r), 0, uint16_t(k)}, {Strm::Caller, uint8_t(r), 0});
-      b.plan().sm_bytes += slen;
+      if (ce) b.ce_copy(s1, dst, src, slen);
+      else b.sm_copy(s1, &dst, &src, &slen, 1);
+      b.record({Ev::Phase, uint8_t(r), 0, uint16_t(k)}, s1);
+      moved += slen;
     }
     for (int j = 0; j < m; ++j) {
       const int r = nonroot[j];
-      const StreamId as{Strm::Aux, uint8_t(r), 0};
+      const StreamId as = phase2(r);
       b.touch(as, r);
       Loc dst[kMaxRanks], src[kMaxRanks];
       size_t len[kMaxRanks];
@@ -486,9 +598,12 @@ void plan_bc_scatter(Builder& b, const CliqueDesc& d, const Shares& s) {
         dst[c] = recv_at(r, poff + soff);
         src[c] = recv_at(q, poff + soff);
         len[c++] = slen;
-        b.plan().sm_bytes += slen;
+        moved += slen;
       }
-      b.sm_copy(as, dst, src, len, c);
+      if (ce)
+        for (int i = 0; i < c; ++i) b.ce_copy(as, dst[i], src[i], len[i]);
+      else
+        b.sm_copy(as, dst, src, len, c);
     }
   }
   if (host) {
@@ -529,6 +644,8 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
     case Algo::AgPull: plan_ag_pull(b, d, s); break;
     case Algo::BcPull: plan_bc_pull(b, d, s); break;
     case Algo::BcScatter: plan_bc_scatter(b, d, s); break;
+    case Algo::ArStaged: plan_staged(b, d, s, true); break;
+    case Algo::RsStaged: plan_staged(b, d, s, false); break;
     default: break;
   }
 }

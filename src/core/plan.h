@@ -29,7 +29,9 @@ namespace nb {
 // Logical streams. `dev` is a rank index of the clique. D2H and H2D lanes
 // live on rank `dev`'s GPU; Host(lane) lives on rank 0's GPU and only waits,
 // records and runs the CPU reduction.
-enum class Strm : uint8_t { Caller, Aux, Copy, D2H, H2D, Host, Count };
+// Copy and Push are two copy-engine streams per GPU (pulls and pushes of a
+// staged route run concurrently on different engines).
+enum class Strm : uint8_t { Caller, Aux, Copy, D2H, H2D, Host, Push, Count };
 struct StreamId {
   Strm kind = Strm::Caller;
   uint8_t dev = 0;
@@ -40,7 +42,9 @@ inline bool operator!=(StreamId a, StreamId b) { return !(a == b); }
 
 // Logical events, each recorded on one stream. Done(stream) marks the end of
 // an internal stream's work in this plan (index = stream kind).
-enum class Ev : uint8_t { InputReady, Join, Phase, Done, D2HDone, H2DDone, HostDone, LaneFree, Count };
+// TempFree(dev) marks the end of a staged call's last read of its scratch:
+// the next staged call's first copy into that scratch waits for it.
+enum class Ev : uint8_t { InputReady, Join, Phase, Done, D2HDone, H2DDone, HostDone, LaneFree, TempFree, Count };
 struct EventId {
   Ev kind = Ev::InputReady;
   uint8_t dev = 0;
@@ -52,7 +56,9 @@ bool operator==(EventId a, EventId b);
 // Buffers. Send/Recv are the caller's (per rank); Bounce(dev, lane) is the
 // pinned-host staging buffer a rank's D2H fills; HostOut(lane) holds the
 // host reduction's result.
-enum class Buf : uint8_t { None, Send, Recv, Bounce, HostOut };
+// Temp(dev) is a per-GPU device scratch buffer the staged routes land peer
+// data in.
+enum class Buf : uint8_t { None, Send, Recv, Bounce, HostOut, Temp };
 struct Loc {
   Buf buf = Buf::None;
   uint8_t dev = 0;
@@ -64,6 +70,7 @@ inline Loc send_at(int r, size_t off) { return {Buf::Send, uint8_t(r), 0, off}; 
 inline Loc recv_at(int r, size_t off) { return {Buf::Recv, uint8_t(r), 0, off}; }
 inline Loc bounce_at(int r, int lane) { return {Buf::Bounce, uint8_t(r), uint8_t(lane), 0}; }
 inline Loc hostout_at(int lane) { return {Buf::HostOut, 0, uint8_t(lane), 0}; }
+inline Loc temp_at(int r, size_t off) { return {Buf::Temp, uint8_t(r), 0, off}; }
 
 // Record: event := current position of stream.   Wait: stream waits event.
 // CeCopy: dst[0,bytes) := src[0,bytes) by a copy engine.
@@ -90,6 +97,7 @@ struct Needs {
   size_t bounce_bytes = 0;     // per rank per lane, and per HostOut lane
   uint16_t phase_events = 0;   // Phase(dev, index) indices per rank
   size_t nvls_bytes = 0;       // multicast scratch per GPU
+  size_t temp_bytes = 0;       // device scratch per GPU (staged routes)
   void merge(const Needs& o);
 };
 

@@ -72,9 +72,15 @@ bool is_data(OpKind k) {
          k == OpKind::HostReduce || k == OpKind::NvlsReduce;
 }
 
+// Nodes: the plan's ops [0, m), the NVLS gang node m, then per rank r a
+// virtual "producer" m+1+r (the caller's work before the call on its stream:
+// it wrote rank r's buffers) and "consumer" m+1+N+r (the caller's work after
+// the call: it reads and overwrites them). Races against these make missing
+// InputReady and Join waits visible.
 struct Graph {
-  int nodes = 0;  // ops, plus one gang node at index ops.size() when present
+  int nodes = 0;
   int gang = -1;
+  int producer0 = 0, consumer0 = 0;
   std::vector<std::vector<int>> preds;
   std::vector<int> caller_end;  // per rank: last node on its caller stream
   std::string error;
@@ -83,13 +89,17 @@ struct Graph {
 Graph build_graph(const Plan& plan) {
   Graph g;
   const int m = int(plan.ops.size());
+  const int n = plan.desc.nranks;
   bool has_gang = false;
   for (const PlanOp& op : plan.ops) has_gang |= op.kind == OpKind::NvlsReduce;
-  g.nodes = m + (has_gang ? 1 : 0);
   g.gang = has_gang ? m : -1;
+  g.producer0 = m + 1;
+  g.consumer0 = m + 1 + n;
+  g.nodes = m + 1 + 2 * n;
   g.preds.assign(size_t(g.nodes), {});
   std::map<StreamKey, int> last;
   std::map<EventKey, int> last_record;
+  for (int r = 0; r < n; ++r) last[StreamKey{uint8_t(Strm::Caller), uint8_t(r), 0}] = g.producer0 + r;
   for (int i = 0; i < m; ++i) {
     const PlanOp& op = plan.ops[size_t(i)];
     const auto it = last.find(skey(op.stream));
@@ -107,10 +117,11 @@ Graph build_graph(const Plan& plan) {
     if (op.kind == OpKind::Record) last_record[ekey(op.event)] = i;
     last[skey(op.stream)] = i;
   }
-  g.caller_end.assign(size_t(plan.desc.nranks), -1);
-  for (int r = 0; r < plan.desc.nranks; ++r) {
+  g.caller_end.assign(size_t(n), -1);
+  for (int r = 0; r < n; ++r) {
     const auto it = last.find(StreamKey{uint8_t(Strm::Caller), uint8_t(r), 0});
     if (it != last.end()) g.caller_end[size_t(r)] = it->second;
+    g.preds[size_t(g.consumer0 + r)].push_back(g.caller_end[size_t(r)]);
   }
   return g;
 }
@@ -146,9 +157,11 @@ int arena_of(const Loc& l, int nranks) {
     case Buf::Send: case Buf::Recv: return l.dev;
     case Buf::Bounce: return nranks + int(l.dev) * kMaxLanes + l.lane;
     case Buf::HostOut: return nranks + kMaxRanks * kMaxLanes + l.lane;
+    case Buf::Temp: return nranks + kMaxRanks * kMaxLanes + kMaxLanes + l.dev;
     default: return -1;
   }
 }
+constexpr int kTempArena0 = kMaxRanks * kMaxLanes + kMaxLanes;  // relative to nranks
 size_t offset_of(const Loc& l, const SimLayout& lay) {
   switch (l.buf) {
     case Buf::Send: return lay.send_off[l.dev] + l.off;
@@ -220,6 +233,28 @@ std::string check_plan(const Plan& plan, const SimLayout& lay) {
         break;
       }
   }
+  // The reduction kernels issue 16-byte vector accesses: every reduce operand
+  // must start on a 16-byte boundary of its (16-byte aligned) buffer.
+  for (size_t i = 0; i < plan.ops.size(); ++i) {
+    const PlanOp& op = plan.ops[i];
+    if (op.kind != OpKind::SmReduce) continue;
+    for (int k = 0; k < op.nsrc + op.ndst; ++k) {
+      const Loc& l = k < op.nsrc ? op.src[k] : op.dst[k - op.nsrc];
+      if (l.off % 16 != 0) {
+        std::snprintf(msg, sizeof msg, "op %zu: reduce operand at offset %zu is not 16-byte aligned",
+                      i, l.off);
+        return msg;
+      }
+    }
+  }
+  // The caller's own work before and after the call writes the whole arena
+  // of its rank (send and receive buffers, in-place aliases included).
+  for (int r = 0; r < lay.nranks; ++r)
+    for (int v : {g.producer0 + r, g.consumer0 + r}) {
+      data_index[size_t(v)] = int(data_nodes.size());
+      data_nodes.push_back(v);
+      acc.push_back({Access{r, 0, lay.arena_bytes[r], true}});
+    }
   // Bounds: every access inside its arena (device arenas only; host arenas
   // are sized by the plan's needs).
   for (size_t di = 0; di < acc.size(); ++di)
@@ -233,6 +268,8 @@ std::string check_plan(const Plan& plan, const SimLayout& lay) {
       if (a.arena >= lay.nranks && a.arena < lay.nranks + kMaxRanks * kMaxLanes &&
           a.hi > plan.needs.bounce_bytes)
         return "bounce access beyond the planned bounce size";
+      if (a.arena >= lay.nranks + kTempArena0 && a.hi > plan.needs.temp_bytes)
+        return "scratch access beyond the planned scratch size";
     }
   // Ancestor bitsets over data nodes, in topological order.
   const size_t D = data_nodes.size(), W = (D + 63) / 64;
@@ -260,15 +297,20 @@ std::string check_plan(const Plan& plan, const SimLayout& lay) {
         if (conflict) break;
       }
       if (conflict && !before(a, b) && !before(b, a)) {
-        std::snprintf(msg, sizeof msg, "race: ops %d and %d touch the same bytes unordered",
-                      data_nodes[a], data_nodes[b]);
+        auto name = [&](int v) {
+          if (v >= g.consumer0) return "the caller's later work on rank " + std::to_string(v - g.consumer0);
+          if (v >= g.producer0) return "the caller's earlier work on rank " + std::to_string(v - g.producer0);
+          return "op " + std::to_string(v);
+        };
+        std::snprintf(msg, sizeof msg, "race: %s and %s touch the same bytes unordered",
+                      name(data_nodes[a]).c_str(), name(data_nodes[b]).c_str());
         return msg;
       }
     }
   for (int r = 0; r < plan.desc.nranks; ++r) {
     const int end = g.caller_end[size_t(r)];
     for (size_t a = 0; a < D; ++a) {
-      if (data_nodes[a] == end) continue;
+      if (data_nodes[a] == end || data_nodes[a] >= g.consumer0) continue;
       if (end < 0 || !((anc[size_t(end)][a / 64] >> (a % 64)) & 1)) {
         std::snprintf(msg, sizeof msg, "op %d is not joined into rank %d's caller stream",
                       data_nodes[a], r);
@@ -286,8 +328,9 @@ std::string simulate_plan(const Plan& plan, const SimLayout& lay, const FoldPara
   std::vector<int> order;
   if (!topo_order(g, order, &rng)) return "plan has a dependency cycle";
   const int n = lay.nranks;
-  std::vector<std::vector<uint8_t>> host(size_t(kMaxRanks * kMaxLanes + kMaxLanes));
-  for (auto& h : host) h.assign(plan.needs.bounce_bytes, 0xCD);
+  std::vector<std::vector<uint8_t>> host(size_t(kTempArena0 + kMaxRanks));
+  for (size_t i = 0; i < host.size(); ++i)
+    host[i].assign(i < size_t(kTempArena0) ? plan.needs.bounce_bytes : plan.needs.temp_bytes, 0xCD);
   auto ptr = [&](const Loc& l) -> uint8_t* {
     const int a = arena_of(l, n);
     if (a < n) return arenas[size_t(a)].data() + offset_of(l, lay);

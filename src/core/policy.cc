@@ -58,6 +58,8 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else if (a == "pull" && *kind == Kind::AllGather) *algo = Algo::AgPull;
   else if (a == "pull" && *kind == Kind::Broadcast) *algo = Algo::BcPull;
   else if (a == "scatter" && *kind == Kind::Broadcast) *algo = Algo::BcScatter;
+  else if (a == "staged" && *kind == Kind::AllReduce) *algo = Algo::ArStaged;
+  else if (a == "staged" && *kind == Kind::ReduceScatter) *algo = Algo::RsStaged;
   else return false;
   return true;
 }
@@ -110,7 +112,11 @@ Policy policy_from_env(const EnvLookup& env) {
   if (parse_int(env("NCCL_B200_THREADS"), &i) && (i == 128 || i == 256 || i == 512 || i == 1024))
     p.threads = int(i);
   if (parse_int(env("NCCL_B200_BC_PIECES"), &i) && i >= 1 && i <= 64) p.bc_pieces = int(i);
+  if (parse_size(env("NCCL_B200_STAGE_PIECE"), &z) && z >= 64 * 1024 && z % 16 == 0) p.stage_piece = z;
+  if (parse_int(env("NCCL_B200_STAGE_DEPTH"), &i) && i >= 1 && i <= 8) p.stage_depth = int(i);
   if (parse_bool(env("NCCL_B200_CALIBRATE"), &b)) p.calibrate = b;
+  if (parse_bool(env("NCCL_B200_TUNE"), &b)) p.tune = b;
+  if (parse_size(env("NCCL_B200_TUNE_BYTES"), &z) && z >= kMiB) p.tune_bytes = z;
   if (const char* s = env("NCCL_B200_CALIB_CACHE")) p.calib_cache = s;
   if (parse_int(env("NCCL_B200_TIMEOUT_MS"), &i) && i >= 1) p.device_timeout_ns = uint64_t(i) * 1000000ull;
   const char* summary = env("NCCL_SHIM_SUMMARY");

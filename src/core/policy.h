@@ -42,7 +42,11 @@ struct Policy {
   int blocks_per_sm = 2;
   int threads = 512;
   int bc_pieces = 4;                // scatter/all-gather broadcast pipeline depth
+  size_t stage_piece = 64 * kMiB;   // staged routes: bytes per peer per pipelined piece
+  int stage_depth = 3;              // staged routes: scratch pieces in flight
   bool calibrate = true;            // measure path bandwidths at init
+  bool tune = true;                 // time candidate routes at init, keep the fastest
+  size_t tune_bytes = 256 * kMiB;   // message size the route tuning runs at
   std::string calib_cache;          // JSON cache path ("" = none)
   uint64_t device_timeout_ns = 2000000000ull;  // bound of every in-kernel wait
   bool summary = false;             // NCCL_SHIM_SUMMARY=1 or NCCL_B200_SUMMARY=1

@@ -43,6 +43,8 @@ enum class Algo : uint8_t {
   AgPull,      // rank r pulls every peer's slot into its own output
   BcPull,      // every non-root pulls the root's buffer (2 ranks)
   BcScatter,   // scatter slices from the root, then all-gather them (N ranks)
+  ArStaged,    // copy engines pull slice r into scratch, a local fused fold, CE pushes
+  RsStaged,    // copy engines pull slot r into scratch, a local fused fold
   Count
 };
 

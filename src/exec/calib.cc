@@ -16,8 +16,6 @@ namespace nb {
 
 namespace {
 
-CalibResult g_last;
-
 struct DevBufs {
   int dev = -1;
   void* a = nullptr;  // pulled from by the next device
@@ -34,7 +32,9 @@ bool ok(cudaError_t e) {
   return false;
 }
 
-std::string cache_key(const int* devices, int n) {
+}  // namespace
+
+std::string calib_cache_key(const int* devices, int n) {
   std::ostringstream k;
   int drv = 0;
   cudaDriverGetVersion(&drv);
@@ -54,6 +54,8 @@ std::string cache_key(const int* devices, int n) {
   }
   return k.str();
 }
+
+namespace {
 
 // Time `body` on every device at once: each device's s1 records e0 before,
 // and its streams record e1 (and e3 on s2) after; returns the max elapsed ms.
@@ -90,8 +92,6 @@ float time_all(std::vector<DevBufs>& d, Body body, bool use_s2) {
 }
 
 }  // namespace
-
-const CalibResult& last_calibration() { return g_last; }
 
 CalibResult calibrate(const int* devices, int n, const Policy& p, Summary* summary) {
   CalibResult r;
@@ -215,27 +215,19 @@ CalibResult calibrate(const int* devices, int n, const Policy& p, Summary* summa
   return r;
 }
 
-Shares calibrate_shares(const int* devices, int n, const Policy& p, Summary* s) {
-  const std::string key = cache_key(devices, n);
-  if (!p.calib_cache.empty()) {
-    std::ifstream in(p.calib_cache);
-    if (in) {
-      std::stringstream ss;
-      ss << in.rdbuf();
-      CalibResult c;
-      if (calib_from_json(ss.str(), key, &c)) {
-        g_last = c;
-        if (s) s->note("calibration loaded from cache");
-        return shares_from(c, Algo::ArTwoShot, n);
-      }
-    }
-  }
-  g_last = calibrate(devices, n, p, s);
-  if (g_last.valid && !p.calib_cache.empty()) {
-    std::ofstream out(p.calib_cache);
-    if (out) out << calib_to_json(g_last, key);
-  }
-  return shares_from(g_last, Algo::ArTwoShot, n);
+bool calib_load(const std::string& path, const std::string& key, CalibResult* out) {
+  if (path.empty()) return false;
+  std::ifstream in(path);
+  if (!in) return false;
+  std::stringstream ss;
+  ss << in.rdbuf();
+  return calib_from_json(ss.str(), key, out);
+}
+
+void calib_save(const std::string& path, const std::string& key, const CalibResult& c) {
+  if (path.empty() || !c.valid) return;
+  std::ofstream out(path);
+  if (out) out << calib_to_json(c, key);
 }
 
 }  // namespace nb

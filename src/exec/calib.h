@@ -2,9 +2,11 @@
 // once, the SM-driven NVLink pull bandwidth, the copy-engine peer-copy
 // bandwidth (alone and alongside SM pulls), the pinned-host PCIe bandwidth
 // (D2H and H2D, every GPU concurrently) and the CPU fold throughput. Results
-// are optionally cached in a JSON file keyed by GPU UUIDs, driver and NCCL
-// versions (NCCL_B200_CALIB_CACHE).
+// (with the route tuning of abi/tune.cc) are optionally cached in a JSON
+// file keyed by GPU UUIDs and driver version (NCCL_B200_CALIB_CACHE).
 #pragma once
+
+#include <string>
 
 #include "core/calib_model.h"
 #include "core/policy.h"
@@ -13,8 +15,8 @@
 namespace nb {
 
 CalibResult calibrate(const int* devices, int n, const Policy& p, Summary* s);
-const CalibResult& last_calibration();
-// Calibrate (or load the cache) and return the AllReduce shares.
-Shares calibrate_shares(const int* devices, int n, const Policy& p, Summary* s);
+std::string calib_cache_key(const int* devices, int n);
+bool calib_load(const std::string& path, const std::string& key, CalibResult* out);
+void calib_save(const std::string& path, const std::string& key, const CalibResult& c);
 
 }  // namespace nb

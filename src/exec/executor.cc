@@ -77,8 +77,8 @@ bool Executor::ensure_device(int dev, std::string* why) {
     return false;
   }
   r.sm_count = sms;
-  bool ok = make_stream(r.aux) && make_stream(r.copy) && make_event(r.input_ready) &&
-            make_event(r.join);
+  bool ok = make_stream(r.aux) && make_stream(r.copy) && make_stream(r.push) &&
+            make_event(r.input_ready) && make_event(r.join) && make_event(r.temp_free);
   for (int l = 0; ok && l < kMaxLanes; ++l)
     ok = make_stream(r.d2h[l]) && make_stream(r.h2d[l]) && make_event(r.d2h_done[l]) &&
          make_event(r.h2d_done[l]);
@@ -208,6 +208,24 @@ bool Executor::ensure(const Needs& needs, const int* devices, int n, std::string
       }
       r.phase.push_back(e);
     }
+    if (needs.temp_bytes > r.temp_bytes) {
+      // Growing the scratch first drains this device (work may still read it).
+      if (r.temp && (cudaDeviceSynchronize() != cudaSuccess || cudaFree(r.temp) != cudaSuccess)) {
+        cudaGetLastError();
+        if (why) *why = "scratch release failed";
+        return false;
+      }
+      r.temp = nullptr;
+      r.temp_bytes = 0;
+      void* p = nullptr;
+      if (cudaMalloc(&p, needs.temp_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        if (why) *why = "scratch allocation failed";
+        return false;
+      }
+      r.temp = p;
+      r.temp_bytes = needs.temp_bytes;
+    }
   }
   if (needs.lanes > 0 && !ensure_lanes(devices[0], needs.lanes, needs.bounce_bytes, devices, n, why))
     return false;
@@ -222,6 +240,7 @@ cudaStream_t Executor::bind_stream(StreamId s, const Binding& b) {
   switch (s.kind) {
     case Strm::Aux: return r.aux;
     case Strm::Copy: return r.copy;
+    case Strm::Push: return r.push;
     case Strm::D2H: return r.d2h[s.lane];
     case Strm::H2D: return r.h2d[s.lane];
     default: return nullptr;
@@ -242,6 +261,7 @@ cudaEvent_t Executor::bind_event(EventId e, const Binding& b) {
   switch (e.kind) {
     case Ev::InputReady: return r.input_ready;
     case Ev::Join: return r.join;
+    case Ev::TempFree: return r.temp_free;
     case Ev::Phase: return e.index < r.phase.size() ? r.phase[e.index] : nullptr;
     case Ev::Done: return r.done[e.index][e.lane];
     case Ev::D2HDone: return r.d2h_done[e.lane];
@@ -256,6 +276,7 @@ char* Executor::bind_loc(const Loc& l, const Binding& b) {
     case Buf::Recv: return static_cast<char*>(b.recv[l.dev]) + l.off;
     case Buf::Bounce: return static_cast<char*>(device(b.device[l.dev])->bounce[l.lane]) + l.off;
     case Buf::HostOut: return static_cast<char*>(lanes_.out[l.lane]) + l.off;
+    case Buf::Temp: return static_cast<char*>(device(b.device[l.dev])->temp) + l.off;
     default: return nullptr;
   }
 }

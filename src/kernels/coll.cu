@@ -305,6 +305,12 @@ cudaError_t launch_reduce(const ReduceLaunch& r, LaunchShape shape, cudaStream_t
   const ReduceFn fn = pick_reduce(r.fold.dtype, r.nsrc);
   if (!fn) return cudaErrorInvalidValue;
   if (r.bytes == 0) return cudaSuccess;
+  // The kernel issues 16-byte vector accesses: refuse (never launch) any
+  // operand that is not 16-byte aligned.
+  for (int i = 0; i < r.nsrc; ++i)
+    if (reinterpret_cast<uintptr_t>(r.src[i]) % 16) return cudaErrorMisalignedAddress;
+  for (int i = 0; i < r.ndst; ++i)
+    if (reinterpret_cast<uintptr_t>(r.dst[i]) % 16) return cudaErrorMisalignedAddress;
   KReduceArgs k{};
   for (int i = 0; i < r.nsrc; ++i) {
     k.src[i] = r.src[i];
