@@ -166,9 +166,14 @@ void prewarm(const int* devices, int n) {
   const bool nvls = r.policy.nvls != NvlsMode::Off && nvls_supported(devices, n);
   Needs needs = prewarm_needs(n, r.policy, s, nvls);
   // Scratch of the staged routes, sized for the tuned choice.
-  if (n > 1 && (r.calib[n].preferred[0] == int(Algo::ArStaged) ||
-                r.calib[n].preferred[2] == int(Algo::RsStaged)))
-    needs.temp_bytes = size_t(r.policy.stage_depth) * size_t(n - 1) * r.policy.stage_piece;
+  for (int k : {int(Kind::AllReduce), int(Kind::ReduceScatter)}) {
+    const CalibResult& c = r.calib[n];
+    if (n < 2 || (c.preferred[k] != int(Algo::ArStaged) && c.preferred[k] != int(Algo::RsStaged)))
+      continue;
+    const size_t piece = c.stage_piece_mib[k] > 0 ? size_t(c.stage_piece_mib[k]) << 20 : r.policy.stage_piece;
+    const int depth = c.stage_depth[k] > 0 ? c.stage_depth[k] : r.policy.stage_depth;
+    needs.temp_bytes = std::max(needs.temp_bytes, size_t(depth) * size_t(n - 1) * piece);
+  }
   if (!r.exec.ensure(needs, devices, n, &why)) {
     cudaGetLastError();
     if (r.summary.enabled()) r.summary.note("prewarm_failed " + why);

@@ -21,22 +21,50 @@ namespace {
 struct Candidate {
   Algo algo;
   int ce_ppm;
+  int host_ppm;
+  int piece_mib;  // staged routes
+  int depth;
 };
 
-std::vector<Candidate> candidates(Kind k, int n, bool nvls) {
+// Every candidate route of a kind; a host-lane variant is added wherever the
+// rate model (measured PCIe, NVLink and fold rates) predicts a host share.
+std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& rates) {
+  std::vector<Candidate> v;
+  auto add = [&](Algo a, int ce, int piece = 0, int depth = 0) {
+    v.push_back({a, ce, 0, piece, depth});
+    const int host = shares_from(rates, a, n).host_ppm;
+    if (host > 0) v.push_back({a, ce, host, piece, depth});
+  };
   switch (k) {
-    case Kind::AllReduce: {
-      std::vector<Candidate> v{{Algo::ArTwoShot, 0}, {Algo::ArStaged, 0}};
-      if (nvls && n >= 2) v.push_back({Algo::ArNvls, 0});
-      return v;
-    }
-    case Kind::ReduceScatter: return {{Algo::RsPull, 0}, {Algo::RsStaged, 0}};
-    case Kind::AllGather: return {{Algo::AgPull, 0}, {Algo::AgPull, 10000}};
+    case Kind::AllReduce:
+      add(Algo::ArTwoShot, 0);
+      add(Algo::ArStaged, 0, 64, 3);
+      add(Algo::ArStaged, 0, 128, 2);
+      add(Algo::ArStaged, 0, 256, 2);
+      if (nvls && n >= 2) v.push_back({Algo::ArNvls, 0, 0, 0, 0});
+      break;
+    case Kind::ReduceScatter:
+      add(Algo::RsPull, 0);
+      add(Algo::RsStaged, 0, 64, 3);
+      add(Algo::RsStaged, 0, 128, 2);
+      add(Algo::RsStaged, 0, 256, 2);
+      break;
+    case Kind::AllGather:
+      add(Algo::AgPull, 0);
+      add(Algo::AgPull, 10000);
+      break;
     case Kind::Broadcast:
-      if (n >= 3) return {{Algo::BcScatter, 0}, {Algo::BcScatter, 10000}, {Algo::BcPull, 10000}};
-      return {{Algo::BcPull, 0}, {Algo::BcPull, 10000}};
-    default: return {};
+      if (n >= 3) {
+        add(Algo::BcScatter, 0);
+        add(Algo::BcScatter, 10000);
+      }
+      add(Algo::BcPull, 0);
+      add(Algo::BcPull, 10000);
+      break;
+    default:
+      break;
   }
+  return v;
 }
 
 double busbw_factor(Kind k, int n) {
@@ -86,10 +114,13 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
       b.recv[i] = recv[size_t(i)];
     }
     double best_ms = 1e30;
-    Candidate best{Algo::Fallback, -1};
-    for (const Candidate& c : candidates(kind, n, nvls)) {
+    Candidate best{Algo::Fallback, -1, -1, 0, 0};
+    for (const Candidate& c : candidates(kind, n, nvls, *out)) {
       Shares s;
       s.ce_ppm = c.ce_ppm;
+      s.host_ppm = c.host_ppm;
+      s.stage_piece = size_t(c.piece_mib) << 20;
+      s.stage_depth = c.depth;
       Plan plan;
       build_plan(c.algo, d, r.policy, s, plan);
       std::string why;
@@ -130,9 +161,10 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
       }
       char line[160];
       const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? bytes : d.bytes;
-      std::snprintf(line, sizeof line, "tune %s n=%d %s ce_ppm=%d busbw_gbs=%.1f",
-                    kind_name(kind), n, algo_name(c.algo), c.ce_ppm,
-                    logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
+      std::snprintf(line, sizeof line,
+                    "tune %s n=%d %s ce_ppm=%d host_ppm=%d piece_mib=%d depth=%d busbw_gbs=%.1f",
+                    kind_name(kind), n, algo_name(c.algo), c.ce_ppm, c.host_ppm, c.piece_mib,
+                    c.depth, logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
       r.summary.note(line);
       if (ms < best_ms) {
         best_ms = ms;
@@ -142,6 +174,9 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
     if (best.algo != Algo::Fallback) {
       out->preferred[kk] = int(best.algo);
       out->ce_ppm[kk] = best.ce_ppm;
+      out->host_ppm[kk] = best.host_ppm;
+      out->stage_piece_mib[kk] = best.piece_mib;
+      out->stage_depth[kk] = best.depth;
       const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? bytes : d.bytes;
       out->route_gbs[kk] = logical / (best_ms * 1e-3) / 1e9 * busbw_factor(kind, n);
     }

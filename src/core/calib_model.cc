@@ -44,9 +44,14 @@ Shares shares_from(const CalibResult& c, Algo a, int n) {
                        a == Algo::BcScatter;
   if (ce_algo && c.nvlink_mix_gbs > 1.03 * bnv && c.mix_ce_fraction > 0)
     s.ce_ppm = int(std::min(0.5, c.mix_ce_fraction) * 10000.0);
-  // A measured route choice overrides the model's copy-engine share.
-  for (int k = 0; k < 4; ++k)
-    if (c.preferred[k] == int(a) && c.ce_ppm[k] >= 0) s.ce_ppm = c.ce_ppm[k];
+  // A measured route choice overrides the model for that route.
+  for (int k = 0; k < 4; ++k) {
+    if (c.preferred[k] != int(a)) continue;
+    if (c.ce_ppm[k] >= 0) s.ce_ppm = c.ce_ppm[k];
+    if (c.host_ppm[k] >= 0) s.host_ppm = c.host_ppm[k];
+    if (c.stage_piece_mib[k] > 0) s.stage_piece = size_t(c.stage_piece_mib[k]) << 20;
+    if (c.stage_depth[k] > 0) s.stage_depth = c.stage_depth[k];
+  }
   return s;
 }
 
@@ -55,13 +60,18 @@ std::string calib_to_json(const CalibResult& c, const std::string& key) {
   std::snprintf(buf, sizeof buf,
                 "{\"key\": \"%s\", \"nvlink_sm_gbs\": %.3f, \"nvlink_ce_gbs\": %.3f, "
                 "\"nvlink_mix_gbs\": %.3f, \"mix_ce_fraction\": %.5f, \"pcie_d2h_gbs\": %.3f, "
-                "\"pcie_h2d_gbs\": %.3f, \"fold_gbs\": %.3f, "
-                "\"pref0\": %d, \"pref1\": %d, \"pref2\": %d, \"pref3\": %d, "
-                "\"ce0\": %d, \"ce1\": %d, \"ce2\": %d, \"ce3\": %d}\n",
+                "\"pcie_h2d_gbs\": %.3f, \"fold_gbs\": %.3f",
                 key.c_str(), c.nvlink_sm_gbs, c.nvlink_ce_gbs, c.nvlink_mix_gbs, c.mix_ce_fraction,
-                c.pcie_d2h_gbs, c.pcie_h2d_gbs, c.fold_gbs, c.preferred[0], c.preferred[1],
-                c.preferred[2], c.preferred[3], c.ce_ppm[0], c.ce_ppm[1], c.ce_ppm[2], c.ce_ppm[3]);
-  return buf;
+                c.pcie_d2h_gbs, c.pcie_h2d_gbs, c.fold_gbs);
+  std::string s = buf;
+  for (int k = 0; k < 4; ++k) {
+    std::snprintf(buf, sizeof buf,
+                  ", \"pref%d\": %d, \"ce%d\": %d, \"host%d\": %d, \"piece%d\": %d, \"depth%d\": %d",
+                  k, c.preferred[k], k, c.ce_ppm[k], k, c.host_ppm[k], k, c.stage_piece_mib[k], k,
+                  c.stage_depth[k]);
+    s += buf;
+  }
+  return s + "}\n";
 }
 
 static bool json_number(const std::string& text, const char* name, double* out) {
@@ -90,9 +100,12 @@ bool calib_from_json(const std::string& text, const std::string& key, CalibResul
   if (!ok) return false;
   for (int k = 0; k < 4; ++k) {
     double v = 0;
-    const std::string pn = "pref" + std::to_string(k), cn = "ce" + std::to_string(k);
-    if (json_number(text, pn.c_str(), &v)) c.preferred[k] = int(v);
-    if (json_number(text, cn.c_str(), &v)) c.ce_ppm[k] = int(v);
+    const std::string K = std::to_string(k);
+    if (json_number(text, ("pref" + K).c_str(), &v)) c.preferred[k] = int(v);
+    if (json_number(text, ("ce" + K).c_str(), &v)) c.ce_ppm[k] = int(v);
+    if (json_number(text, ("host" + K).c_str(), &v)) c.host_ppm[k] = int(v);
+    if (json_number(text, ("piece" + K).c_str(), &v)) c.stage_piece_mib[k] = int(v);
+    if (json_number(text, ("depth" + K).c_str(), &v)) c.stage_depth[k] = int(v);
   }
   c.valid = true;
   *out = c;

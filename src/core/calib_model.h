@@ -32,6 +32,9 @@ struct CalibResult {
   // its copy-engine share (parts per 10000), -1 / Fallback when untuned.
   int preferred[4] = {0, 0, 0, 0};
   int ce_ppm[4] = {-1, -1, -1, -1};
+  int host_ppm[4] = {-1, -1, -1, -1};
+  int stage_piece_mib[4] = {0, 0, 0, 0};
+  int stage_depth[4] = {0, 0, 0, 0};
   double route_gbs[4] = {0, 0, 0, 0};  // busbw of the chosen route at the tuning size
 };
 

@@ -356,8 +356,8 @@ void plan_staged(Builder& b, const CliqueDesc& d, const Shares& s, bool allreduc
   const int n = b.n();
   b.prologue();
   const Policy& p = b.policy();
-  const size_t piece = p.stage_piece;
-  const int depth = p.stage_depth;
+  const size_t piece = s.stage_piece ? s.stage_piece : p.stage_piece;
+  const int depth = s.stage_depth ? s.stage_depth : p.stage_depth;
   int ranks[kMaxRanks];
   all_ranks(n, ranks);
   if (n > 1) b.plan().needs.temp_bytes = size_t(depth) * size_t(n - 1) * piece;

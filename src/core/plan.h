@@ -102,9 +102,12 @@ struct Needs {
 };
 
 // Per-path shares in parts per 10000 of the bytes a rank receives.
+// Staged routes also take their pipeline shape from here (0 = policy default).
 struct Shares {
   int host_ppm = 0;
   int ce_ppm = 0;
+  size_t stage_piece = 0;
+  int stage_depth = 0;
 };
 
 struct Plan {

@@ -36,17 +36,17 @@ struct Policy {
   int ce_share_ppm = -1;            // copy-engine peer copies (pure-copy shares)
   int lanes = 4;                    // reusable pinned-host lanes per GPU
   size_t host_piece = 16 * kMiB;    // host-lane staging piece (16-byte multiple)
-  size_t min_host_bytes = 64 * kMiB;  // below this per GPU, no host share
+  size_t min_host_bytes = 16 * kMiB;  // below this per GPU, no host share
   int host_threads = 8;             // CPU threads of the host reduction
   size_t sm_chunk = 512 * kMiB;     // pipelining piece of the SM share
   int blocks_per_sm = 2;
   int threads = 512;
   int bc_pieces = 4;                // scatter/all-gather broadcast pipeline depth
-  size_t stage_piece = 64 * kMiB;   // staged routes: bytes per peer per pipelined piece
-  int stage_depth = 3;              // staged routes: scratch pieces in flight
+  size_t stage_piece = 128 * kMiB;  // staged routes: bytes per peer per pipelined piece
+  int stage_depth = 2;              // staged routes: scratch pieces in flight
   bool calibrate = true;            // measure path bandwidths at init
   bool tune = true;                 // time candidate routes at init, keep the fastest
-  size_t tune_bytes = 256 * kMiB;   // message size the route tuning runs at
+  size_t tune_bytes = 2 * kGiB;     // message size the route tuning runs at
   std::string calib_cache;          // JSON cache path ("" = none)
   uint64_t device_timeout_ns = 2000000000ull;  // bound of every in-kernel wait
   bool summary = false;             // NCCL_SHIM_SUMMARY=1 or NCCL_B200_SUMMARY=1
