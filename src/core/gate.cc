@@ -67,6 +67,7 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
     case Algo::BcScatter: return k == Kind::Broadcast && nranks >= 3;
     case Algo::ArStaged: return k == Kind::AllReduce;
     case Algo::RsStaged: return k == Kind::ReduceScatter;
+    case Algo::BcChain: return k == Kind::Broadcast;
     default: return false;
   }
 }

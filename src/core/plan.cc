@@ -392,8 +392,12 @@ void plan_staged(Builder& b, const CliqueDesc& d, const Shares& s, bool allreduc
       if (n > 1) {
         if (k >= depth) b.wait(cs, {Ev::Phase, uint8_t(r), 0, uint16_t(2 * (k - depth) + 1)});
         else if (k == 0) b.wait(cs, {Ev::TempFree, uint8_t(r), 0, 0});
-        for (int q = 0; q < n; ++q)
-          if (q != r) b.ce_copy(cs, temp_at(r, slot + size_t(peer_index[q]) * piece), send_at(q, src), cb);
+        // Peers in rotated order (r+1, r+2, ...): at any moment every rank
+        // pulls from a different peer.
+        for (int i = 1; i < n; ++i) {
+          const int q = (r + i) % n;
+          b.ce_copy(cs, temp_at(r, slot + size_t(peer_index[q]) * piece), send_at(q, src), cb);
+        }
         b.record({Ev::Phase, uint8_t(r), 0, uint16_t(2 * k)}, cs);
         b.wait(cl, {Ev::Phase, uint8_t(r), 0, uint16_t(2 * k)});
       }
@@ -405,8 +409,8 @@ void plan_staged(Builder& b, const CliqueDesc& d, const Shares& s, bool allreduc
       b.record({Ev::Phase, uint8_t(r), 0, uint16_t(2 * k + 1)}, cl);
       if (allreduce && n > 1) {
         b.wait(ps, {Ev::Phase, uint8_t(r), 0, uint16_t(2 * k + 1)});
-        for (int q = 0; q < n; ++q)
-          if (q != r) b.ce_copy(ps, recv_at(q, dst_base + host + rel), dst, cb);
+        for (int i = 1; i < n; ++i)
+          b.ce_copy(ps, recv_at((r + i) % n, dst_base + host + rel), dst, cb);
       }
     }
     if (n > 1) b.record({Ev::TempFree, uint8_t(r), 0, 0}, cl);
@@ -461,12 +465,12 @@ void plan_ag_pull(Builder& b, const CliqueDesc& d, const Shares& s) {
     b.sm_copy({Strm::Caller, uint8_t(r), 0}, dst, src, len, k);
     b.plan().sm_bytes += sm * size_t(n - 1);
     if (ce) {
-      // Peers alternate between the two copy-engine streams so that two
-      // engines pull concurrently.
-      int e = 0;
-      for (int q = 0; q < n; ++q) {
-        if (q == r) continue;
-        const StreamId cs{(e++ % 2) ? Strm::Push : Strm::Copy, uint8_t(r), 0};
+      // Peers in rotated order (r+1, r+2, ...), alternating between the two
+      // copy-engine streams: two engines pull concurrently and, at any
+      // moment, no peer serves more than two ranks.
+      for (int i = 1; i < n; ++i) {
+        const int q = (r + i) % n;
+        const StreamId cs{(i % 2) ? Strm::Copy : Strm::Push, uint8_t(r), 0};
         b.touch(cs, r);
         b.touch(cs, q);
         b.ce_copy(cs, recv_at(r, size_t(q) * slot + sm), send_at(q, sm), ce);
@@ -589,8 +593,8 @@ void plan_bc_scatter(Builder& b, const CliqueDesc& d, const Shares& s) {
       Loc dst[kMaxRanks], src[kMaxRanks];
       size_t len[kMaxRanks];
       int c = 0;
-      for (int i = 0; i < m; ++i) {
-        if (i == j) continue;
+      for (int t = 1; t < m; ++t) {  // rotated: non-root j reads j+1, j+2, ...
+        const int i = (j + t) % m;
         const int q = nonroot[i];
         b.wait(as, {Ev::Phase, uint8_t(q), 0, uint16_t(k)});
         size_t soff, slen;
@@ -610,6 +614,63 @@ void plan_bc_scatter(Builder& b, const CliqueDesc& d, const Shares& s) {
     Loc dsts[kMaxRanks];
     for (int j = 0; j < m; ++j) dsts[j] = recv_at(nonroot[j], body);
     Loc src = send_at(root, body);
+    b.host_stage(&root, &src, 1, nonroot, dsts, m, host, false);
+  }
+  b.join();
+}
+
+// Broadcast by a pipelined chain over the ranks root, root+1, ..., root+n-1.
+// The buffer is cut into pieces; hop h (1..n-1) pulls piece k from hop h-1
+// (the root's send buffer for h = 1, else the predecessor's output) once the
+// predecessor holds it. Every rank receives each byte once and forwards it
+// once, so every link carries the buffer once per direction and the hops of
+// different pieces overlap; the time is about (pieces + n - 2) piece times.
+// Data moves by copy engine (ce share >= 50 %) or by SM copy kernels.
+void plan_bc_chain(Builder& b, const CliqueDesc& d, const Shares& s) {
+  const int n = b.n();
+  const int root = d.root;
+  b.prologue();
+  const Policy& p = b.policy();
+  const size_t bytes = d.bytes;
+  const size_t host = n > 1 ? host_share(bytes, s.host_ppm, p) : 0;
+  const size_t body = bytes - host;
+  const size_t piece = s.stage_piece ? s.stage_piece : p.stage_piece;
+  const bool ce = s.ce_ppm >= 5000;
+  size_t& moved = ce ? b.plan().ce_bytes : b.plan().sm_bytes;
+  if (!d.in_place[root]) {
+    const StreamId as{ce ? Strm::Push : Strm::Aux, uint8_t(root), 0};
+    b.touch(as, root);
+    const Loc dst = recv_at(root, 0), src = send_at(root, 0);
+    if (ce) b.ce_copy(as, dst, src, bytes);
+    else b.sm_copy(as, &dst, &src, &bytes, 1);
+  }
+  int k = 0;
+  for (size_t off = 0; off < body; off += piece, ++k) {
+    const size_t cb = std::min(piece, body - off);
+    for (int h = 1; h < n; ++h) {
+      const int r = (root + h) % n, pred = (root + h - 1) % n;
+      const StreamId s1{ce ? Strm::Copy : Strm::Caller, uint8_t(r), 0};
+      b.touch(s1, r);
+      b.touch(s1, pred);
+      if (h > 1) b.wait(s1, {Ev::Phase, uint8_t(pred), 0, uint16_t(k)});
+      const Loc src = h == 1 ? send_at(root, off) : recv_at(pred, off);
+      const Loc dst = recv_at(r, off);
+      if (ce) b.ce_copy(s1, dst, src, cb);
+      else b.sm_copy(s1, &dst, &src, &cb, 1);
+      b.record({Ev::Phase, uint8_t(r), 0, uint16_t(k)}, s1);
+      moved += cb;
+    }
+  }
+  if (host) {
+    int nonroot[kMaxRanks];
+    Loc dsts[kMaxRanks];
+    int m = 0;
+    for (int r = 0; r < n; ++r)
+      if (r != root) {
+        nonroot[m] = r;
+        dsts[m++] = recv_at(r, body);
+      }
+    const Loc src = send_at(root, body);
     b.host_stage(&root, &src, 1, nonroot, dsts, m, host, false);
   }
   b.join();
@@ -646,6 +707,7 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
     case Algo::BcScatter: plan_bc_scatter(b, d, s); break;
     case Algo::ArStaged: plan_staged(b, d, s, true); break;
     case Algo::RsStaged: plan_staged(b, d, s, false); break;
+    case Algo::BcChain: plan_bc_chain(b, d, s); break;
     default: break;
   }
 }

@@ -60,6 +60,7 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else if (a == "scatter" && *kind == Kind::Broadcast) *algo = Algo::BcScatter;
   else if (a == "staged" && *kind == Kind::AllReduce) *algo = Algo::ArStaged;
   else if (a == "staged" && *kind == Kind::ReduceScatter) *algo = Algo::RsStaged;
+  else if (a == "chain" && *kind == Kind::Broadcast) *algo = Algo::BcChain;
   else return false;
   return true;
 }

@@ -45,6 +45,7 @@ enum class Algo : uint8_t {
   BcScatter,   // scatter slices from the root, then all-gather them (N ranks)
   ArStaged,    // copy engines pull slice r into scratch, a local fused fold, CE pushes
   RsStaged,    // copy engines pull slot r into scratch, a local fused fold
+  BcChain,     // pipelined chain: each rank pulls every piece from its predecessor
   Count
 };
 

@@ -215,12 +215,19 @@ __global__ void __launch_bounds__(512, 2) reduce_kernel(const __grid_constant__ 
   }
 }
 
+// Tiles are interleaved across segments (tile t belongs to segment t % nseg)
+// so that at any moment every source is being read: pulls from several peers
+// spread over all their links instead of queueing on one peer at a time.
 __global__ void __launch_bounds__(512) copy_kernel(const __grid_constant__ KCopyArgs a) {
-  const unsigned long long tiles = a.tile_start[a.nseg];
+  unsigned long long rounds = 0;
+  for (int i = 0; i < a.nseg; ++i)
+    rounds = max(rounds, a.tile_start[i + 1] - a.tile_start[i]);
+  const unsigned long long tiles = rounds * (unsigned long long)a.nseg;
   for (unsigned long long t = blockIdx.x; t < tiles; t += gridDim.x) {
-    int s = 0;
-    while (s + 1 < a.nseg && t >= a.tile_start[s + 1]) ++s;
-    const unsigned long long lo = (t - a.tile_start[s]) * kTileBytes;
+    const int s = int(t % (unsigned long long)a.nseg);
+    const unsigned long long round = t / (unsigned long long)a.nseg;
+    if (round >= a.tile_start[s + 1] - a.tile_start[s]) continue;
+    const unsigned long long lo = round * kTileBytes;
     const unsigned long long hi = min(lo + (unsigned long long)kTileBytes, a.len[s]);
     const char* src = static_cast<const char*>(a.src[s]) + lo;
     char* dst = static_cast<char*>(a.dst[s]) + lo;

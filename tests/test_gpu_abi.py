@@ -16,8 +16,7 @@ from conftest import REPO, gpu_count, need_gpus
 
 pytestmark = pytest.mark.gpu
 
-ALGO = {"fallback": 0, "ar_twoshot": 1, "ar_nvls": 2, "rs_pull": 3, "ag_pull": 4, "bc_pull": 5,
-        "bc_scatter": 6}
+from scc26_nccl_shim_b200._core import ALGO  # noqa: E402
 
 
 @pytest.fixture(scope="module")
@@ -129,7 +128,8 @@ def test_multi_gpu_collectives(nc, n):
         before = sum(nc.custom_calls(a) for a in ALGO.values() if a)
         run_kind(nc, kind, comms, devs, c, root=n - 1)
         run_kind(nc, kind, comms, devs, c, inplace=True)
-        assert sum(nc.custom_calls(a) for a in ALGO.values() if a) >= before + 2, kind
+        assert sum(nc.custom_calls(a) for a in ALGO.values() if a) >= before + 2, \
+            (kind, nc.summary_text())
     run_kind(nc, "allreduce", comms, devs, count, dtype=torch.bfloat16)
     run_kind(nc, "allreduce", comms, devs, count, op="avg")
     for c in comms:

@@ -138,7 +138,7 @@ def test_copy_segments_alignment():
 
 CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", "allgather"),
          ("bc_pull", "broadcast"), ("bc_scatter", "broadcast"), ("ar_staged", "allreduce"),
-         ("rs_staged", "reducescatter")]
+         ("rs_staged", "reducescatter"), ("bc_chain", "broadcast")]
 
 
 @pytest.mark.parametrize("algo,kind", CASES)
@@ -169,7 +169,8 @@ def test_virtual_rank_plans(algo, kind, n, inplace):
         recvs = sends if inplace else [torch.empty(count, device="cuda:0") for _ in range(n)]
     inputs = [s.clone() for s in sends]
     root = n - 1
-    ce = 3000 if algo in ("ar_twoshot", "ag_pull", "bc_pull") else (10000 if algo == "bc_scatter" else 0)
+    ce = 3000 if algo in ("ar_twoshot", "ag_pull", "bc_pull") else \
+        (10000 if algo in ("bc_scatter", "bc_chain") else 0)
     emu.plan(algo, kind, sends, recvs, root=root, ce_ppm=ce)
     torch.cuda.synchronize()
     for r in range(n):
