@@ -317,6 +317,7 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
   const ExecStatus status = r.exec.execute(plan, b, &error, &r.fault);
   if (status == ExecStatus::Failed) {
     r.poisoned = true;
+    if (error == cudaErrorLaunchTimeout) r.summary.count_timeout();  // a bounded wait ran out
     std::fprintf(stderr,
                  "[nccl-b200] %s: CUDA error after custom work was enqueued (%s); returning "
                  "ncclUnhandledCudaError, custom paths disabled for this process\n",
@@ -703,6 +704,9 @@ size_t nb_summary_text(char* buf, size_t cap) {
   }
   return all.size();
 }
+int nb_nvls_supported(const int* devices, int n) { return nvls_supported(devices, n) ? 1 : 0; }
+unsigned nb_nvls_status(const int* devices, int n) { return nvls_status(devices, n); }
+
 // The tuned route of a collective kind on cliques of n ranks (-1 untuned).
 int nb_route(int n, int kind) {
   if (n < 1 || n > kMaxRanks || kind < 0 || kind >= int(Kind::Count) || !rt().calib[n].valid) return -1;

@@ -125,7 +125,9 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
   }
   if (s.capturing) return fallback(Reason::Capturing);
   if (p.first_pass && !s.first_pass_done) return fallback(Reason::FirstPass);
-  const Algo algo = choose_algo(a, n, s.nvls_available, p, s.preferred[size_t(a.kind)]);
+  Algo algo = choose_algo(a, n, s.nvls_available, p, s.preferred[size_t(a.kind)]);
+  // The multimem kernel moves whole 16-byte vectors only.
+  if (algo == Algo::ArNvls && call_bytes(a) % 16 != 0) algo = Algo::ArTwoShot;
   if (algo == Algo::Fallback) return fallback(Reason::PolicyFallback);
   return {algo, Reason::None};
 }

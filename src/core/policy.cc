@@ -120,6 +120,7 @@ Policy policy_from_env(const EnvLookup& env) {
   if (parse_size(env("NCCL_B200_TUNE_BYTES"), &z) && z >= kMiB) p.tune_bytes = z;
   if (const char* s = env("NCCL_B200_CALIB_CACHE")) p.calib_cache = s;
   if (parse_int(env("NCCL_B200_TIMEOUT_MS"), &i) && i >= 1) p.device_timeout_ns = uint64_t(i) * 1000000ull;
+  if (parse_int(env("NCCL_B200_TEST_NVLS_SKEW"), &i) && i >= 0) p.test_nvls_skew = unsigned(i);
   const char* summary = env("NCCL_SHIM_SUMMARY");
   if (summary && !std::strcmp(summary, "1")) p.summary = true;
   if (parse_bool(env("NCCL_B200_SUMMARY"), &b)) p.summary = b;

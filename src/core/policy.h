@@ -49,6 +49,9 @@ struct Policy {
   size_t tune_bytes = 2 * kGiB;     // message size the route tuning runs at
   std::string calib_cache;          // JSON cache path ("" = none)
   uint64_t device_timeout_ns = 2000000000ull;  // bound of every in-kernel wait
+  // Test hook: raise the NVLS barrier targets so that no arrival can meet
+  // them; every wait then runs out (bounded) and reports its status.
+  unsigned test_nvls_skew = 0;
   bool summary = false;             // NCCL_SHIM_SUMMARY=1 or NCCL_B200_SUMMARY=1
   int min_nccl_version = 21900;     // supported libnccl range (ncclConfig_t layout)
   int max_nccl_version = 22999;

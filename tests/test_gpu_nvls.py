@@ -1,0 +1,107 @@
+"""NVLS (multimem) AllReduce on real GPUs, in child processes (the route is
+forced through the environment, which the library reads once at load)."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+from conftest import REPO, gpu_count, need_gpus
+
+pytestmark = pytest.mark.gpu
+
+CHILD = r"""
+import sys, ctypes as C, torch
+sys.path.insert(0, {repo!r})
+from scc26_nccl_shim_b200.parallel.nccl import Nccl, collective, NcclError
+from scc26_nccl_shim_b200._core import ALGO
+n = {n}
+devs = list(range(n))
+nc = Nccl("interposer")
+arr = (C.c_int * n)(*devs)
+supported = nc.shim.nb_nvls_supported(arr, n)
+comms = nc.comm_init_all(devs)
+streams = [torch.cuda.current_stream(d).cuda_stream for d in devs]
+out = []
+for dtype in (torch.float32, torch.bfloat16):
+    for op in ("sum", "avg"):
+        for count in ((16 << 20), (100 << 20) + 4 * 1024):
+            lim = 15 if dtype == torch.bfloat16 else 1 << 18
+            xs = [torch.randint(-lim, lim + 1, (count,), device=f"cuda:{{d}}").to(dtype) for d in devs]
+            ys = [torch.empty_like(x) for x in xs]
+            for it in range(2):
+                collective(nc, "allreduce", xs, ys, comms, streams, op=op)
+            for d in devs:
+                torch.cuda.synchronize(d)
+            ref = sum(x.to("cuda:0").float() for x in xs)
+            if op == "avg":
+                ref = ref / n
+            ok = all(torch.equal(y.to("cuda:0"), ref.to(dtype)) for y in ys)
+            out.append("ok" if ok else "bad")
+print("RESULT", supported, ",".join(out), nc.custom_calls(ALGO["ar_nvls"]))
+"""
+
+
+def run_child(n, extra_env):
+    env = dict(os.environ, NCCL_B200_NVLS="on", NCCL_B200_ALGO="ar=nvls", NCCL_B200_TUNE="0",
+               **extra_env)
+    r = subprocess.run([sys.executable, "-c", CHILD.format(repo=REPO, n=n)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    return int(line[1]), line[2].split(","), int(line[3])
+
+
+@pytest.mark.parametrize("n", [1, 2, 4, 8])
+def test_nvls_allreduce(n):
+    need_gpus(n)
+    supported, results, calls = run_child(n, {})
+    assert all(r == "ok" for r in results), results
+    if supported:
+        assert calls >= len(results), "NVLS route did not run"
+
+
+TIMEOUT_CHILD = r"""
+import sys, ctypes as C, torch
+sys.path.insert(0, {repo!r})
+from scc26_nccl_shim_b200.parallel.nccl import Nccl, collective, NcclError
+nc = Nccl("interposer")
+arr = (C.c_int * 1)(0)
+if not nc.shim.nb_nvls_supported(arr, 1):
+    print("RESULT unsupported"); sys.exit(0)
+comms = nc.comm_init_all([0])
+x = torch.ones(16 << 20, device="cuda:0"); y = torch.empty_like(x)
+s = [torch.cuda.current_stream(0).cuda_stream]
+out = []
+for i in range(4):
+    try:
+        collective(nc, "allreduce", [x], [y], comms, s)
+        torch.cuda.synchronize(); out.append("ok" if torch.equal(x, y) else "stale")
+    except NcclError as e:
+        torch.cuda.synchronize(); out.append("err%d" % e.code)
+    out.append("s%d" % nc.shim.nb_nvls_status(arr, 1))
+print("RESULT", ",".join(out), nc.shim.nb_poisoned())
+"""
+
+
+def test_nvls_bounded_wait_reports_timeout():
+    """A barrier target nothing can reach: every in-kernel wait runs out after
+    200 ms, the kernel records the status and returns (the GPU stays usable),
+    the next call returns ncclUnhandledCudaError and later calls use NCCL."""
+    need_gpus(1)
+    env = dict(os.environ, NCCL_B200_NVLS="on", NCCL_B200_ALGO="ar=nvls", NCCL_B200_TUNE="0",
+               NCCL_B200_TEST_NVLS_SKEW="1000", NCCL_B200_TIMEOUT_MS="200")
+    r = subprocess.run([sys.executable, "-c", TIMEOUT_CHILD.format(repo=REPO)], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    if line[1] == "unsupported":
+        pytest.skip("multicast objects unavailable on this GPU")
+    seq = line[1].split(",")
+    # call 1: first pass on NCCL; call 2: NVLS kernel times out (status 1);
+    # call 3: reported as an error and the process is poisoned; call 4: NCCL.
+    assert seq[0] == "ok" and seq[1] == "s0"
+    assert seq[3] == "s1", seq
+    assert seq[4] == "err1", seq
+    assert seq[6] == "ok", seq
+    assert line[2] == "1"
