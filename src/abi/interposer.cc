@@ -310,6 +310,7 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
   std::string why;
   if (r.fault.fail_setup() || !r.exec.ensure(plan.needs, info.devices, n, &why)) {
     cudaGetLastError();
+    if (!why.empty()) r.summary.note(std::string("setup_failed ") + algo_name(d.algo) + ": " + why);
     reason = Reason::SetupFailed;
     return Outcome::Fallback;
   }

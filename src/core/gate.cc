@@ -58,6 +58,7 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
   switch (a) {
     case Algo::ArTwoShot: return k == Kind::AllReduce;
     case Algo::ArNvls:
+      // A multicast object needs at least two devices.
       return k == Kind::AllReduce && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
              (op == RedOp::Sum || op == RedOp::Avg);

@@ -296,7 +296,7 @@ bool nvls_supported(const int* devices, int n) {
   for (const auto& e : cache)
     if (e.first == key) return e.second;
   const Driver& d = driver();
-  bool ok = d.ok && n >= 1;
+  bool ok = d.ok && n >= 2;  // cuMulticastCreate rejects a one-device team
   for (int i = 0; ok && i < n; ++i) {
     CUdevice dev;
     int mc = 0;
@@ -355,7 +355,13 @@ bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why
   const size_t size = round_up(mprop.size, gran);
   mprop.size = size;
   CUmemGenericAllocationHandle mc = 0;
-  if (d.MulticastCreate(&mc, &mprop) != CUDA_SUCCESS) return fail("cuMulticastCreate");
+  const CUresult cr = d.MulticastCreate(&mc, &mprop);
+  if (cr != CUDA_SUCCESS) {
+    char what[96];
+    std::snprintf(what, sizeof what, "cuMulticastCreate(devices=%d, size=%zu) returned %d", n, size,
+                  int(cr));
+    return fail(what);
+  }
   for (int i = 0; i < n; ++i) {
     CUdevice dev;
     if (d.DeviceGet(&dev, devices[i]) != CUDA_SUCCESS || d.MulticastAddDevice(mc, dev) != CUDA_SUCCESS)

@@ -39,26 +39,27 @@ for dtype in (torch.float32, torch.bfloat16):
             ok = all(torch.equal(y.to("cuda:0"), ref.to(dtype)) for y in ys)
             out.append("ok" if ok else "bad")
 print("RESULT", supported, ",".join(out), nc.custom_calls(ALGO["ar_nvls"]))
+print("\n".join(l for l in nc.summary_text().splitlines() if not l.endswith("calls=0")))
 """
 
 
 def run_child(n, extra_env):
     env = dict(os.environ, NCCL_B200_NVLS="on", NCCL_B200_ALGO="ar=nvls", NCCL_B200_TUNE="0",
-               **extra_env)
+               NCCL_B200_SUMMARY="1", **extra_env)
     r = subprocess.run([sys.executable, "-c", CHILD.format(repo=REPO, n=n)], env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-3000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
-    return int(line[1]), line[2].split(","), int(line[3])
+    return int(line[1]), line[2].split(","), int(line[3]), r.stdout
 
 
-@pytest.mark.parametrize("n", [1, 2, 4, 8])
+@pytest.mark.parametrize("n", [2, 4, 8])
 def test_nvls_allreduce(n):
     need_gpus(n)
-    supported, results, calls = run_child(n, {})
-    assert all(r == "ok" for r in results), results
+    supported, results, calls, log = run_child(n, {})
+    assert all(r == "ok" for r in results), (results, log)
     if supported:
-        assert calls >= len(results), "NVLS route did not run"
+        assert calls >= len(results), "NVLS route did not run:\n" + log
 
 
 TIMEOUT_CHILD = r"""
@@ -66,29 +67,33 @@ import sys, ctypes as C, torch
 sys.path.insert(0, {repo!r})
 from scc26_nccl_shim_b200.parallel.nccl import Nccl, collective, NcclError
 nc = Nccl("interposer")
-arr = (C.c_int * 1)(0)
-if not nc.shim.nb_nvls_supported(arr, 1):
+arr = (C.c_int * 2)(0, 1)
+if not nc.shim.nb_nvls_supported(arr, 2):
     print("RESULT unsupported"); sys.exit(0)
-comms = nc.comm_init_all([0])
-x = torch.ones(16 << 20, device="cuda:0"); y = torch.empty_like(x)
-s = [torch.cuda.current_stream(0).cuda_stream]
+comms = nc.comm_init_all([0, 1])
+xs = [torch.ones(16 << 20, device=f"cuda:{{d}}") for d in (0, 1)]
+ys = [torch.empty_like(x) for x in xs]
+s = [torch.cuda.current_stream(d).cuda_stream for d in (0, 1)]
 out = []
 for i in range(4):
     try:
-        collective(nc, "allreduce", [x], [y], comms, s)
-        torch.cuda.synchronize(); out.append("ok" if torch.equal(x, y) else "stale")
+        collective(nc, "allreduce", xs, ys, comms, s)
+        for d in (0, 1): torch.cuda.synchronize(d)
+        out.append("ok" if all(torch.equal(y, 2 * x) for x, y in zip(xs, ys)) else "stale")
     except NcclError as e:
-        torch.cuda.synchronize(); out.append("err%d" % e.code)
-    out.append("s%d" % nc.shim.nb_nvls_status(arr, 1))
+        for d in (0, 1): torch.cuda.synchronize(d)
+        out.append("err%d" % e.code)
+    out.append("s%d" % nc.shim.nb_nvls_status(arr, 2))
 print("RESULT", ",".join(out), nc.shim.nb_poisoned())
 """
 
 
 def test_nvls_bounded_wait_reports_timeout():
-    """A barrier target nothing can reach: every in-kernel wait runs out after
-    200 ms, the kernel records the status and returns (the GPU stays usable),
-    the next call returns ncclUnhandledCudaError and later calls use NCCL."""
-    need_gpus(1)
+    """A barrier target nothing can reach, on a 2-GPU clique: every in-kernel
+    wait runs out after 200 ms, the kernels record the status and return (the
+    GPUs stay usable), the next call returns ncclUnhandledCudaError and later
+    calls use NCCL. No rank dies and no GPU faults."""
+    need_gpus(2)
     env = dict(os.environ, NCCL_B200_NVLS="on", NCCL_B200_ALGO="ar=nvls", NCCL_B200_TUNE="0",
                NCCL_B200_TEST_NVLS_SKEW="1000", NCCL_B200_TIMEOUT_MS="200")
     r = subprocess.run([sys.executable, "-c", TIMEOUT_CHILD.format(repo=REPO)], env=env,
