@@ -44,16 +44,19 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
       if (nvls && n >= 2) v.push_back({Algo::ArNvls, 0, 0, 0, 0});
       break;
     case Kind::ReduceScatter:
+      if (nvls && n >= 2) v.push_back({Algo::RsNvls, 0, 0, 0, 0});
       add(Algo::RsPull, 0);
       add(Algo::RsStaged, 0, 64, 3);
       add(Algo::RsStaged, 0, 128, 2);
       add(Algo::RsStaged, 0, 256, 2);
       break;
     case Kind::AllGather:
+      if (nvls && n >= 2) v.push_back({Algo::AgNvls, 0, 0, 0, 0});
       add(Algo::AgPull, 0);
       add(Algo::AgPull, 10000);
       break;
     case Kind::Broadcast:
+      if (nvls && n >= 2) v.push_back({Algo::BcNvls, 0, 0, 0, 0});
       if (n >= 3) {
         add(Algo::BcScatter, 0);
         add(Algo::BcScatter, 10000);

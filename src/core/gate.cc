@@ -69,6 +69,12 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
     case Algo::ArStaged: return k == Kind::AllReduce;
     case Algo::RsStaged: return k == Kind::ReduceScatter;
     case Algo::BcChain: return k == Kind::Broadcast;
+    case Algo::BcNvls: return k == Kind::Broadcast && nvls_available && nranks >= 2;
+    case Algo::AgNvls: return k == Kind::AllGather && nvls_available && nranks >= 2;
+    case Algo::RsNvls:
+      return k == Kind::ReduceScatter && nvls_available && nranks >= 2 &&
+             (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
+             (op == RedOp::Sum || op == RedOp::Avg);
     default: return false;
   }
 }
@@ -127,8 +133,22 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
   if (s.capturing) return fallback(Reason::Capturing);
   if (p.first_pass && !s.first_pass_done) return fallback(Reason::FirstPass);
   Algo algo = choose_algo(a, n, s.nvls_available, p, s.preferred[size_t(a.kind)]);
-  // The multimem kernel moves whole 16-byte vectors only.
-  if (algo == Algo::ArNvls && call_bytes(a) % 16 != 0) algo = Algo::ArTwoShot;
+  // The multimem kernels move whole 16-byte vectors only: every buffer and
+  // every slot must be 16-byte aligned.
+  const bool nvls = algo == Algo::ArNvls || algo == Algo::BcNvls || algo == Algo::AgNvls ||
+                    algo == Algo::RsNvls;
+  bool aligned = call_bytes(a) % 16 == 0;
+  for (const CallDesc& c : calls)
+    aligned = aligned && c.recv % 16 == 0 && (c.send % 16 == 0 || (c.kind == Kind::Broadcast && c.rank != c.root));
+  if (nvls && !aligned) {
+    const Policy q = [&] {
+      Policy x = p;
+      x.nvls = NvlsMode::Off;
+      x.force_algo[size_t(a.kind)] = Algo::Fallback;
+      return x;
+    }();
+    algo = choose_algo(a, n, false, q);
+  }
   if (algo == Algo::Fallback) return fallback(Reason::PolicyFallback);
   return {algo, Reason::None};
 }

@@ -20,7 +20,7 @@ void Needs::merge(const Needs& o) {
 }
 
 void slice_of(size_t bytes, int parts, int i, size_t* off, size_t* len) {
-  const size_t base = (bytes / size_t(parts)) & ~size_t(15);
+  const size_t base = (bytes / size_t(parts)) & ~size_t(31);
   *off = base * size_t(i);
   *len = i == parts - 1 ? bytes - *off : base;
 }
@@ -676,11 +676,12 @@ void plan_bc_chain(Builder& b, const CliqueDesc& d, const Shares& s) {
   b.join();
 }
 
-// NVLS AllReduce: one gang op per rank on its aux stream, after every rank's
-// input is ready. Inside, rank r copies its input into its multicast-bound
-// scratch, then reduces slice r through the switch (multimem.ld_reduce) and
-// multicasts the result (multimem.st), then copies its output out, with
-// bounded in-kernel barriers between the phases.
+// NVLS routes (AllReduce, Broadcast, AllGather, ReduceScatter): one gang op
+// per rank on its aux stream, after every rank's input is ready. Inside,
+// the kernels move data through the rank's multicast-bound scratch and the
+// switch (multimem.ld_reduce / multimem.st) with bounded in-kernel barriers
+// between pipelined rounds (exec/nvls.cu). The prologue waits make the
+// members of a gang start together, so those barriers wait only for skew.
 void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p) {
   const int n = b.n();
   b.prologue();
@@ -708,6 +709,7 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
     case Algo::ArStaged: plan_staged(b, d, s, true); break;
     case Algo::RsStaged: plan_staged(b, d, s, false); break;
     case Algo::BcChain: plan_bc_chain(b, d, s); break;
+    case Algo::BcNvls: case Algo::AgNvls: case Algo::RsNvls: plan_ar_nvls(b, d, p); break;
     default: break;
   }
 }

@@ -120,8 +120,8 @@ struct Plan {
   size_t sm_bytes = 0, ce_bytes = 0, host_bytes = 0;
 };
 
-// 16-byte-aligned split of `bytes` into `parts` consecutive slices; the last
-// slice takes the remainder.
+// 32-byte-aligned split of `bytes` into `parts` consecutive slices (the
+// kernels' widest vector); the last slice takes the remainder.
 void slice_of(size_t bytes, int parts, int i, size_t* off, size_t* len);
 // Host-lane share of `len` bytes at `ppm`: a whole number of 16-byte units,
 // zero below the policy minimum.

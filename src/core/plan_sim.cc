@@ -340,14 +340,41 @@ std::string simulate_plan(const Plan& plan, const SimLayout& lay, const FoldPara
   std::vector<uint8_t> tmp;
   for (int v : order) {
     if (v == g.gang) {
-      // One NVLS AllReduce over the whole buffer for every rank.
+      // The whole NVLS collective for every rank at once.
       const size_t bytes = plan.desc.bytes;
-      tmp.assign(bytes, 0);
-      const void* srcs[kMaxRanks];
-      for (int q = 0; q < n; ++q) srcs[q] = arenas[size_t(q)].data() + lay.send_off[q];
-      host_fold(fp, srcs, n, tmp.data(), bytes);
-      for (int q = 0; q < n; ++q)
-        std::memcpy(arenas[size_t(q)].data() + lay.recv_off[q], tmp.data(), bytes);
+      auto send = [&](int q) { return arenas[size_t(q)].data() + lay.send_off[q]; };
+      auto recv = [&](int q) { return arenas[size_t(q)].data() + lay.recv_off[q]; };
+      switch (plan.desc.kind) {
+        case Kind::AllReduce: {
+          tmp.assign(bytes, 0);
+          const void* srcs[kMaxRanks];
+          for (int q = 0; q < n; ++q) srcs[q] = send(q);
+          host_fold(fp, srcs, n, tmp.data(), bytes);
+          for (int q = 0; q < n; ++q) std::memcpy(recv(q), tmp.data(), bytes);
+          break;
+        }
+        case Kind::Broadcast:
+          tmp.assign(send(plan.desc.root), send(plan.desc.root) + bytes);
+          for (int q = 0; q < n; ++q) std::memcpy(recv(q), tmp.data(), bytes);
+          break;
+        case Kind::AllGather:
+          tmp.clear();
+          for (int q = 0; q < n; ++q) tmp.insert(tmp.end(), send(q), send(q) + bytes);
+          for (int q = 0; q < n; ++q) std::memcpy(recv(q), tmp.data(), tmp.size());
+          break;
+        case Kind::ReduceScatter: {
+          std::vector<uint8_t> all(bytes * size_t(n));
+          for (int r = 0; r < n; ++r) {
+            const void* srcs[kMaxRanks];
+            for (int q = 0; q < n; ++q) srcs[q] = send(q) + size_t(r) * bytes;
+            host_fold(fp, srcs, n, all.data() + size_t(r) * bytes, bytes);
+          }
+          for (int r = 0; r < n; ++r) std::memcpy(recv(r), all.data() + size_t(r) * bytes, bytes);
+          break;
+        }
+        default:
+          break;
+      }
       continue;
     }
     if (v >= int(plan.ops.size())) continue;

@@ -61,6 +61,9 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else if (a == "staged" && *kind == Kind::AllReduce) *algo = Algo::ArStaged;
   else if (a == "staged" && *kind == Kind::ReduceScatter) *algo = Algo::RsStaged;
   else if (a == "chain" && *kind == Kind::Broadcast) *algo = Algo::BcChain;
+  else if (a == "nvls" && *kind == Kind::Broadcast) *algo = Algo::BcNvls;
+  else if (a == "nvls" && *kind == Kind::AllGather) *algo = Algo::AgNvls;
+  else if (a == "nvls" && *kind == Kind::ReduceScatter) *algo = Algo::RsNvls;
   else return false;
   return true;
 }

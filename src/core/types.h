@@ -46,6 +46,9 @@ enum class Algo : uint8_t {
   ArStaged,    // copy engines pull slice r into scratch, a local fused fold, CE pushes
   RsStaged,    // copy engines pull slot r into scratch, a local fused fold
   BcChain,     // pipelined chain: each rank pulls every piece from its predecessor
+  BcNvls,      // the root multicasts through the switch (multimem.st)
+  AgNvls,      // every rank multicasts its slot through the switch
+  RsNvls,      // every rank multimem.ld_reduces its own slot
   Count
 };
 

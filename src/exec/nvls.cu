@@ -52,6 +52,9 @@ struct NvlsArgs {
   unsigned* status;          // mapped host word: nonzero = a wait expired
   unsigned base;             // flag value before this call's first barrier
   int nranks, rank, dtype, avg;
+  int mode;                  // collective kind (xfer kernel)
+  int root;                  // Broadcast
+  unsigned long long slot;   // AllGather / ReduceScatter per-rank slot bytes
 };
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -118,41 +121,61 @@ __device__ __forceinline__ void portion(unsigned long long rlen, int n, int q, u
   *hi = soff + b;
 }
 
-__device__ __forceinline__ void copy16(char* dst, const char* src, unsigned long long bytes) {
+// Copy `bytes` with the `nthreads` threads of a warp group (thread index t).
+__device__ __forceinline__ void copy16(char* dst, const char* src, unsigned long long bytes, int t,
+                                       int nthreads) {
   const unsigned long long nv = bytes / 16;
   constexpr int U = 4;
-  for (unsigned long long i = threadIdx.x; i < nv; i += blockDim.x * U) {
+  for (unsigned long long i = t; i < nv; i += (unsigned long long)nthreads * U) {
     uint4 v[U];
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (i + u * blockDim.x < nv) v[u] = __ldcs(reinterpret_cast<const uint4*>(src) + i + u * blockDim.x);
+      if (i + u * nthreads < nv) v[u] = __ldcs(reinterpret_cast<const uint4*>(src) + i + u * nthreads);
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (i + u * blockDim.x < nv) __stcs(reinterpret_cast<uint4*>(dst) + i + u * blockDim.x, v[u]);
+      if (i + u * nthreads < nv) __stcs(reinterpret_cast<uint4*>(dst) + i + u * nthreads, v[u]);
   }
 }
 
-__global__ void __launch_bounds__(512) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
+// Warp specialization: the first half of the block's warps reduce through
+// the switch (NVLink-bound) while the second half copies rounds in and out
+// of the scratch (HBM-bound), so the two resources work at the same time.
+__global__ void __launch_bounds__(1024, 1) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
   __shared__ int abort_flag;
   if (threadIdx.x == 0) abort_flag = 0;
   __syncthreads();
   const int n = a.nranks;
   const unsigned long long rounds = (a.bytes + a.round - 1) / a.round;
   const float inv = 1.0f / float(n);
+  const int half = blockDim.x / 2;
+  const bool reducer = threadIdx.x < half;
+  const int t = reducer ? threadIdx.x : threadIdx.x - half;
   for (unsigned long long s = 0; s < rounds + 2; ++s) {
-    // C(s-2): copy the reduced round out of the scratch.
-    if (s >= 2) {
-      const unsigned long long i = s - 2, rbase = i * a.round;
-      const unsigned long long rlen = min(a.round, a.bytes - rbase);
-      const char* buf = a.uc + (i % 3) * a.buf_stride;
-      for (int q = 0; q < n; ++q) {
-        unsigned long long lo, hi;
-        portion(rlen, n, q, &lo, &hi);
-        copy16(a.recv + rbase + lo, buf + lo, hi - lo);
+    if (!reducer) {
+      // C(s-2): copy the reduced round out of the scratch.
+      if (s >= 2) {
+        const unsigned long long i = s - 2, rbase = i * a.round;
+        const unsigned long long rlen = min(a.round, a.bytes - rbase);
+        const char* buf = a.uc + (i % 3) * a.buf_stride;
+        for (int q = 0; q < n; ++q) {
+          unsigned long long lo, hi;
+          portion(rlen, n, q, &lo, &hi);
+          copy16(a.recv + rbase + lo, buf + lo, hi - lo, t, half);
+        }
       }
-    }
-    // B(s-1): reduce and multicast this rank's slice.
-    if (s >= 1 && s - 1 < rounds) {
+      // A(s): copy this GPU's input round into its scratch.
+      if (s < rounds) {
+        const unsigned long long rbase = s * a.round;
+        const unsigned long long rlen = min(a.round, a.bytes - rbase);
+        char* buf = a.uc + (s % 3) * a.buf_stride;
+        for (int q = 0; q < n; ++q) {
+          unsigned long long lo, hi;
+          portion(rlen, n, q, &lo, &hi);
+          copy16(buf + lo, a.send + rbase + lo, hi - lo, t, half);
+        }
+      }
+    } else if (s >= 1 && s - 1 < rounds) {
+      // B(s-1): reduce and multicast this rank's slice.
       const unsigned long long i = s - 1, rbase = i * a.round;
       const unsigned long long rlen = min(a.round, a.bytes - rbase);
       char* mbuf = a.mc + (i % 3) * a.buf_stride;
@@ -160,26 +183,15 @@ __global__ void __launch_bounds__(512) nvls_allreduce_kernel(const __grid_consta
       portion(rlen, n, a.rank, &lo, &hi);
       const unsigned long long nv = (hi - lo) / 16;
       constexpr int U = 4;
-      for (unsigned long long v = threadIdx.x; v < nv; v += blockDim.x * U) {
+      for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
         uint4 x[U];
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          if (v + u * blockDim.x < nv) x[u] = ld_reduce(mbuf + lo + (v + u * blockDim.x) * 16, a.dtype);
+          if (v + u * half < nv) x[u] = ld_reduce(mbuf + lo + (v + u * half) * 16, a.dtype);
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          if (v + u * blockDim.x < nv)
-            mc_store(mbuf + lo + (v + u * blockDim.x) * 16, a.avg ? scale(x[u], a.dtype, inv) : x[u]);
-      }
-    }
-    // A(s): copy this GPU's input round into its scratch.
-    if (s < rounds) {
-      const unsigned long long rbase = s * a.round;
-      const unsigned long long rlen = min(a.round, a.bytes - rbase);
-      char* buf = a.uc + (s % 3) * a.buf_stride;
-      for (int q = 0; q < n; ++q) {
-        unsigned long long lo, hi;
-        portion(rlen, n, q, &lo, &hi);
-        copy16(buf + lo, a.send + rbase + lo, hi - lo);
+          if (v + u * half < nv)
+            mc_store(mbuf + lo + (v + u * half) * 16, a.avg ? scale(x[u], a.dtype, inv) : x[u]);
       }
     }
     // Barrier: this block's counterparts on every GPU finished step s.
@@ -200,6 +212,121 @@ __global__ void __launch_bounds__(512) nvls_allreduce_kernel(const __grid_consta
     }
     __syncthreads();
     if (abort_flag) return;
+  }
+}
+
+// This block's part [lo, hi) of a flat range of `len` bytes (16-byte units).
+__device__ __forceinline__ void flat_portion(unsigned long long len, unsigned long long* lo,
+                                             unsigned long long* hi) {
+  const unsigned long long per = ((len + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+  *lo = min(len, per * blockIdx.x);
+  *hi = min(len, *lo + per);
+}
+
+__device__ __forceinline__ bool nvls_barrier(const NvlsArgs& a, unsigned long long s, int* abort_flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    mc_arrive(a.mc_flags + blockIdx.x);
+    const unsigned target = a.base + unsigned(a.nranks) * unsigned(s + 1);
+    const unsigned long long start = globaltimer();
+    while (int(ld_acquire(a.uc_flags + blockIdx.x) - target) < 0) {
+      if (globaltimer() - start > a.timeout_ns) {
+        *reinterpret_cast<volatile unsigned*>(a.status) = 1u;
+        __threadfence_system();
+        *abort_flag = 1;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return *abort_flag == 0;
+}
+
+// Broadcast / AllGather / ReduceScatter through the switch, with the same
+// three-buffer scratch, per-block bounded barriers and warp split as the
+// AllReduce kernel:
+//  Broadcast: the root multicasts round s of its input (multimem.st) while
+//    every GPU copies round s-1 out of its scratch; root sends each byte once.
+//  AllGather: every rank multicasts its part of round s into its own part of
+//    the round buffer; every GPU copies round s-1 (all parts) out.
+//  ReduceScatter: every GPU copies round s of its input in; every rank
+//    multimem.ld_reduces its own part of round s-1 straight into its output.
+__global__ void __launch_bounds__(1024, 1) nvls_xfer_kernel(const __grid_constant__ NvlsArgs a) {
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = 0;
+  __syncthreads();
+  const int n = a.nranks;
+  const int half = blockDim.x / 2;
+  const bool mover = threadIdx.x < half;  // switch-side warps
+  const int t = mover ? threadIdx.x : threadIdx.x - half;
+  const float inv = 1.0f / float(n);
+  const bool bc = a.mode == int(Kind::Broadcast);
+  const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)n) & ~15ull);
+  const unsigned long long total = bc ? a.bytes : a.slot;
+  const unsigned long long rounds = (total + part - 1) / part;
+  for (unsigned long long s = 0; s < rounds + 1; ++s) {
+    if (a.mode == int(Kind::ReduceScatter)) {
+      if (!mover && s < rounds) {  // A(s): copy every slot's part of round s in
+        const unsigned long long plen = min(part, total - s * part);
+        char* buf = a.uc + (s % 3) * a.buf_stride;
+        unsigned long long lo, hi;
+        flat_portion(plen, &lo, &hi);
+        for (int q = 0; q < n; ++q)
+          copy16(buf + q * part + lo, a.send + q * a.slot + s * part + lo, hi - lo, t, half);
+      }
+      if (mover && s >= 1) {  // B(s-1): reduce the own part into the output
+        const unsigned long long i = s - 1, plen = min(part, total - i * part);
+        const char* mbuf = a.mc + (i % 3) * a.buf_stride + a.rank * part;
+        unsigned long long lo, hi;
+        flat_portion(plen, &lo, &hi);
+        const unsigned long long nv = (hi - lo) / 16;
+        constexpr int U = 4;
+        for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
+          uint4 x[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (v + u * half < nv) x[u] = ld_reduce(mbuf + lo + (v + u * half) * 16, a.dtype);
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (v + u * half < nv)
+              __stcs(reinterpret_cast<uint4*>(a.recv + i * part + lo) + v + u * half,
+                     a.avg ? scale(x[u], a.dtype, inv) : x[u]);
+        }
+      }
+    } else {
+      if (!mover && s >= 1) {  // C(s-1): copy round s-1 out
+        const unsigned long long i = s - 1, plen = min(part, total - i * part);
+        const char* buf = a.uc + (i % 3) * a.buf_stride;
+        unsigned long long lo, hi;
+        flat_portion(plen, &lo, &hi);
+        if (bc) {
+          copy16(a.recv + i * part + lo, buf + lo, hi - lo, t, half);
+        } else {
+          for (int q = 0; q < n; ++q)
+            copy16(a.recv + q * a.slot + i * part + lo, buf + q * part + lo, hi - lo, t, half);
+        }
+      }
+      if (mover && s < rounds && (!bc || a.rank == a.root)) {  // B(s): multicast
+        const unsigned long long plen = min(part, total - s * part);
+        char* mbuf = a.mc + (s % 3) * a.buf_stride + (bc ? 0 : a.rank * part);
+        const char* src = a.send + s * part;
+        unsigned long long lo, hi;
+        flat_portion(plen, &lo, &hi);
+        const unsigned long long nv = (hi - lo) / 16;
+        constexpr int U = 4;
+        for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
+          uint4 x[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (v + u * half < nv) x[u] = __ldcs(reinterpret_cast<const uint4*>(src + lo) + v + u * half);
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (v + u * half < nv) mc_store(mbuf + lo + (v + u * half) * 16, x[u]);
+        }
+      }
+    }
+    if (!nvls_barrier(a, s, &abort_flag)) return;
   }
 }
 
@@ -434,14 +561,26 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.rank = r;
   a.dtype = int(plan.desc.dtype);
   a.avg = plan.desc.op == RedOp::Avg;
+  a.mode = int(plan.desc.kind);
+  a.root = plan.desc.root;
+  a.slot = plan.desc.bytes;  // AG send slot / RS receive slot
   (void)dev;
-  void* argv[] = {&a};
-  const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(nvls_allreduce_kernel),
-                                                    dim3(unsigned(c->blocks)), dim3(512), argv, 0, s);
-  if (r == b.nranks - 1) {
-    const unsigned long long rounds = (a.bytes + a.round - 1) / a.round;
-    c->barriers += rounds + 2;
+  const bool ar = plan.desc.kind == Kind::AllReduce;
+  // Barriers this call runs (one per step); every rank runs the same count.
+  unsigned long long steps = 0;
+  if (ar) {
+    steps = (a.bytes + a.round - 1) / a.round + 2;
+  } else {
+    const bool bc = plan.desc.kind == Kind::Broadcast;
+    const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)b.nranks) & ~15ull);
+    steps = (plan.desc.bytes + part - 1) / part + 1;
+    if (!bc && part == 0) return cudaErrorInvalidValue;
   }
+  void* argv[] = {&a};
+  const void* fn = ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel)
+                      : reinterpret_cast<const void*>(nvls_xfer_kernel);
+  const cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(1024), argv, 0, s);
+  if (r == b.nranks - 1) c->barriers += steps;
   return e;
 }
 

@@ -175,38 +175,79 @@ __device__ __forceinline__ uint4 fold_vec(const uint4 (&v)[NSRC], int op, int nr
   return out;
 }
 
-template <typename T, int NSRC>
-__global__ void __launch_bounds__(512, 2) reduce_kernel(const __grid_constant__ KReduceArgs a) {
+// A VB-byte vector (16: ld/st.global.v4; 32: the sm_100 256-bit
+// ld/st.global.v8, which halves the request count on NVLink).
+template <int VB>
+struct VecT {
+  uint4 h[VB / 16];
+};
+
+template <int VB>
+__device__ __forceinline__ VecT<VB> ldv(const VecT<VB>* p) {
+  VecT<VB> v;
+  if constexpr (VB == 32) {
+    asm volatile("ld.global.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v.h[0].x), "=r"(v.h[0].y), "=r"(v.h[0].z), "=r"(v.h[0].w), "=r"(v.h[1].x),
+                   "=r"(v.h[1].y), "=r"(v.h[1].z), "=r"(v.h[1].w)
+                 : "l"(p));
+  } else {
+    v.h[0] = __ldcs(reinterpret_cast<const uint4*>(p));
+  }
+  return v;
+}
+
+template <int VB>
+__device__ __forceinline__ void stv(VecT<VB>* p, const VecT<VB>& v) {
+  if constexpr (VB == 32) {
+    asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.h[0].x),
+                 "r"(v.h[0].y), "r"(v.h[0].z), "r"(v.h[0].w), "r"(v.h[1].x), "r"(v.h[1].y),
+                 "r"(v.h[1].z), "r"(v.h[1].w)
+                 : "memory");
+  } else {
+    __stcs(reinterpret_cast<uint4*>(p), v.h[0]);
+  }
+}
+
+template <typename T, int NSRC, int VB>
+__global__ void __launch_bounds__(512, VB == 32 ? 1 : 2) reduce_kernel(const __grid_constant__ KReduceArgs a) {
   using A = typename Acc<T>::type;
-  constexpr int U = (8 / NSRC) > 0 ? (8 / NSRC) : 1;
+  using V = VecT<VB>;
+  // About eight 16-byte loads in flight per thread.
+  constexpr int U = (8 * 16 / VB / NSRC) > 0 ? (8 * 16 / VB / NSRC) : 1;
   A s[NSRC];
 #pragma unroll
   for (int k = 0; k < NSRC; ++k) s[k] = load_scale<T>(a, k);
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   const unsigned long long tid = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
   for (unsigned long long base = tid; base < a.nvec; base += stride * U) {
-    uint4 v[U][NSRC];
+    V v[U][NSRC];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const unsigned long long idx = base + u * stride;
       if (idx < a.nvec) {
 #pragma unroll
-        for (int k = 0; k < NSRC; ++k)
-          v[u][k] = ld_stream(static_cast<const uint4*>(a.src[k]) + idx);
+        for (int k = 0; k < NSRC; ++k) v[u][k] = ldv<VB>(static_cast<const V*>(a.src[k]) + idx);
       }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const unsigned long long idx = base + u * stride;
       if (idx < a.nvec) {
-        const uint4 out = fold_vec<T, NSRC>(v[u], a.op, a.nranks, s);
-        for (int d = 0; d < a.ndst; ++d) st_stream(static_cast<uint4*>(a.dst[d]) + idx, out);
+        V out;
+#pragma unroll
+        for (int j = 0; j < VB / 16; ++j) {
+          uint4 part[NSRC];
+#pragma unroll
+          for (int k = 0; k < NSRC; ++k) part[k] = v[u][k].h[j];
+          out.h[j] = fold_vec<T, NSRC>(part, a.op, a.nranks, s);
+        }
+        for (int d = 0; d < a.ndst; ++d) stv<VB>(static_cast<V*>(a.dst[d]) + idx, out);
       }
     }
   }
-  // Trailing elements that do not fill a 16-byte vector.
+  // Trailing elements that do not fill a vector.
   if (blockIdx.x == 0 && threadIdx.x < a.tail_elems) {
-    const unsigned long long e = a.nvec * (16 / sizeof(T)) + threadIdx.x;
+    const unsigned long long e = a.nvec * (VB / sizeof(T)) + threadIdx.x;
     A acc = first<T>(static_cast<const T*>(a.src[0])[e], a.op, s[0]);
 #pragma unroll
     for (int k = 1; k < NSRC; ++k) acc = combine<T>(acc, static_cast<const T*>(a.src[k])[e], a.op, s[k]);
@@ -232,7 +273,25 @@ __global__ void __launch_bounds__(512) copy_kernel(const __grid_constant__ KCopy
     const char* src = static_cast<const char*>(a.src[s]) + lo;
     char* dst = static_cast<char*>(a.dst[s]) + lo;
     const unsigned long long n = hi - lo;
-    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 31) == 0) {
+      using V = VecT<32>;
+      const unsigned long long nvec = n / 32;
+      constexpr int U = 4;
+      for (unsigned long long base = threadIdx.x; base < nvec; base += blockDim.x * U) {
+        V v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const unsigned long long i = base + u * blockDim.x;
+          if (i < nvec) v[u] = ldv<32>(reinterpret_cast<const V*>(src) + i);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const unsigned long long i = base + u * blockDim.x;
+          if (i < nvec) stv<32>(reinterpret_cast<V*>(dst) + i, v[u]);
+        }
+      }
+      for (unsigned long long i = nvec * 32 + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    } else if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
       const unsigned long long nvec = n / 16;
       constexpr int U = 8;
       for (unsigned long long base = threadIdx.x; base < nvec; base += blockDim.x * U) {
@@ -261,26 +320,28 @@ __global__ void __launch_bounds__(512) copy_kernel(const __grid_constant__ KCopy
 
 using ReduceFn = void (*)(KReduceArgs);
 
-template <typename T>
+template <typename T, int VB = 16>
 ReduceFn reduce_for(int nsrc) {
   switch (nsrc) {
-    case 1: return reduce_kernel<T, 1>;
-    case 2: return reduce_kernel<T, 2>;
-    case 3: return reduce_kernel<T, 3>;
-    case 4: return reduce_kernel<T, 4>;
-    case 5: return reduce_kernel<T, 5>;
-    case 6: return reduce_kernel<T, 6>;
-    case 7: return reduce_kernel<T, 7>;
-    case 8: return reduce_kernel<T, 8>;
+    case 1: return reduce_kernel<T, 1, VB>;
+    case 2: return reduce_kernel<T, 2, VB>;
+    case 3: return reduce_kernel<T, 3, VB>;
+    case 4: return reduce_kernel<T, 4, VB>;
+    case 5: return reduce_kernel<T, 5, VB>;
+    case 6: return reduce_kernel<T, 6, VB>;
+    case 7: return reduce_kernel<T, 7, VB>;
+    case 8: return reduce_kernel<T, 8, VB>;
     default: return nullptr;
   }
 }
 
-ReduceFn pick_reduce(DType t, int nsrc) {
+// 32-byte vectors for the hot floating types when every operand allows it.
+ReduceFn pick_reduce(DType t, int nsrc, bool wide) {
   switch (t) {
-    case DType::F32: return reduce_for<float>(nsrc);
-    case DType::F16: return reduce_for<__half>(nsrc);
-    case DType::BF16: return reduce_for<__nv_bfloat16>(nsrc);
+    case DType::F32: return wide ? reduce_for<float, 32>(nsrc) : reduce_for<float>(nsrc);
+    case DType::F16: return wide ? reduce_for<__half, 32>(nsrc) : reduce_for<__half>(nsrc);
+    case DType::BF16:
+      return wide ? reduce_for<__nv_bfloat16, 32>(nsrc) : reduce_for<__nv_bfloat16>(nsrc);
     case DType::F64: return reduce_for<double>(nsrc);
     case DType::I8: return reduce_for<int8_t>(nsrc);
     case DType::U8: return reduce_for<uint8_t>(nsrc);
@@ -309,15 +370,18 @@ cudaError_t launch_reduce(const ReduceLaunch& r, LaunchShape shape, cudaStream_t
   if (!es || r.nsrc < 1 || r.nsrc > kMaxRanks || r.ndst < 1 || r.ndst > kMaxRanks ||
       r.bytes % es)
     return cudaErrorInvalidValue;
-  const ReduceFn fn = pick_reduce(r.fold.dtype, r.nsrc);
-  if (!fn) return cudaErrorInvalidValue;
   if (r.bytes == 0) return cudaSuccess;
-  // The kernel issues 16-byte vector accesses: refuse (never launch) any
-  // operand that is not 16-byte aligned.
-  for (int i = 0; i < r.nsrc; ++i)
-    if (reinterpret_cast<uintptr_t>(r.src[i]) % 16) return cudaErrorMisalignedAddress;
-  for (int i = 0; i < r.ndst; ++i)
-    if (reinterpret_cast<uintptr_t>(r.dst[i]) % 16) return cudaErrorMisalignedAddress;
+  // The kernel issues 16- or 32-byte vector accesses: refuse (never launch)
+  // any operand that is not 16-byte aligned; use 32 when all are 32-aligned.
+  uintptr_t any = 0;
+  for (int i = 0; i < r.nsrc; ++i) any |= reinterpret_cast<uintptr_t>(r.src[i]);
+  for (int i = 0; i < r.ndst; ++i) any |= reinterpret_cast<uintptr_t>(r.dst[i]);
+  if (any % 16) return cudaErrorMisalignedAddress;
+  const bool hot = r.fold.dtype == DType::F32 || r.fold.dtype == DType::BF16 || r.fold.dtype == DType::F16;
+  const bool wide = hot && any % 32 == 0;
+  const int vb = wide ? 32 : 16;
+  const ReduceFn fn = pick_reduce(r.fold.dtype, r.nsrc, wide);
+  if (!fn) return cudaErrorInvalidValue;
   KReduceArgs k{};
   for (int i = 0; i < r.nsrc; ++i) {
     k.src[i] = r.src[i];
@@ -325,8 +389,8 @@ cudaError_t launch_reduce(const ReduceLaunch& r, LaunchShape shape, cudaStream_t
     k.scale[i] = r.fold.scalars[i];
   }
   for (int i = 0; i < r.ndst; ++i) k.dst[i] = r.dst[i];
-  k.nvec = r.bytes / 16;
-  k.tail_elems = (r.bytes - k.nvec * 16) / es;
+  k.nvec = r.bytes / vb;
+  k.tail_elems = (r.bytes - k.nvec * vb) / es;
   k.ndst = r.ndst;
   k.op = int(r.fold.op);
   k.nranks = r.fold.nranks;

@@ -31,7 +31,10 @@ def run_kind(nc, kind, comms, devs, count, dtype=torch.float32, op="sum", inplac
     n = len(devs)
     streams = [torch.cuda.current_stream(d).cuda_stream for d in devs]
     gens = [torch.Generator(device=f"cuda:{d}").manual_seed(100 + d) for d in devs]
-    lim = 127 if dtype == torch.bfloat16 else 1023
+    # Every partial sum must be exact in the element type, so any reduction
+    # order (the NVSwitch's included) gives the same bits: |sum| <= 256 for
+    # bf16 (8-bit significand), <= 2048 for fp16.
+    lim = {torch.bfloat16: 256 // n, torch.float16: 2048 // n}.get(dtype, 1023)
     def data(d, c):
         return torch.randint(-lim, lim + 1, (c,), device=f"cuda:{d}", generator=gens[devs.index(d)]).to(dtype)
     if kind == "reducescatter":

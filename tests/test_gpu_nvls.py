@@ -62,6 +62,39 @@ def test_nvls_allreduce(n):
         assert calls >= len(results), "NVLS route did not run:\n" + log
 
 
+KINDS_CHILD = r"""
+import sys, ctypes as C, torch
+sys.path.insert(0, {repo!r}); sys.path.insert(0, {repo!r} + "/tests")
+from scc26_nccl_shim_b200.parallel.nccl import Nccl
+from scc26_nccl_shim_b200._core import ALGO
+from test_gpu_abi import run_kind
+n = {n}
+devs = list(range(n))
+nc = Nccl("interposer")
+comms = nc.comm_init_all(devs)
+for kind in ("broadcast", "allgather", "reducescatter"):
+    c = (48 << 20) // 4 // n if kind != "broadcast" else (300 << 20) // 4
+    for inplace in (False, True):
+        run_kind(nc, kind, comms, devs, c, inplace=inplace, root=n - 1)
+    run_kind(nc, kind, comms, devs, c, dtype=torch.bfloat16)
+print("RESULT", nc.custom_calls(ALGO["bc_nvls"]), nc.custom_calls(ALGO["ag_nvls"]),
+      nc.custom_calls(ALGO["rs_nvls"]))
+"""
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_nvls_broadcast_allgather_reducescatter(n):
+    need_gpus(n)
+    env = dict(os.environ, NCCL_B200_NVLS="on", NCCL_B200_ALGO="bc=nvls,ag=nvls,rs=nvls",
+               NCCL_B200_TUNE="0", NCCL_B200_FIRST_PASS="0", NCCL_B200_RS_MIN="1K",
+               NCCL_B200_AG_MIN="1K")
+    r = subprocess.run([sys.executable, "-c", KINDS_CHILD.format(repo=REPO, n=n)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    assert all(int(x) >= 3 for x in line[1:]), line
+
+
 TIMEOUT_CHILD = r"""
 import sys, ctypes as C, torch
 sys.path.insert(0, {repo!r})
