@@ -28,6 +28,9 @@ struct Policy {
   NvlsMode nvls = NvlsMode::Auto;
   int nvls_min_ranks = 4;           // NVLS AllReduce only pays off from 4 ranks
   size_t nvls_round_bytes = 256 * kMiB;  // multicast scratch per GPU (one round)
+  int nvls_threads = 768;           // threads per block of the NVLS kernels
+  int nvls_movers = 512;            // of those: switch-side workers (the rest copy)
+  int nvls_unroll = 4;              // multimem requests in flight per switch-side thread
   Algo force_algo[size_t(Kind::Count)] = {Algo::Fallback, Algo::Fallback, Algo::Fallback,
                                           Algo::Fallback};  // Fallback = choose
   // Shares in parts per 10000 of the bytes each GPU receives. Negative =

@@ -52,6 +52,7 @@ struct NvlsArgs {
   unsigned* status;          // mapped host word: nonzero = a wait expired
   unsigned base;             // flag value before this call's first barrier
   int nranks, rank, dtype, avg;
+  int movers;                // threads of a block that work through the switch
   int mode;                  // collective kind (xfer kernel)
   int root;                  // Broadcast
   unsigned long long slot;   // AllGather / ReduceScatter per-rank slot bytes
@@ -140,16 +141,19 @@ __device__ __forceinline__ void copy16(char* dst, const char* src, unsigned long
 // Warp specialization: the first half of the block's warps reduce through
 // the switch (NVLink-bound) while the second half copies rounds in and out
 // of the scratch (HBM-bound), so the two resources work at the same time.
-__global__ void __launch_bounds__(1024, 1) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
+// U: multimem requests in flight per switch-side thread.
+template <int U, int DT>
+__global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
   __shared__ int abort_flag;
   if (threadIdx.x == 0) abort_flag = 0;
   __syncthreads();
   const int n = a.nranks;
   const unsigned long long rounds = (a.bytes + a.round - 1) / a.round;
   const float inv = 1.0f / float(n);
-  const int half = blockDim.x / 2;
-  const bool reducer = threadIdx.x < half;
-  const int t = reducer ? threadIdx.x : threadIdx.x - half;
+  // The first a.movers threads work through the switch; the rest copy.
+  const bool reducer = int(threadIdx.x) < a.movers;
+  const int t = reducer ? threadIdx.x : threadIdx.x - a.movers;
+  const int half = reducer ? a.movers : int(blockDim.x) - a.movers;  // this group's size
   for (unsigned long long s = 0; s < rounds + 2; ++s) {
     if (!reducer) {
       // C(s-2): copy the reduced round out of the scratch.
@@ -182,16 +186,15 @@ __global__ void __launch_bounds__(1024, 1) nvls_allreduce_kernel(const __grid_co
       unsigned long long lo, hi;
       portion(rlen, n, a.rank, &lo, &hi);
       const unsigned long long nv = (hi - lo) / 16;
-      constexpr int U = 4;
       for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
         uint4 x[U];
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          if (v + u * half < nv) x[u] = ld_reduce(mbuf + lo + (v + u * half) * 16, a.dtype);
+          if (v + u * half < nv) x[u] = ld_reduce(mbuf + lo + (v + u * half) * 16, DT);
 #pragma unroll
         for (int u = 0; u < U; ++u)
           if (v + u * half < nv)
-            mc_store(mbuf + lo + (v + u * half) * 16, a.avg ? scale(x[u], a.dtype, inv) : x[u]);
+            mc_store(mbuf + lo + (v + u * half) * 16, a.avg ? scale(x[u], DT, inv) : x[u]);
       }
     }
     // Barrier: this block's counterparts on every GPU finished step s.
@@ -252,14 +255,15 @@ __device__ __forceinline__ bool nvls_barrier(const NvlsArgs& a, unsigned long lo
 //    the round buffer; every GPU copies round s-1 (all parts) out.
 //  ReduceScatter: every GPU copies round s of its input in; every rank
 //    multimem.ld_reduces its own part of round s-1 straight into its output.
-__global__ void __launch_bounds__(1024, 1) nvls_xfer_kernel(const __grid_constant__ NvlsArgs a) {
+template <int U, int DT>
+__global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant__ NvlsArgs a) {
   __shared__ int abort_flag;
   if (threadIdx.x == 0) abort_flag = 0;
   __syncthreads();
   const int n = a.nranks;
-  const int half = blockDim.x / 2;
-  const bool mover = threadIdx.x < half;  // switch-side warps
-  const int t = mover ? threadIdx.x : threadIdx.x - half;
+  const bool mover = int(threadIdx.x) < a.movers;  // switch-side warps
+  const int t = mover ? threadIdx.x : threadIdx.x - a.movers;
+  const int half = mover ? a.movers : int(blockDim.x) - a.movers;  // this group's size
   const float inv = 1.0f / float(n);
   const bool bc = a.mode == int(Kind::Broadcast);
   const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)n) & ~15ull);
@@ -281,17 +285,16 @@ __global__ void __launch_bounds__(1024, 1) nvls_xfer_kernel(const __grid_constan
         unsigned long long lo, hi;
         flat_portion(plen, &lo, &hi);
         const unsigned long long nv = (hi - lo) / 16;
-        constexpr int U = 4;
         for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
           uint4 x[U];
 #pragma unroll
           for (int u = 0; u < U; ++u)
-            if (v + u * half < nv) x[u] = ld_reduce(mbuf + lo + (v + u * half) * 16, a.dtype);
+            if (v + u * half < nv) x[u] = ld_reduce(mbuf + lo + (v + u * half) * 16, DT);
 #pragma unroll
           for (int u = 0; u < U; ++u)
             if (v + u * half < nv)
               __stcs(reinterpret_cast<uint4*>(a.recv + i * part + lo) + v + u * half,
-                     a.avg ? scale(x[u], a.dtype, inv) : x[u]);
+                     a.avg ? scale(x[u], DT, inv) : x[u]);
         }
       }
     } else {
@@ -314,7 +317,6 @@ __global__ void __launch_bounds__(1024, 1) nvls_xfer_kernel(const __grid_constan
         unsigned long long lo, hi;
         flat_portion(plen, &lo, &hi);
         const unsigned long long nv = (hi - lo) / 16;
-        constexpr int U = 4;
         for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
           uint4 x[U];
 #pragma unroll
@@ -331,6 +333,26 @@ __global__ void __launch_bounds__(1024, 1) nvls_xfer_kernel(const __grid_constan
 }
 
 // ------------------------------------------------------------------ host side
+
+template <int U>
+const void* pick_dtype(bool ar, DType t) {
+  constexpr int F = int(DType::F32), B = int(DType::BF16), H = int(DType::F16);
+  switch (t) {
+    case DType::BF16:
+      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, B>)
+                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, B>);
+    case DType::F16:
+      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, H>)
+                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, H>);
+    default:  // fp32, and the raw 16-byte copies of AllGather/Broadcast
+      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, F>)
+                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, F>);
+  }
+}
+
+const void* pick_kernel(bool ar, bool u8, DType t) {
+  return u8 ? pick_dtype<8>(ar, t) : pick_dtype<4>(ar, t);
+}
 
 template <typename Fn>
 Fn drv(const char* name) {
@@ -576,10 +598,12 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
     steps = (plan.desc.bytes + part - 1) / part + 1;
     if (!bc && part == 0) return cudaErrorInvalidValue;
   }
+  const int threads = p.nvls_threads;
+  a.movers = std::min(p.nvls_movers, threads - 128);
   void* argv[] = {&a};
-  const void* fn = ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel)
-                      : reinterpret_cast<const void*>(nvls_xfer_kernel);
-  const cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(1024), argv, 0, s);
+  const void* fn = pick_kernel(ar, p.nvls_unroll >= 8, plan.desc.dtype);
+  const cudaError_t e =
+      cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(unsigned(threads)), argv, 0, s);
   if (r == b.nranks - 1) c->barriers += steps;
   return e;
 }
