@@ -113,20 +113,55 @@ __device__ __forceinline__ uint4 scale(uint4 v, int dtype, float inv) {
 // boundaries are 16-byte aligned (the message is a multiple of 16 bytes).
 __device__ __forceinline__ void portion(unsigned long long rlen, int n, int q, unsigned long long* lo,
                                         unsigned long long* hi) {
-  const unsigned long long base = (rlen / (unsigned long long)n) & ~15ull;
+  // Slices and block parts start on 32-byte boundaries (the copiers' vector).
+  const unsigned long long base = (rlen / (unsigned long long)n) & ~31ull;
   const unsigned long long soff = base * (unsigned long long)q;
   const unsigned long long slen = q == n - 1 ? rlen - soff : base;
-  const unsigned long long per = ((slen + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+  const unsigned long long per = ((slen + gridDim.x - 1) / gridDim.x + 31) & ~31ull;
   const unsigned long long a = min(slen, per * blockIdx.x), b = min(slen, a + per);
   *lo = soff + a;
   *hi = soff + b;
 }
 
-// Copy `bytes` with the `nthreads` threads of a warp group (thread index t).
+struct V32 {
+  uint4 lo, hi;
+};
+__device__ __forceinline__ V32 ld32(const void* p) {
+  V32 v;
+  asm volatile("ld.global.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.lo.x), "=r"(v.lo.y), "=r"(v.lo.z), "=r"(v.lo.w), "=r"(v.hi.x), "=r"(v.hi.y),
+                 "=r"(v.hi.z), "=r"(v.hi.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st32(void* p, const V32& v) {
+  asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.lo.x), "r"(v.lo.y),
+               "r"(v.lo.z), "r"(v.lo.w), "r"(v.hi.x), "r"(v.hi.y), "r"(v.hi.z), "r"(v.hi.w)
+               : "memory");
+}
+
+// Copy `bytes` (a multiple of 16) with the `nthreads` threads of a warp group
+// (thread index t): 32-byte vectors when both ends allow, else 16-byte.
 __device__ __forceinline__ void copy16(char* dst, const char* src, unsigned long long bytes, int t,
                                        int nthreads) {
-  const unsigned long long nv = bytes / 16;
   constexpr int U = 4;
+  unsigned long long done = 0;
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 31) == 0) {
+    const unsigned long long nv = bytes / 32;
+    for (unsigned long long i = t; i < nv; i += (unsigned long long)nthreads * U) {
+      V32 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i + u * nthreads < nv) v[u] = ld32(src + (i + u * nthreads) * 32);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i + u * nthreads < nv) st32(dst + (i + u * nthreads) * 32, v[u]);
+    }
+    done = nv * 32;
+  }
+  const unsigned long long nv = (bytes - done) / 16;
+  src += done;
+  dst += done;
   for (unsigned long long i = t; i < nv; i += (unsigned long long)nthreads * U) {
     uint4 v[U];
 #pragma unroll
@@ -221,7 +256,7 @@ __global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_con
 // This block's part [lo, hi) of a flat range of `len` bytes (16-byte units).
 __device__ __forceinline__ void flat_portion(unsigned long long len, unsigned long long* lo,
                                              unsigned long long* hi) {
-  const unsigned long long per = ((len + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+  const unsigned long long per = ((len + gridDim.x - 1) / gridDim.x + 31) & ~31ull;
   *lo = min(len, per * blockIdx.x);
   *hi = min(len, *lo + per);
 }
@@ -266,7 +301,7 @@ __global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant
   const int half = mover ? a.movers : int(blockDim.x) - a.movers;  // this group's size
   const float inv = 1.0f / float(n);
   const bool bc = a.mode == int(Kind::Broadcast);
-  const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)n) & ~15ull);
+  const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)n) & ~31ull);
   const unsigned long long total = bc ? a.bytes : a.slot;
   const unsigned long long rounds = (total + part - 1) / part;
   for (unsigned long long s = 0; s < rounds + 1; ++s) {
@@ -594,7 +629,7 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
     steps = (a.bytes + a.round - 1) / a.round + 2;
   } else {
     const bool bc = plan.desc.kind == Kind::Broadcast;
-    const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)b.nranks) & ~15ull);
+    const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)b.nranks) & ~31ull);
     steps = (plan.desc.bytes + part - 1) / part + 1;
     if (!bc && part == 0) return cudaErrorInvalidValue;
   }
