@@ -78,3 +78,53 @@ def plan(algo, kind, sends, recvs, op="sum", root=0, ce_ppm=0, scalars=None, cou
 
 def kernel_launches() -> int:
     return int(lib().nb_kernel_launches())
+
+
+def bench(kernel: str, n: int, mib: int, dtype: str = "float32", ndst: int = 1, iters: int = 20,
+          warmup: int = 3) -> dict:
+    """Time one kernel on virtual-rank buffers of the current device with CUDA
+    events: `reduce` folds n sources of `mib` MiB into ndst destinations;
+    `copy` moves n segments of `mib` MiB. Total sources exceed the 126 MB L2
+    for the default sizes, so every launch streams from HBM."""
+    import torch
+    dt = getattr(torch, dtype)
+    es = torch.tensor([], dtype=dt).element_size()
+    count = (mib << 20) // es
+    srcs = [torch.randn(count, device="cuda").to(dt) for _ in range(n)]
+    if kernel == "reduce":
+        dsts = [torch.empty_like(srcs[0]) for _ in range(ndst)]
+        run = lambda: reduce(srcs, dsts)  # noqa: E731
+        moved = (n + ndst) * count * es
+    elif kernel == "copy":
+        dsts = [torch.empty_like(s) for s in srcs]
+        run = lambda: copy(srcs, dsts, [count * es] * n)  # noqa: E731
+        moved = 2 * n * count * es
+    else:
+        raise ValueError(kernel)
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        run()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    return {"kernel": kernel, "n": n, "mib": mib, "dtype": dtype, "ndst": ndst,
+            "ms": round(ms, 4), "hbm_gbs": round(moved / ms / 1e6, 1)}
+
+
+if __name__ == "__main__":
+    import argparse
+    import json
+    p = argparse.ArgumentParser(description="time one sm_100a collective kernel on one GPU")
+    p.add_argument("--kernel", choices=["reduce", "copy"], default="reduce")
+    p.add_argument("--n", type=int, default=8)
+    p.add_argument("--mib", type=int, default=64)
+    p.add_argument("--dtype", default="float32")
+    p.add_argument("--ndst", type=int, default=1)
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    a = p.parse_args()
+    print(json.dumps(bench(a.kernel, a.n, a.mib, a.dtype, a.ndst, a.iters, a.warmup)))

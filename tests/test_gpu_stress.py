@@ -1,0 +1,48 @@
+"""The back-to-back stress harness (scc26_nccl_shim_b200.parallel.stress) on
+the GPUs this run sees: every standard and boundary case must PASS with no
+guard damage, and the checker mutation self-test must make cases FAIL."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+from conftest import REPO, gpu_count, need_gpus
+
+pytestmark = pytest.mark.gpu
+
+
+def run(args, env=None):
+    r = subprocess.run([sys.executable, "-m", "scc26_nccl_shim_b200.parallel.stress", *args],
+                       cwd=REPO, env=dict(os.environ, **(env or {})), capture_output=True, text=True,
+                       timeout=900)
+    rows = [l.split("\t") for l in r.stdout.splitlines()[1:] if "\t" in l]
+    return r.returncode, rows, r.stdout + r.stderr[-3000:]
+
+
+def test_stress_all_cases_pass():
+    need_gpus(1)
+    n = min(2, gpu_count())
+    rc, rows, log = run(["--gpus", str(n), "--iters", "3", "--scale", "4"])
+    assert rc == 0, log
+    assert rows and all(r[4] == "PASS" and r[5] == "0" for r in rows), log
+    # The eligible large cases ran on the interposer's own routes.
+    custom = {r[0] for r in rows if r[6] == "custom"}
+    assert any(c.startswith("allreduce_float32") for c in custom), log
+    assert "allreduce_max_fallback" in {r[0] for r in rows}
+
+
+def test_stress_checker_mutation_fails():
+    need_gpus(1)
+    n = min(2, gpu_count())
+    rc, rows, log = run(["--gpus", str(n), "--iters", "2", "--scale", "8", "--corrupt-shift", "3",
+                         "--filter", "float32_oop", "--no-boundary"])
+    assert rc != 0, log
+    assert rows and all(r[4] == "FAIL" for r in rows), log
+
+
+def test_stress_differential_against_stock_nccl():
+    need_gpus(2)
+    rc, rows, log = run(["--gpus", "2", "--iters", "2", "--scale", "8", "--diff", "--no-boundary",
+                         "--filter", "oop"])
+    assert rc == 0, log
