@@ -215,6 +215,7 @@ def worker(args) -> int:
         for _ in range(args.warmup):
             collective(nc, kind, sends, recvs, comms, streams)
         sync_all()
+        nvls_trace(nc, devs, kind, reset_only=True)
         l0 = nc.kernel_launches()
         starts = [torch.cuda.Event(enable_timing=True) for _ in devs]
         stops = [torch.cuda.Event(enable_timing=True) for _ in devs]
@@ -232,6 +233,7 @@ def worker(args) -> int:
         if sampler:
             clocks = sampler.stop()
         ms = max(starts[i].elapsed_time(stops[i]) for i in range(n)) / args.steps
+        nvls_trace(nc, devs, kind, steps=args.steps)
         l1 = nc.kernel_launches()
         if kind == "allreduce" and l0 is not None:
             launches = l1 - l0
@@ -299,6 +301,26 @@ def worker(args) -> int:
         sys.stderr.write(nc.summary_text())
     print(json.dumps(line), flush=True)
     return 0
+
+
+def nvls_trace(nc, devs, kind, reset_only=False, steps=1):
+    """With NCCL_B200_NVLS_TRACE=1: the NVLS kernels' per-block phase times
+    (mean over blocks, per call) of every rank, to stderr. Read outside the
+    timed region (it synchronizes the devices)."""
+    import ctypes as C
+    if not os.environ.get("NCCL_B200_NVLS_TRACE") or nc.shim is None or \
+            not hasattr(nc.shim, "nb_nvls_trace"):
+        return
+    n = len(devs)
+    arr = (C.c_int * n)(*devs)
+    for r in range(n):
+        out = (C.c_double * 4)()
+        blocks = nc.shim.nb_nvls_trace(arr, n, r, out, 1)
+        if reset_only or blocks <= 0:
+            continue
+        ms = [v / 1e6 / steps for v in out]
+        sys.stderr.write(f"nvls_trace {kind} rank={r} blocks={blocks} per_call_ms mover={ms[0]:.3f} "
+                         f"copier={ms[1]:.3f} barrier_wait={ms[2]:.3f} total={ms[3]:.3f}\n")
 
 
 def end_to_end(torch, nc, comms, sends, recvs, streams, devs, count, args):

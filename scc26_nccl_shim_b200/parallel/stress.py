@@ -40,6 +40,7 @@ from dataclasses import dataclass
 
 import torch
 
+from .._core import ALGO, policy_value
 from ..utils.data import adversarial, exact
 from .nccl import Nccl, collective
 
@@ -82,15 +83,16 @@ def standard_cases(n: int, scale: int = 1) -> list[Case]:
     return cases
 
 
-def boundary_cases(n: int, threshold_bytes: int) -> list[Case]:
-    """Element counts at -1, 0, +1 around the routing threshold."""
+def boundary_cases(n: int, thresholds: dict) -> list[Case]:
+    """Element counts at -1, 0, +1 around each kind's routing threshold
+    (AllGather's applies to the whole output, so to n slots)."""
     out = []
     for kind in ("allreduce", "broadcast", "allgather"):
         for d in (-1, 0, 1):
             if kind == "allgather":
-                c = threshold_bytes // 4 // n + d
+                c = thresholds[kind] // 4 // n + d
             else:
-                c = threshold_bytes // 4 + d
+                c = thresholds[kind] // 4 + d
             out.append(Case(f"bnd_{kind}_{d:+d}", kind, "float32", c))
     return out
 
@@ -116,6 +118,18 @@ class Buffers:
         for raw in (self.send_raw, self.recv_raw):
             bad += (raw[:GUARD] != PATTERN).sum() + (raw[-GUARD:] != PATTERN).sum()
         return bad
+
+
+def custom_total(nc: Nccl) -> int:
+    return sum(nc.custom_calls(a) or 0 for a in range(1, len(ALGO)))
+
+
+def thresholds() -> dict:
+    """Per-kind routing thresholds (bytes) as the library's policy parser
+    reads them from this process's environment."""
+    env = {k: v for k, v in os.environ.items() if k.startswith("NCCL_B200_")}
+    return {kind: int(policy_value(env, f"{key}_min"))
+            for kind, key in (("allreduce", "ar"), ("allgather", "ag"), ("broadcast", "bc"))}
 
 
 def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, seed: int,
@@ -145,7 +159,7 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
         return b.send(), b.send()
 
     mism = [torch.zeros((), dtype=torch.int64, device=f"cuda:{d}") for d in devs]
-    custom_before = sum(nc.custom_calls(a) or 0 for a in range(1, 16))
+    custom_before = custom_total(nc)
     shadows = None
     if diff and ref is not None:
         shadows = [torch.empty(recv_elems, dtype=dtype, device=f"cuda:{d}") for d in devs]
@@ -190,7 +204,7 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
         torch.cuda.synchronize(d)
     total = int(sum(m.item() for m in mism))
     guard = int(sum(b.guard_bad().item() for b in bufs))
-    custom = sum(nc.custom_calls(a) or 0 for a in range(1, 16)) > custom_before
+    custom = custom_total(nc) > custom_before
     return {"case": case.name, "iters": iters, "bytes": c * es, "mismatches": total,
             "status": "PASS" if total == 0 and guard == 0 else "FAIL", "guard_bad": guard,
             "route": "custom" if custom else "nccl", "kind": case.kind,
@@ -238,8 +252,7 @@ def main(argv=None) -> int:
     comms = nc.comm_init_all(devs)
     cases = standard_cases(len(devs), a.scale)
     if not a.no_boundary:
-        thr = int(os.environ.get("NCCL_B200_AR_MIN_BYTES_HINT", 32 << 20))
-        cases += boundary_cases(len(devs), thr)
+        cases += boundary_cases(len(devs), thresholds())
     if a.filter:
         cases = [c for c in cases if a.filter in c.name]
     # Warm-up: the first eligible call of the process always runs on NCCL.

@@ -21,7 +21,7 @@ MASK64 = (1 << 64) - 1
 
 def _mix64(z: torch.Tensor) -> torch.Tensor:
     # splitmix64 on int64 tensors (arithmetic wraps modulo 2^64).
-    z = z + 0x9E3779B97F4A7C15 - (1 << 64)
+    z = z + (0x9E3779B97F4A7C15 - (1 << 64))
     z = (z ^ (z >> 30) & 0x3FFFFFFFF) * (0xBF58476D1CE4E5B9 - (1 << 64))
     z = (z ^ (z >> 27) & 0x1FFFFFFFFF) * (0x94D049BB133111EB - (1 << 64))
     return z ^ (z >> 31) & 0x1FFFFFFFF

@@ -14,6 +14,7 @@
 // symbol resolution, version gate, call model, group buffering, pair
 // registry, init interposers with prewarm, runtime checks, pair runner,
 // GroupEnd with device restore, and the passthrough wrappers.
+#include <nvtx3/nvToolsExt.h>
 #include <dlfcn.h>
 
 #include <cstddef>
@@ -315,7 +316,16 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
     return Outcome::Fallback;
   }
   cudaError_t error = cudaSuccess;
+  // Optional NVTX range around the submission (NCCL_B200_NVTX=1), named by
+  // route, rank count and logical bytes, for timeline tools.
+  if (r.policy.nvtx) {
+    char label[96];
+    std::snprintf(label, sizeof label, "nccl-b200 %s n=%d bytes=%zu", algo_name(d.algo), n,
+                  logical_bytes(descs[0]));
+    nvtxRangePushA(label);
+  }
   const ExecStatus status = r.exec.execute(plan, b, &error, &r.fault);
+  if (r.policy.nvtx) nvtxRangePop();
   if (status == ExecStatus::Failed) {
     r.poisoned = true;
     if (error == cudaErrorLaunchTimeout) r.summary.count_timeout();  // a bounded wait ran out
@@ -707,6 +717,9 @@ size_t nb_summary_text(char* buf, size_t cap) {
 }
 int nb_nvls_supported(const int* devices, int n) { return nvls_supported(devices, n) ? 1 : 0; }
 unsigned nb_nvls_status(const int* devices, int n) { return nvls_status(devices, n); }
+int nb_nvls_trace(const int* devices, int n, int rank, double* out4, int reset) {
+  return nvls_trace_read(devices, n, rank, out4, reset != 0);
+}
 
 // The tuned route of a collective kind on cliques of n ranks (-1 untuned).
 int nb_route(int n, int kind) {

@@ -31,6 +31,8 @@ struct Policy {
   int nvls_threads = 768;           // threads per block of the NVLS kernels
   int nvls_movers = 512;            // of those: switch-side workers (the rest copy)
   int nvls_unroll = 4;              // multimem requests in flight per switch-side thread
+  bool nvls_trace = false;          // per-block phase timing in the NVLS kernels
+  bool nvtx = false;                // NVTX range per custom submission
   Algo force_algo[size_t(Kind::Count)] = {Algo::Fallback, Algo::Fallback, Algo::Fallback,
                                           Algo::Fallback};  // Fallback = choose
   // Shares in parts per 10000 of the bytes each GPU receives. Negative =

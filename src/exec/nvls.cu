@@ -56,6 +56,7 @@ struct NvlsArgs {
   int mode;                  // collective kind (xfer kernel)
   int root;                  // Broadcast
   unsigned long long slot;   // AllGather / ReduceScatter per-rank slot bytes
+  unsigned long long* trace; // per-block phase timing record, or null
 };
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -140,37 +141,120 @@ __device__ __forceinline__ void st32(void* p, const V32& v) {
                : "memory");
 }
 
-// Copy `bytes` (a multiple of 16) with the `nthreads` threads of a warp group
-// (thread index t): 32-byte vectors when both ends allow, else 16-byte.
+// Copy `bytes` (a multiple of 16, below 4 GiB) with the `nthreads` threads of
+// a warp group (thread index t): 32-byte vectors, U in flight per thread,
+// when both ends allow; else 16-byte vectors. Full groups of U run without
+// predicates; 32-bit indices keep the loop within the 768-thread register
+// budget (80 per thread).
 __device__ __forceinline__ void copy16(char* dst, const char* src, unsigned long long bytes, int t,
                                        int nthreads) {
   constexpr int U = 4;
-  unsigned long long done = 0;
+  unsigned n32 = 0;
   if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 31) == 0) {
-    const unsigned long long nv = bytes / 32;
-    for (unsigned long long i = t; i < nv; i += (unsigned long long)nthreads * U) {
+    n32 = unsigned(bytes / 32);
+    const unsigned nt = unsigned(nthreads);
+    unsigned i = unsigned(t);
+    for (; i + nt * (U - 1) < n32; i += nt * U) {
       V32 v[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (i + u * nthreads < nv) v[u] = ld32(src + (i + u * nthreads) * 32);
+      for (int u = 0; u < U; ++u) v[u] = ld32(src + size_t(i + u * nt) * 32);
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (i + u * nthreads < nv) st32(dst + (i + u * nthreads) * 32, v[u]);
+      for (int u = 0; u < U; ++u) st32(dst + size_t(i + u * nt) * 32, v[u]);
     }
-    done = nv * 32;
+    for (; i < n32; i += nt) st32(dst + size_t(i) * 32, ld32(src + size_t(i) * 32));
   }
-  const unsigned long long nv = (bytes - done) / 16;
-  src += done;
-  dst += done;
-  for (unsigned long long i = t; i < nv; i += (unsigned long long)nthreads * U) {
-    uint4 v[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (i + u * nthreads < nv) v[u] = __ldcs(reinterpret_cast<const uint4*>(src) + i + u * nthreads);
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (i + u * nthreads < nv) __stcs(reinterpret_cast<uint4*>(dst) + i + u * nthreads, v[u]);
+  const size_t done = size_t(n32) * 32;
+  const unsigned n16 = unsigned((bytes - done) / 16);
+  const uint4* s16 = reinterpret_cast<const uint4*>(src + done);
+  uint4* d16 = reinterpret_cast<uint4*>(dst + done);
+  const unsigned nt = unsigned(nthreads);
+  unsigned i = unsigned(t);
+  for (; i + nt < n16; i += 2 * nt) {
+    const uint4 a = __ldcs(s16 + i), b = __ldcs(s16 + i + nt);
+    __stcs(d16 + i, a);
+    __stcs(d16 + i + nt, b);
   }
+  if (i < n16) __stcs(d16 + i, __ldcs(s16 + i));
+}
+
+// Calls st(i, ld(i)) for i = t, t + nt, ... below n, with the U loads of a
+// group issued before its U stores (U requests in flight per thread).
+template <int U, typename Ld, typename St>
+__device__ __forceinline__ void strided(unsigned t, unsigned nt, unsigned n, Ld ld, St st) {
+  unsigned i = t;
+  for (; i + nt * (U - 1) < n; i += nt * U) {
+    uint4 x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) x[u] = ld(i + u * nt);
+#pragma unroll
+    for (int u = 0; u < U; ++u) st(i + u * nt, x[u]);
+  }
+  for (; i < n; i += nt) st(i, ld(i));
+}
+
+// Optional per-block phase timing (NCCL_B200_NVLS_TRACE): per step, the time
+// until the last warp of each group finished its work and the time spent in
+// the cross-GPU barrier, accumulated over the call and added to a per-block
+// record {mover busy, copier busy, barrier wait, total} in nanoseconds.
+// The state lives in shared memory, so tracing costs no registers.
+struct Tracer {
+  // Shared: [0] latest mover finish, [1] latest copier finish, [2] step
+  // start, [3..6] accumulated mover busy, copier busy, barrier wait, total.
+  unsigned long long* sh;
+  bool on;
+  __device__ Tracer(unsigned long long* shared, bool enabled) : sh(shared), on(enabled) {
+    if (on && threadIdx.x == 0) {
+      for (int k = 0; k < 7; ++k) sh[k] = 0;
+      sh[2] = globaltimer();
+    }
+  }
+  __device__ void group_done(bool mover_group) {
+    if (!on) return;
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) atomicMax(&sh[mover_group ? 0 : 1], globaltimer());
+  }
+  // Thread 0 only, between the two __syncthreads of a barrier.
+  __device__ void step(unsigned long long t_sync, unsigned long long t_end) {
+    if (!on) return;
+    const unsigned long long t0 = sh[2];
+    sh[3] += sh[0] > t0 ? sh[0] - t0 : 0;
+    sh[4] += sh[1] > t0 ? sh[1] - t0 : 0;
+    sh[5] += t_end - t_sync;
+    sh[6] += t_end - t0;
+    sh[2] = t_end;
+    sh[0] = sh[1] = 0;
+  }
+  __device__ void flush(const NvlsArgs& a) {
+    if (!on || threadIdx.x != 0) return;
+    unsigned long long* rec = a.trace + 4ull * blockIdx.x;
+    for (int k = 0; k < 4; ++k) rec[k] += sh[3 + k];
+  }
+};
+
+// Cross-GPU barrier of step s for this block: every GPU's block of the same
+// index finished step s. Bounded by %globaltimer: on expiry the status word
+// in mapped host memory is set and every thread of the block returns false.
+__device__ __forceinline__ bool nvls_barrier(const NvlsArgs& a, unsigned long long s, int* abort_flag,
+                                             Tracer& tr) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long t_sync = tr.on ? globaltimer() : 0;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    mc_arrive(a.mc_flags + blockIdx.x);
+    const unsigned target = a.base + unsigned(a.nranks) * unsigned(s + 1);
+    const unsigned long long start = globaltimer();
+    while (int(ld_acquire(a.uc_flags + blockIdx.x) - target) < 0) {
+      if (globaltimer() - start > a.timeout_ns) {
+        *reinterpret_cast<volatile unsigned*>(a.status) = 1u;  // mapped host word
+        __threadfence_system();
+        *abort_flag = 1;
+        break;
+      }
+    }
+    tr.step(t_sync, tr.on ? globaltimer() : 0);
+  }
+  __syncthreads();
+  return *abort_flag == 0;
 }
 
 // Warp specialization: the first half of the block's warps reduce through
@@ -180,7 +264,9 @@ __device__ __forceinline__ void copy16(char* dst, const char* src, unsigned long
 template <int U, int DT>
 __global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
   __shared__ int abort_flag;
+  __shared__ unsigned long long trace_sh[7];
   if (threadIdx.x == 0) abort_flag = 0;
+  Tracer tr(trace_sh, a.trace != nullptr);
   __syncthreads();
   const int n = a.nranks;
   const unsigned long long rounds = (a.bytes + a.round - 1) / a.round;
@@ -220,37 +306,17 @@ __global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_con
       char* mbuf = a.mc + (i % 3) * a.buf_stride;
       unsigned long long lo, hi;
       portion(rlen, n, a.rank, &lo, &hi);
-      const unsigned long long nv = (hi - lo) / 16;
-      for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
-        uint4 x[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (v + u * half < nv) x[u] = ld_reduce(mbuf + lo + (v + u * half) * 16, DT);
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (v + u * half < nv)
-            mc_store(mbuf + lo + (v + u * half) * 16, a.avg ? scale(x[u], DT, inv) : x[u]);
-      }
+      char* base = mbuf + lo;
+      strided<U>(
+          unsigned(t), unsigned(half), unsigned((hi - lo) / 16),
+          [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
+          [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, a.avg ? scale(x, DT, inv) : x); });
     }
     // Barrier: this block's counterparts on every GPU finished step s.
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
-      mc_arrive(a.mc_flags + blockIdx.x);
-      const unsigned target = a.base + unsigned(n) * unsigned(s + 1);
-      const unsigned long long start = globaltimer();
-      while (int(ld_acquire(a.uc_flags + blockIdx.x) - target) < 0) {
-        if (globaltimer() - start > a.timeout_ns) {
-          *reinterpret_cast<volatile unsigned*>(a.status) = 1u;  // mapped host word
-          __threadfence_system();
-          abort_flag = 1;
-          break;
-        }
-      }
-    }
-    __syncthreads();
-    if (abort_flag) return;
+    tr.group_done(reducer);
+    if (!nvls_barrier(a, s, &abort_flag, tr)) return;
   }
+  tr.flush(a);
 }
 
 // This block's part [lo, hi) of a flat range of `len` bytes (16-byte units).
@@ -261,25 +327,6 @@ __device__ __forceinline__ void flat_portion(unsigned long long len, unsigned lo
   *hi = min(len, *lo + per);
 }
 
-__device__ __forceinline__ bool nvls_barrier(const NvlsArgs& a, unsigned long long s, int* abort_flag) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    mc_arrive(a.mc_flags + blockIdx.x);
-    const unsigned target = a.base + unsigned(a.nranks) * unsigned(s + 1);
-    const unsigned long long start = globaltimer();
-    while (int(ld_acquire(a.uc_flags + blockIdx.x) - target) < 0) {
-      if (globaltimer() - start > a.timeout_ns) {
-        *reinterpret_cast<volatile unsigned*>(a.status) = 1u;
-        __threadfence_system();
-        *abort_flag = 1;
-        break;
-      }
-    }
-  }
-  __syncthreads();
-  return *abort_flag == 0;
-}
 
 // Broadcast / AllGather / ReduceScatter through the switch, with the same
 // three-buffer scratch, per-block bounded barriers and warp split as the
@@ -293,7 +340,9 @@ __device__ __forceinline__ bool nvls_barrier(const NvlsArgs& a, unsigned long lo
 template <int U, int DT>
 __global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant__ NvlsArgs a) {
   __shared__ int abort_flag;
+  __shared__ unsigned long long trace_sh[7];
   if (threadIdx.x == 0) abort_flag = 0;
+  Tracer tr(trace_sh, a.trace != nullptr);
   __syncthreads();
   const int n = a.nranks;
   const bool mover = int(threadIdx.x) < a.movers;  // switch-side warps
@@ -319,18 +368,12 @@ __global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant
         const char* mbuf = a.mc + (i % 3) * a.buf_stride + a.rank * part;
         unsigned long long lo, hi;
         flat_portion(plen, &lo, &hi);
-        const unsigned long long nv = (hi - lo) / 16;
-        for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
-          uint4 x[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (v + u * half < nv) x[u] = ld_reduce(mbuf + lo + (v + u * half) * 16, DT);
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (v + u * half < nv)
-              __stcs(reinterpret_cast<uint4*>(a.recv + i * part + lo) + v + u * half,
-                     a.avg ? scale(x[u], DT, inv) : x[u]);
-        }
+        const char* base = mbuf + lo;
+        uint4* out = reinterpret_cast<uint4*>(a.recv + i * part + lo);
+        strided<U>(
+            unsigned(t), unsigned(half), unsigned((hi - lo) / 16),
+            [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
+            [&](unsigned v, uint4 x) { __stcs(out + v, a.avg ? scale(x, DT, inv) : x); });
       }
     } else {
       if (!mover && s >= 1) {  // C(s-1): copy round s-1 out
@@ -351,20 +394,18 @@ __global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant
         const char* src = a.send + s * part;
         unsigned long long lo, hi;
         flat_portion(plen, &lo, &hi);
-        const unsigned long long nv = (hi - lo) / 16;
-        for (unsigned long long v = t; v < nv; v += (unsigned long long)half * U) {
-          uint4 x[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (v + u * half < nv) x[u] = __ldcs(reinterpret_cast<const uint4*>(src + lo) + v + u * half);
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (v + u * half < nv) mc_store(mbuf + lo + (v + u * half) * 16, x[u]);
-        }
+        const uint4* in = reinterpret_cast<const uint4*>(src + lo);
+        char* base = mbuf + lo;
+        strided<U>(
+            unsigned(t), unsigned(half), unsigned((hi - lo) / 16),
+            [&](unsigned v) { return __ldcs(in + v); },
+            [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, x); });
       }
     }
-    if (!nvls_barrier(a, s, &abort_flag)) return;
+    tr.group_done(mover);
+    if (!nvls_barrier(a, s, &abort_flag, tr)) return;
   }
+  tr.flush(a);
 }
 
 // ------------------------------------------------------------------ host side
@@ -451,6 +492,7 @@ struct Context {
   unsigned* status = nullptr;  // mapped pinned host word
   unsigned* status_dev = nullptr;
   unsigned long long barriers = 0;  // per-block barriers run so far on this scratch
+  std::vector<unsigned long long*> trace;  // per device: blocks x 4 phase-time records
   int blocks = 0;
   bool broken = false;
 };
@@ -578,6 +620,11 @@ bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why
     c->mc.push_back(reinterpret_cast<char*>(mv));
     if (cudaMemset(reinterpret_cast<char*>(uc) + 3 * stride, 0, flags_bytes) != cudaSuccess)
       return fail("flag init");
+    unsigned long long* tr = nullptr;
+    const size_t tr_bytes = size_t(blocks) * 4 * sizeof(unsigned long long);
+    if (cudaMalloc(&tr, tr_bytes) != cudaSuccess || cudaMemset(tr, 0, tr_bytes) != cudaSuccess)
+      return fail("trace records");
+    c->trace.push_back(tr);
   }
   for (int i = 0; i < n; ++i)
     if (cudaSetDevice(devices[i]) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
@@ -621,6 +668,7 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.mode = int(plan.desc.kind);
   a.root = plan.desc.root;
   a.slot = plan.desc.bytes;  // AG send slot / RS receive slot
+  a.trace = p.nvls_trace ? c->trace[size_t(r)] : nullptr;
   (void)dev;
   const bool ar = plan.desc.kind == Kind::AllReduce;
   // Barriers this call runs (one per step); every rank runs the same count.
@@ -641,6 +689,27 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
       cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(unsigned(threads)), argv, 0, s);
   if (r == b.nranks - 1) c->barriers += steps;
   return e;
+}
+
+int nvls_trace_read(const int* devices, int n, int rank, double out[4], bool reset) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Context* c = find(devices, n);
+  if (!c || rank < 0 || rank >= n) return -1;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(devices[rank]) != cudaSuccess) return -1;
+  std::vector<unsigned long long> rec(size_t(c->blocks) * 4);
+  const size_t bytes = rec.size() * sizeof(unsigned long long);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(rec.data(), c->trace[size_t(rank)], bytes, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && reset) e = cudaMemset(c->trace[size_t(rank)], 0, bytes);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return -1;
+  for (int k = 0; k < 4; ++k) {
+    double sum = 0;
+    for (int b = 0; b < c->blocks; ++b) sum += double(rec[size_t(b) * 4 + size_t(k)]);
+    out[k] = sum / double(c->blocks);  // mean over blocks, ns
+  }
+  return c->blocks;
 }
 
 unsigned nvls_status(const int* devices, int n) {

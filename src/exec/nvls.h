@@ -30,5 +30,10 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
 // Device-side status of the last NVLS gang on this device set: 0 ok,
 // nonzero = a bounded wait expired. Reading it synchronizes nothing.
 unsigned nvls_status(const int* devices, int n);
+// Phase timing of one rank's NVLS kernels since the last reset (policy
+// nvls_trace): out = mean over blocks of {mover busy, copier busy, barrier
+// wait, total} in ns. Synchronizes that device. Returns the block count, or
+// -1 without an NVLS context.
+int nvls_trace_read(const int* devices, int n, int rank, double out[4], bool reset);
 
 }  // namespace nb

@@ -35,6 +35,7 @@ def test_mixed_64_call_group_falls_back_in_order():
             count //= n
             count -= count % 8
         calls.append((kind, dtype, op, max(8, count)))
+    assert any(k == "send_recv" for k, *_ in calls)
     bufs = []
     for kind, dtype, op, count in calls:
         per = []

@@ -11,10 +11,15 @@ from conftest import REPO, gpu_count, need_gpus
 
 pytestmark = pytest.mark.gpu
 
+# Small thresholds keep the cases small while they still take the custom
+# routes; tuning is skipped (the routes' defaults are exercised).
+SMALL = {"NCCL_B200_AR_MIN": "4M", "NCCL_B200_AG_MIN": "4M", "NCCL_B200_RS_MIN": "4M",
+         "NCCL_B200_BC_MIN": "4M", "NCCL_B200_TUNE": "0"}
+
 
 def run(args, env=None):
     r = subprocess.run([sys.executable, "-m", "scc26_nccl_shim_b200.parallel.stress", *args],
-                       cwd=REPO, env=dict(os.environ, **(env or {})), capture_output=True, text=True,
+                       cwd=REPO, env=dict(os.environ, **SMALL, **(env or {})), capture_output=True, text=True,
                        timeout=900)
     rows = [l.split("\t") for l in r.stdout.splitlines()[1:] if "\t" in l]
     return r.returncode, rows, r.stdout + r.stderr[-3000:]
