@@ -50,7 +50,19 @@ $(OUT)/libnccl_b200.so: $(LIB_CXX_OBJ) $(LIB_CU_OBJ)
 	@mkdir -p $(OUT)
 	$(NVCC) $(ARCH) -shared --cudart shared -Xcompiler -pthread -o $@ $^ -ldl
 
-clean:
-	rm -rf $(BUILD)/core_only $(BUILD)/lib $(OUT)/libnccl_b200.so $(OUT)/libnb_core.so
+# The core and a randomized self-test under AddressSanitizer + UBSan (CPU);
+# SAN_CXX is a compiler whose runtime ships libasan/libubsan.
+SAN_CXX ?= $(shell command -v /usr/bin/g++ || echo $(CXX))
+SAN := -O1 -g -std=c++17 -Isrc -pthread -fsanitize=address,undefined -fno-sanitize-recover=all \
+       -fno-omit-frame-pointer
+sanitize: $(BUILD)/core_selftest_san
 
-.PHONY: all core clean
+$(BUILD)/core_selftest_san: $(CORE_SRC) src/selftest/core_selftest.cc $(HDRS)
+	@mkdir -p $(BUILD)
+	$(SAN_CXX) $(SAN) -o $@ $(CORE_SRC) src/selftest/core_selftest.cc
+
+clean:
+	rm -rf $(BUILD)/core_only $(BUILD)/lib $(BUILD)/core_selftest_san $(OUT)/libnccl_b200.so \
+	       $(OUT)/libnb_core.so
+
+.PHONY: all core sanitize clean

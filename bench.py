@@ -314,13 +314,14 @@ def nvls_trace(nc, devs, kind, reset_only=False, steps=1):
     n = len(devs)
     arr = (C.c_int * n)(*devs)
     for r in range(n):
-        out = (C.c_double * 4)()
+        out = (C.c_double * 6)()
         blocks = nc.shim.nb_nvls_trace(arr, n, r, out, 1)
         if reset_only or blocks <= 0:
             continue
         ms = [v / 1e6 / steps for v in out]
-        sys.stderr.write(f"nvls_trace {kind} rank={r} blocks={blocks} per_call_ms mover={ms[0]:.3f} "
-                         f"copier={ms[1]:.3f} barrier_wait={ms[2]:.3f} total={ms[3]:.3f}\n")
+        sys.stderr.write(f"nvls_trace {kind} rank={r} blocks={blocks} per_call_ms mover_busy={ms[0]:.3f} "
+                         f"mover_wait={ms[1]:.3f} copier_busy={ms[2]:.3f} copier_wait={ms[3]:.3f} "
+                         f"mover_total={ms[4]:.3f} copier_total={ms[5]:.3f}\n")
 
 
 def end_to_end(torch, nc, comms, sends, recvs, streams, devs, count, args):

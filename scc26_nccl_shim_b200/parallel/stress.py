@@ -79,7 +79,7 @@ def standard_cases(n: int, scale: int = 1) -> list[Case]:
     cases.append(Case("allreduce_int32", "allreduce", "int32", base + 3))
     cases.append(Case("allgather_int8", "allgather", "int8", base // n + 1))
     cases.append(Case("broadcast_root0_int8", "broadcast", "int8", base * 4 + 5, root=0))
-    cases.append(Case("allreduce_max_fallback", "allreduce", "float32", base, op="max"))
+    cases.append(Case("allreduce_max", "allreduce", "float32", base, op="max"))
     return cases
 
 

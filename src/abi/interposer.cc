@@ -717,8 +717,8 @@ size_t nb_summary_text(char* buf, size_t cap) {
 }
 int nb_nvls_supported(const int* devices, int n) { return nvls_supported(devices, n) ? 1 : 0; }
 unsigned nb_nvls_status(const int* devices, int n) { return nvls_status(devices, n); }
-int nb_nvls_trace(const int* devices, int n, int rank, double* out4, int reset) {
-  return nvls_trace_read(devices, n, rank, out4, reset != 0);
+int nb_nvls_trace(const int* devices, int n, int rank, double* out6, int reset) {
+  return nvls_trace_read(devices, n, rank, out6, reset != 0);
 }
 
 // The tuned route of a collective kind on cliques of n ranks (-1 untuned).

@@ -356,10 +356,19 @@ void plan_staged(Builder& b, const CliqueDesc& d, const Shares& s, bool allreduc
   const int n = b.n();
   b.prologue();
   const Policy& p = b.policy();
-  const size_t piece = s.stage_piece ? s.stage_piece : p.stage_piece;
+  size_t piece = s.stage_piece ? s.stage_piece : p.stage_piece;
   const int depth = s.stage_depth ? s.stage_depth : p.stage_depth;
   int ranks[kMaxRanks];
   all_ranks(n, ranks);
+  // A message shorter than one piece stages in pieces of its own (rounded)
+  // size, so the scratch it needs scales with the message.
+  size_t longest = 0;
+  for (int r = 0; r < n; ++r) {
+    size_t off = 0, len = d.bytes;
+    if (allreduce) slice_of(d.bytes, n, r, &off, &len);
+    longest = std::max(longest, len - (n > 1 ? host_share(len, s.host_ppm, p) : 0));
+  }
+  piece = std::max<size_t>(256, std::min(piece, (longest + 255) / 256 * 256));
   if (n > 1) b.plan().needs.temp_bytes = size_t(depth) * size_t(n - 1) * piece;
   for (int r = 0; r < n; ++r) {
     size_t off, len;

@@ -1,25 +1,22 @@
-// NVLS AllReduce: multicast objects over the clique's GPUs and the multimem
-// gang kernel.
+// NVLS collectives: multicast objects over the clique's GPUs and the
+// multimem kernels.
 //
 // Setup (once per device set): one multicast object spans every clique GPU;
 // each GPU binds its own physical scratch (cuMemCreate) into it and maps
 // both a unicast view (its own memory) and a multicast view. The scratch
-// holds three round buffers of R bytes plus one flag word per block.
+// holds three round buffers of R bytes plus progress words per block.
 //
-// Kernel (one per GPU, all launched for the same call form a gang): the
-// message is processed in rounds of R bytes, each cut into N slices; rank r
-// owns slice r. Per round: A) copy this GPU's input round into its scratch
-// (unicast); B) for slice r, multimem.ld_reduce through the multicast view
-// (the switch reads every GPU's scratch and returns the sum, accumulated in
-// fp32 for 16-bit types) and multimem.st of the result (the switch writes it
-// into every GPU's scratch); C) copy the round out of the scratch into the
-// output. Steps are software-pipelined over three buffers: step s runs
-// C(s-2), B(s-1), A(s), then one cross-GPU barrier per block
-// (multimem.red.release.sys increments that block's flag on every GPU; the
-// block waits with ld.acquire until all N arrived). Every wait is bounded by
-// %globaltimer: on expiry the kernel writes a status word in mapped host
-// memory and returns; the host turns it into ncclUnhandledCudaError and
-// disables the route. No TMA, and no multicast TMA, is used.
+// Kernels (one per GPU; those launched for one call form a gang): the
+// message is processed in rounds of R bytes. In a block, mover warps work
+// through the switch (multimem.ld_reduce, accumulating 16-bit types in fp32,
+// and multimem.st, which writes every GPU's scratch) while copier warps
+// stream rounds between the user's buffers and this GPU's scratch. The two
+// groups synchronize only through per-(block, group, rank) progress words,
+// each waiting for exactly the steps it consumes, so neither waits on the
+// other group's unrelated work. Every wait is bounded by %globaltimer: on
+// expiry the kernel writes a status word in mapped host memory and returns;
+// the host turns it into ncclUnhandledCudaError and disables the route. No
+// TMA, and no multicast TMA, is used.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -50,7 +47,8 @@ struct NvlsArgs {
   unsigned long long buf_stride;
   unsigned long long timeout_ns;
   unsigned* status;          // mapped host word: nonzero = a wait expired
-  unsigned base;             // flag value before this call's first barrier
+  unsigned base;             // progress epoch before this call
+  unsigned skew;             // added to every wait target (bounded-wait test only)
   int nranks, rank, dtype, avg;
   int movers;                // threads of a block that work through the switch
   int mode;                  // collective kind (xfer kernel)
@@ -69,10 +67,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
-}
-
-__device__ __forceinline__ void mc_arrive(unsigned* p) {
-  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(1u) : "memory");
 }
 
 __device__ __forceinline__ uint4 ld_reduce(const void* p, int dtype) {
@@ -192,103 +186,164 @@ __device__ __forceinline__ void strided(unsigned t, unsigned nt, unsigned n, Ld 
   for (; i < n; i += nt) st(i, ld(i));
 }
 
-// Optional per-block phase timing (NCCL_B200_NVLS_TRACE): per step, the time
-// until the last warp of each group finished its work and the time spent in
-// the cross-GPU barrier, accumulated over the call and added to a per-block
-// record {mover busy, copier busy, barrier wait, total} in nanoseconds.
-// The state lives in shared memory, so tracing costs no registers.
-struct Tracer {
-  // Shared: [0] latest mover finish, [1] latest copier finish, [2] step
-  // start, [3..6] accumulated mover busy, copier busy, barrier wait, total.
-  unsigned long long* sh;
-  bool on;
-  __device__ Tracer(unsigned long long* shared, bool enabled) : sh(shared), on(enabled) {
-    if (on && threadIdx.x == 0) {
-      for (int k = 0; k < 7; ++k) sh[k] = 0;
-      sh[2] = globaltimer();
-    }
-  }
-  __device__ void group_done(bool mover_group) {
-    if (!on) return;
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) atomicMax(&sh[mover_group ? 0 : 1], globaltimer());
-  }
-  // Thread 0 only, between the two __syncthreads of a barrier.
-  __device__ void step(unsigned long long t_sync, unsigned long long t_end) {
-    if (!on) return;
-    const unsigned long long t0 = sh[2];
-    sh[3] += sh[0] > t0 ? sh[0] - t0 : 0;
-    sh[4] += sh[1] > t0 ? sh[1] - t0 : 0;
-    sh[5] += t_end - t_sync;
-    sh[6] += t_end - t0;
-    sh[2] = t_end;
-    sh[0] = sh[1] = 0;
-  }
-  __device__ void flush(const NvlsArgs& a) {
-    if (!on || threadIdx.x != 0) return;
-    unsigned long long* rec = a.trace + 4ull * blockIdx.x;
-    for (int k = 0; k < 4; ++k) rec[k] += sh[3 + k];
-  }
-};
+// ---------------------------------------------------------------- progress
+//
+// The two warp groups of a block run decoupled pipelines and wait only for
+// what they consume. Each block has, on every GPU, one progress word per
+// (group, rank): flag(g, q) = epoch + the number of steps group g of this
+// block index on rank q has completed. A group leader publishes its progress
+// with one multicast store (release, system scope) after the group's
+// bar.sync and a system fence, so every GPU's copy of the word advances; a
+// waiting leader polls its own GPU's words with acquire loads, then releases
+// its group with bar.sync. Values only grow (the host advances the epoch by
+// the largest step count of each call), so a wait is "every listed rank
+// reached v". Every wait is bounded by %globaltimer: on expiry the leader
+// sets the status word in mapped host memory and the shared abort flag, and
+// both groups return at their next wait.
+constexpr int kMover = 0, kCopier = 1;
 
-// Cross-GPU barrier of step s for this block: every GPU's block of the same
-// index finished step s. Bounded by %globaltimer: on expiry the status word
-// in mapped host memory is set and every thread of the block returns false.
-__device__ __forceinline__ bool nvls_barrier(const NvlsArgs& a, unsigned long long s, int* abort_flag,
-                                             Tracer& tr) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned long long t_sync = tr.on ? globaltimer() : 0;
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    mc_arrive(a.mc_flags + blockIdx.x);
-    const unsigned target = a.base + unsigned(a.nranks) * unsigned(s + 1);
-    const unsigned long long start = globaltimer();
-    while (int(ld_acquire(a.uc_flags + blockIdx.x) - target) < 0) {
-      if (globaltimer() - start > a.timeout_ns) {
-        *reinterpret_cast<volatile unsigned*>(a.status) = 1u;  // mapped host word
-        __threadfence_system();
-        *abort_flag = 1;
-        break;
-      }
-    }
-    tr.step(t_sync, tr.on ? globaltimer() : 0);
-  }
-  __syncthreads();
-  return *abort_flag == 0;
+__device__ __forceinline__ unsigned flag_index(int group, int q) {
+  return (blockIdx.x * 2u + unsigned(group)) * unsigned(kMaxRanks) + unsigned(q);
 }
 
-// Warp specialization: the first half of the block's warps reduce through
-// the switch (NVLink-bound) while the second half copies rounds in and out
-// of the scratch (HBM-bound), so the two resources work at the same time.
-// U: multimem requests in flight per switch-side thread.
+__device__ __forceinline__ void group_sync(bool mover, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(mover ? 1 : 2), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void mc_publish(unsigned* p, unsigned v) {
+  asm volatile("multimem.st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Per-thread view of its warp group. `tr` (shared, leader only) accumulates
+// the optional phase timing: [0] busy, [1] waiting, [2] last mark, [3] start.
+struct Grp {
+  bool mover;
+  int t, nt;
+  bool leader;
+  volatile int* abort;
+  unsigned long long* tr;
+};
+
+__device__ __forceinline__ Grp make_group(const NvlsArgs& a, int* abort_flag,
+                                          unsigned long long (*trace_sh)[4]) {
+  Grp g;
+  g.mover = int(threadIdx.x) < a.movers;
+  g.t = g.mover ? int(threadIdx.x) : int(threadIdx.x) - a.movers;
+  g.nt = g.mover ? a.movers : int(blockDim.x) - a.movers;
+  g.leader = g.t == 0;
+  g.abort = abort_flag;
+  g.tr = a.trace ? trace_sh[g.mover ? 0 : 1] : nullptr;
+  return g;
+}
+
+// Leader: wait until flag(group, q) >= v on every rank q (only `only` when
+// it is >= 0), then release the group. False for every thread of the group
+// when a wait expired here or the other group aborted.
+__device__ bool group_wait(const NvlsArgs& a, const Grp& g, int group, unsigned v, int only) {
+  if (g.leader) {
+    const unsigned long long t0 = globaltimer();
+    if (g.tr) g.tr[0] += t0 - g.tr[2];
+    const unsigned target = v + a.skew;
+    for (int q = 0; q < a.nranks; ++q) {
+      if (only >= 0 && q != only) continue;
+      const unsigned* f = a.uc_flags + flag_index(group, q);
+      while (int(ld_acquire(f) - target) < 0) {
+        if (*g.abort) break;
+        if (globaltimer() - t0 > a.timeout_ns) {
+          *reinterpret_cast<volatile unsigned*>(a.status) = 1u;  // mapped host word
+          __threadfence_system();
+          *g.abort = 1;
+          break;
+        }
+      }
+      if (*g.abort) break;
+    }
+    if (g.tr) {
+      const unsigned long long t1 = globaltimer();
+      g.tr[1] += t1 - t0;
+      g.tr[2] = t1;
+    }
+  }
+  group_sync(g.mover, g.nt);
+  return *g.abort == 0;
+}
+
+// The group finished a step: its writes are ordered before the leader's
+// release of flag(own group, this rank) = v on every GPU.
+__device__ __forceinline__ void group_publish(const NvlsArgs& a, const Grp& g, unsigned v) {
+  group_sync(g.mover, g.nt);
+  if (g.leader) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    mc_publish(a.mc_flags + flag_index(g.mover ? kMover : kCopier, a.rank), v);
+  }
+}
+
+// Optional per-block phase timing (NCCL_B200_NVLS_TRACE): each leader adds
+// {busy, waiting, total} ns of its group to the block's record
+// {mover busy, mover wait, copier busy, copier wait, mover total, copier total}.
+__device__ __forceinline__ void trace_begin(const Grp& g) {
+  if (g.tr && g.leader) {
+    g.tr[0] = g.tr[1] = 0;
+    g.tr[2] = g.tr[3] = globaltimer();
+  }
+}
+__device__ __forceinline__ void trace_end(const NvlsArgs& a, const Grp& g) {
+  if (!g.tr || !g.leader) return;
+  const unsigned long long t = globaltimer();
+  unsigned long long* rec = a.trace + 8ull * blockIdx.x;
+  const int o = g.mover ? 0 : 2;
+  rec[o] += g.tr[0] + (t - g.tr[2]);
+  rec[o + 1] += g.tr[1];
+  rec[4 + (g.mover ? 0 : 1)] += t - g.tr[3];
+}
+
+// AllReduce. Warp specialization: movers reduce through the switch
+// (NVLink-bound), copiers stream rounds in and out of the scratch
+// (HBM-bound). Rounds of R bytes cut into N slices; rank r owns slice r.
+//   copier step s: C(s-2) after every rank's B(s-2); A(s); publish s+1.
+//   mover  step s: B(s) after every rank's A(s); publish s+1.
+// A(s) reuses buffer s%3 after every rank's B(s-3) (implied by the wait
+// before C(s-2)); B(s) stores into every rank's buffer s%3 after that rank's
+// A(s), hence after its C(s-3). U: multimem requests in flight per thread.
 template <int U, int DT>
 __global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
   __shared__ int abort_flag;
-  __shared__ unsigned long long trace_sh[7];
+  __shared__ unsigned long long trace_sh[2][4];
   if (threadIdx.x == 0) abort_flag = 0;
-  Tracer tr(trace_sh, a.trace != nullptr);
+  const Grp g = make_group(a, &abort_flag, trace_sh);
+  trace_begin(g);
   __syncthreads();
   const int n = a.nranks;
-  const unsigned long long rounds = (a.bytes + a.round - 1) / a.round;
+  const unsigned rounds = unsigned((a.bytes + a.round - 1) / a.round);
   const float inv = 1.0f / float(n);
-  // The first a.movers threads work through the switch; the rest copy.
-  const bool reducer = int(threadIdx.x) < a.movers;
-  const int t = reducer ? threadIdx.x : threadIdx.x - a.movers;
-  const int half = reducer ? a.movers : int(blockDim.x) - a.movers;  // this group's size
-  for (unsigned long long s = 0; s < rounds + 2; ++s) {
-    if (!reducer) {
-      // C(s-2): copy the reduced round out of the scratch.
+  if (g.mover) {
+    for (unsigned s = 0; s < rounds; ++s) {
+      if (!group_wait(a, g, kCopier, a.base + s + 1, -1)) return;
+      const unsigned long long rbase = s * a.round;
+      const unsigned long long rlen = min(a.round, a.bytes - rbase);
+      unsigned long long lo, hi;
+      portion(rlen, n, a.rank, &lo, &hi);
+      char* base = a.mc + (s % 3) * a.buf_stride + lo;
+      strided<U>(
+          unsigned(g.t), unsigned(g.nt), unsigned((hi - lo) / 16),
+          [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
+          [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, a.avg ? scale(x, DT, inv) : x); });
+      group_publish(a, g, a.base + s + 1);
+    }
+  } else {
+    for (unsigned s = 0; s < rounds + 2; ++s) {
       if (s >= 2) {
-        const unsigned long long i = s - 2, rbase = i * a.round;
+        if (!group_wait(a, g, kMover, a.base + s - 1, -1)) return;
+        const unsigned i = s - 2;
+        const unsigned long long rbase = i * a.round;
         const unsigned long long rlen = min(a.round, a.bytes - rbase);
         const char* buf = a.uc + (i % 3) * a.buf_stride;
         for (int q = 0; q < n; ++q) {
           unsigned long long lo, hi;
           portion(rlen, n, q, &lo, &hi);
-          copy16(a.recv + rbase + lo, buf + lo, hi - lo, t, half);
+          copy16(a.recv + rbase + lo, buf + lo, hi - lo, g.t, g.nt);
         }
       }
-      // A(s): copy this GPU's input round into its scratch.
       if (s < rounds) {
         const unsigned long long rbase = s * a.round;
         const unsigned long long rlen = min(a.round, a.bytes - rbase);
@@ -296,27 +351,13 @@ __global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_con
         for (int q = 0; q < n; ++q) {
           unsigned long long lo, hi;
           portion(rlen, n, q, &lo, &hi);
-          copy16(buf + lo, a.send + rbase + lo, hi - lo, t, half);
+          copy16(buf + lo, a.send + rbase + lo, hi - lo, g.t, g.nt);
         }
       }
-    } else if (s >= 1 && s - 1 < rounds) {
-      // B(s-1): reduce and multicast this rank's slice.
-      const unsigned long long i = s - 1, rbase = i * a.round;
-      const unsigned long long rlen = min(a.round, a.bytes - rbase);
-      char* mbuf = a.mc + (i % 3) * a.buf_stride;
-      unsigned long long lo, hi;
-      portion(rlen, n, a.rank, &lo, &hi);
-      char* base = mbuf + lo;
-      strided<U>(
-          unsigned(t), unsigned(half), unsigned((hi - lo) / 16),
-          [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
-          [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, a.avg ? scale(x, DT, inv) : x); });
+      group_publish(a, g, a.base + s + 1);
     }
-    // Barrier: this block's counterparts on every GPU finished step s.
-    tr.group_done(reducer);
-    if (!nvls_barrier(a, s, &abort_flag, tr)) return;
   }
-  tr.flush(a);
+  trace_end(a, g);
 }
 
 // This block's part [lo, hi) of a flat range of `len` bytes (16-byte units).
@@ -327,85 +368,73 @@ __device__ __forceinline__ void flat_portion(unsigned long long len, unsigned lo
   *hi = min(len, *lo + per);
 }
 
-
 // Broadcast / AllGather / ReduceScatter through the switch, with the same
-// three-buffer scratch, per-block bounded barriers and warp split as the
-// AllReduce kernel:
-//  Broadcast: the root multicasts round s of its input (multimem.st) while
-//    every GPU copies round s-1 out of its scratch; root sends each byte once.
-//  AllGather: every rank multicasts its part of round s into its own part of
-//    the round buffer; every GPU copies round s-1 (all parts) out.
-//  ReduceScatter: every GPU copies round s of its input in; every rank
-//    multimem.ld_reduces its own part of round s-1 straight into its output.
+// three-buffer scratch, decoupled groups and bounded waits:
+//  ReduceScatter: copier A(s) copies every slot's part of round s in (after
+//    every rank's B(s-3), the last reader of buffer s%3); mover B(s), after
+//    every rank's A(s), multimem.ld_reduces its own part into its output.
+//  AllGather: mover B(s) multicasts its slot's part of round s into every
+//    rank's buffer (after every rank's C(s-3)); copier C(s), after every
+//    rank's B(s), copies all parts out.
+//  Broadcast: the root's movers multicast round s (after every rank's
+//    C(s-3)); copiers copy round s out after the root's B(s). The root
+//    sends each byte once.
 template <int U, int DT>
 __global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant__ NvlsArgs a) {
   __shared__ int abort_flag;
-  __shared__ unsigned long long trace_sh[7];
+  __shared__ unsigned long long trace_sh[2][4];
   if (threadIdx.x == 0) abort_flag = 0;
-  Tracer tr(trace_sh, a.trace != nullptr);
+  const Grp g = make_group(a, &abort_flag, trace_sh);
+  trace_begin(g);
   __syncthreads();
   const int n = a.nranks;
-  const bool mover = int(threadIdx.x) < a.movers;  // switch-side warps
-  const int t = mover ? threadIdx.x : threadIdx.x - a.movers;
-  const int half = mover ? a.movers : int(blockDim.x) - a.movers;  // this group's size
   const float inv = 1.0f / float(n);
   const bool bc = a.mode == int(Kind::Broadcast);
+  const bool rs = a.mode == int(Kind::ReduceScatter);
   const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)n) & ~31ull);
   const unsigned long long total = bc ? a.bytes : a.slot;
-  const unsigned long long rounds = (total + part - 1) / part;
-  for (unsigned long long s = 0; s < rounds + 1; ++s) {
-    if (a.mode == int(Kind::ReduceScatter)) {
-      if (!mover && s < rounds) {  // A(s): copy every slot's part of round s in
-        const unsigned long long plen = min(part, total - s * part);
-        char* buf = a.uc + (s % 3) * a.buf_stride;
-        unsigned long long lo, hi;
-        flat_portion(plen, &lo, &hi);
-        for (int q = 0; q < n; ++q)
-          copy16(buf + q * part + lo, a.send + q * a.slot + s * part + lo, hi - lo, t, half);
-      }
-      if (mover && s >= 1) {  // B(s-1): reduce the own part into the output
-        const unsigned long long i = s - 1, plen = min(part, total - i * part);
-        const char* mbuf = a.mc + (i % 3) * a.buf_stride + a.rank * part;
-        unsigned long long lo, hi;
-        flat_portion(plen, &lo, &hi);
-        const char* base = mbuf + lo;
-        uint4* out = reinterpret_cast<uint4*>(a.recv + i * part + lo);
+  const unsigned rounds = unsigned((total + part - 1) / part);
+  for (unsigned s = 0; s < rounds; ++s) {
+    const unsigned long long plen = min(part, total - s * part);
+    unsigned long long lo, hi;
+    flat_portion(plen, &lo, &hi);
+    if (rs) {
+      if (g.mover) {
+        if (!group_wait(a, g, kCopier, a.base + s + 1, -1)) return;
+        const char* base = a.mc + (s % 3) * a.buf_stride + a.rank * part + lo;
+        uint4* out = reinterpret_cast<uint4*>(a.recv + s * part + lo);
         strided<U>(
-            unsigned(t), unsigned(half), unsigned((hi - lo) / 16),
+            unsigned(g.t), unsigned(g.nt), unsigned((hi - lo) / 16),
             [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
             [&](unsigned v, uint4 x) { __stcs(out + v, a.avg ? scale(x, DT, inv) : x); });
+      } else {
+        if (s >= 3 && !group_wait(a, g, kMover, a.base + s - 2, -1)) return;
+        char* buf = a.uc + (s % 3) * a.buf_stride;
+        for (int q = 0; q < n; ++q)
+          copy16(buf + q * part + lo, a.send + q * a.slot + s * part + lo, hi - lo, g.t, g.nt);
       }
+    } else if (g.mover) {
+      if (bc && a.rank != a.root) break;  // only the root's movers send
+      if (s >= 3 && !group_wait(a, g, kCopier, a.base + s - 2, -1)) return;
+      char* base = a.mc + (s % 3) * a.buf_stride + (bc ? 0 : a.rank * part) + lo;
+      const uint4* in = reinterpret_cast<const uint4*>(a.send + s * part + lo);
+      strided<U>(
+          unsigned(g.t), unsigned(g.nt), unsigned((hi - lo) / 16),
+          [&](unsigned v) { return __ldcs(in + v); },
+          [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, x); });
     } else {
-      if (!mover && s >= 1) {  // C(s-1): copy round s-1 out
-        const unsigned long long i = s - 1, plen = min(part, total - i * part);
-        const char* buf = a.uc + (i % 3) * a.buf_stride;
-        unsigned long long lo, hi;
-        flat_portion(plen, &lo, &hi);
-        if (bc) {
-          copy16(a.recv + i * part + lo, buf + lo, hi - lo, t, half);
-        } else {
-          for (int q = 0; q < n; ++q)
-            copy16(a.recv + q * a.slot + i * part + lo, buf + q * part + lo, hi - lo, t, half);
-        }
-      }
-      if (mover && s < rounds && (!bc || a.rank == a.root)) {  // B(s): multicast
-        const unsigned long long plen = min(part, total - s * part);
-        char* mbuf = a.mc + (s % 3) * a.buf_stride + (bc ? 0 : a.rank * part);
-        const char* src = a.send + s * part;
-        unsigned long long lo, hi;
-        flat_portion(plen, &lo, &hi);
-        const uint4* in = reinterpret_cast<const uint4*>(src + lo);
-        char* base = mbuf + lo;
-        strided<U>(
-            unsigned(t), unsigned(half), unsigned((hi - lo) / 16),
-            [&](unsigned v) { return __ldcs(in + v); },
-            [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, x); });
+      if (!group_wait(a, g, kMover, a.base + s + 1, bc ? a.root : -1)) return;
+      const char* buf = a.uc + (s % 3) * a.buf_stride;
+      if (bc) {
+        copy16(a.recv + s * part + lo, buf + lo, hi - lo, g.t, g.nt);
+      } else {
+        for (int q = 0; q < n; ++q)
+          copy16(a.recv + q * a.slot + s * part + lo, buf + q * part + lo, hi - lo, g.t, g.nt);
       }
     }
-    tr.group_done(mover);
-    if (!nvls_barrier(a, s, &abort_flag, tr)) return;
+    group_publish(a, g, a.base + s + 1);
   }
-  tr.flush(a);
+  trace_end(a, g);
 }
 
 // ------------------------------------------------------------------ host side
@@ -491,7 +520,7 @@ struct Context {
   std::vector<char*> uc, mc;
   unsigned* status = nullptr;  // mapped pinned host word
   unsigned* status_dev = nullptr;
-  unsigned long long barriers = 0;  // per-block barriers run so far on this scratch
+  unsigned long long epoch = 0;  // progress value every flag reached after the last call
   std::vector<unsigned long long*> trace;  // per device: blocks x 4 phase-time records
   int blocks = 0;
   bool broken = false;
@@ -562,7 +591,7 @@ bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why
   const int blocks = sms;  // one resident block per SM (cooperative launch)
   const size_t round = std::max<size_t>(round_bytes / 16 * 16, size_t(n) * size_t(blocks) * 16);
   const size_t stride = round_up(round, 1 << 21);
-  const size_t flags_bytes = round_up(size_t(blocks) * sizeof(unsigned), 4096);
+  const size_t flags_bytes = round_up(size_t(blocks) * 2 * kMaxRanks * sizeof(unsigned), 4096);
   CUmulticastObjectProp mprop{};
   mprop.numDevices = unsigned(n);
   mprop.handleTypes = 0;
@@ -621,7 +650,7 @@ bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why
     if (cudaMemset(reinterpret_cast<char*>(uc) + 3 * stride, 0, flags_bytes) != cudaSuccess)
       return fail("flag init");
     unsigned long long* tr = nullptr;
-    const size_t tr_bytes = size_t(blocks) * 4 * sizeof(unsigned long long);
+    const size_t tr_bytes = size_t(blocks) * 8 * sizeof(unsigned long long);
     if (cudaMalloc(&tr, tr_bytes) != cudaSuccess || cudaMemset(tr, 0, tr_bytes) != cudaSuccess)
       return fail("trace records");
     c->trace.push_back(tr);
@@ -660,7 +689,8 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.buf_stride = c->stride;
   a.timeout_ns = p.device_timeout_ns;
   a.status = c->status_dev;
-  a.base = unsigned(c->barriers * (unsigned long long)b.nranks) + p.test_nvls_skew;
+  a.base = unsigned(c->epoch);
+  a.skew = p.test_nvls_skew;
   a.nranks = b.nranks;
   a.rank = r;
   a.dtype = int(plan.desc.dtype);
@@ -671,15 +701,16 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.trace = p.nvls_trace ? c->trace[size_t(r)] : nullptr;
   (void)dev;
   const bool ar = plan.desc.kind == Kind::AllReduce;
-  // Barriers this call runs (one per step); every rank runs the same count.
+  // The largest progress value this call publishes (every rank the same):
+  // the next call's epoch.
   unsigned long long steps = 0;
   if (ar) {
     steps = (a.bytes + a.round - 1) / a.round + 2;
   } else {
     const bool bc = plan.desc.kind == Kind::Broadcast;
     const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)b.nranks) & ~31ull);
-    steps = (plan.desc.bytes + part - 1) / part + 1;
-    if (!bc && part == 0) return cudaErrorInvalidValue;
+    if (part == 0) return cudaErrorInvalidValue;
+    steps = (plan.desc.bytes + part - 1) / part;
   }
   const int threads = p.nvls_threads;
   a.movers = std::min(p.nvls_movers, threads - 128);
@@ -687,26 +718,26 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   const void* fn = pick_kernel(ar, p.nvls_unroll >= 8, plan.desc.dtype);
   const cudaError_t e =
       cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(unsigned(threads)), argv, 0, s);
-  if (r == b.nranks - 1) c->barriers += steps;
+  if (r == b.nranks - 1) c->epoch += steps;
   return e;
 }
 
-int nvls_trace_read(const int* devices, int n, int rank, double out[4], bool reset) {
+int nvls_trace_read(const int* devices, int n, int rank, double out[6], bool reset) {
   std::lock_guard<std::mutex> lk(g_mu);
   Context* c = find(devices, n);
   if (!c || rank < 0 || rank >= n) return -1;
   int prev = 0;
   if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(devices[rank]) != cudaSuccess) return -1;
-  std::vector<unsigned long long> rec(size_t(c->blocks) * 4);
+  std::vector<unsigned long long> rec(size_t(c->blocks) * 8);
   const size_t bytes = rec.size() * sizeof(unsigned long long);
   cudaError_t e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaMemcpy(rec.data(), c->trace[size_t(rank)], bytes, cudaMemcpyDeviceToHost);
   if (e == cudaSuccess && reset) e = cudaMemset(c->trace[size_t(rank)], 0, bytes);
   cudaSetDevice(prev);
   if (e != cudaSuccess) return -1;
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < 6; ++k) {
     double sum = 0;
-    for (int b = 0; b < c->blocks; ++b) sum += double(rec[size_t(b) * 4 + size_t(k)]);
+    for (int b = 0; b < c->blocks; ++b) sum += double(rec[size_t(b) * 8 + size_t(k)]);
     out[k] = sum / double(c->blocks);  // mean over blocks, ns
   }
   return c->blocks;

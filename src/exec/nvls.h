@@ -31,9 +31,9 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
 // nonzero = a bounded wait expired. Reading it synchronizes nothing.
 unsigned nvls_status(const int* devices, int n);
 // Phase timing of one rank's NVLS kernels since the last reset (policy
-// nvls_trace): out = mean over blocks of {mover busy, copier busy, barrier
-// wait, total} in ns. Synchronizes that device. Returns the block count, or
-// -1 without an NVLS context.
-int nvls_trace_read(const int* devices, int n, int rank, double out[4], bool reset);
+// nvls_trace): out = mean over blocks of {mover busy, mover waiting, copier
+// busy, copier waiting, mover total, copier total} in ns. Synchronizes that
+// device. Returns the block count, or -1 without an NVLS context.
+int nvls_trace_read(const int* devices, int n, int rank, double out[6], bool reset);
 
 }  // namespace nb
