@@ -64,6 +64,7 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
       add(Algo::BcPull, 0);
       add(Algo::BcPull, 10000);
       if (n >= 3) {
+        add(Algo::BcChain, 10000, 32, 0);
         add(Algo::BcChain, 10000, 64, 0);
         add(Algo::BcChain, 10000, 128, 0);
         add(Algo::BcChain, 0, 128, 0);

@@ -658,7 +658,9 @@ void plan_bc_chain(Builder& b, const CliqueDesc& d, const Shares& s) {
     const size_t cb = std::min(piece, body - off);
     for (int h = 1; h < n; ++h) {
       const int r = (root + h) % n, pred = (root + h - 1) % n;
-      const StreamId s1{ce ? Strm::Copy : Strm::Caller, uint8_t(r), 0};
+      // Copy-engine pieces alternate between two streams of the receiver, so
+      // the next piece's copy is queued while the previous one drains.
+      const StreamId s1{ce ? (k % 2 ? Strm::Push : Strm::Copy) : Strm::Caller, uint8_t(r), 0};
       b.touch(s1, r);
       b.touch(s1, pred);
       if (h > 1) b.wait(s1, {Ev::Phase, uint8_t(pred), 0, uint16_t(k)});
@@ -704,10 +706,25 @@ void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p) {
   b.join();
 }
 
+// One rank: every collective except a scaled one (PreMulSum) is a copy of
+// the input into the output, done by the copy engine on the caller stream
+// (a device-to-device copy streams HBM at the copy engine's full rate).
+void plan_single(Builder& b, const CliqueDesc& d) {
+  b.prologue();
+  const StreamId cl{Strm::Caller, 0, 0};
+  b.touch(cl, 0);
+  if (!d.in_place[0]) b.ce_copy(cl, recv_at(0, 0), send_at(0, 0), d.bytes);
+  b.join();
+}
+
 }  // namespace
 
 void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s, Plan& out) {
   Builder b(out, algo, d, p);
+  if (d.nranks == 1 && algo != Algo::Fallback && !(reduces(d.kind) && d.op == RedOp::PreMulSum)) {
+    plan_single(b, d);
+    return;
+  }
   switch (algo) {
     case Algo::ArTwoShot: plan_ar_twoshot(b, d, s); break;
     case Algo::ArNvls: plan_ar_nvls(b, d, p); break;

@@ -51,7 +51,7 @@ struct Policy {
   int stage_depth = 2;              // staged routes: scratch pieces in flight
   bool calibrate = true;            // measure path bandwidths at init
   bool tune = true;                 // time candidate routes at init, keep the fastest
-  size_t tune_bytes = 2 * kGiB;     // message size the route tuning runs at
+  size_t tune_bytes = 4 * kGiB;     // message size the route tuning runs at
   std::string calib_cache;          // JSON cache path ("" = none)
   uint64_t device_timeout_ns = 2000000000ull;  // bound of every in-kernel wait
   // Test hook: raise the NVLS barrier targets so that no arrival can meet
