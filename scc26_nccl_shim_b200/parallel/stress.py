@@ -27,6 +27,13 @@ Mutation self-test (--corrupt-shift K): rank 0's output is displaced by K
 elements before the check; every affected case must FAIL, proving that the
 checker can fail.
 
+Ordering controls: --delay-input-device D holds rank D's caller stream
+(a bounded sleep kernel) before every call, so a rank that read a peer's
+input without waiting for it would see stale data; --overwrite-after
+overwrites every input on its caller stream right after the call, which is
+safe only if the call's side streams were joined back into the caller
+streams; --fresh-streams issues every iteration on new caller streams.
+
 Output: one TSV row per case:
   case iters bytes mismatches status guard_bad route kind mode
 Parity: tests/stress_check.cu of the reference (two GPUs, fixed thresholds).
@@ -133,7 +140,8 @@ def thresholds() -> dict:
 
 
 def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, seed: int,
-             diff: bool, corrupt_shift: int) -> dict:
+             diff: bool, corrupt_shift: int, delay_device: int = -1, delay_ms: float = 0.0,
+             overwrite_after: bool = False, fresh_streams: bool = False) -> dict:
     n = len(devs)
     dtype = DTYPES[case.dtype]
     es = torch.tensor([], dtype=dtype).element_size()
@@ -144,7 +152,8 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
     for r, d in enumerate(devs):
         b = Buffers(send_elems * es, recv_elems * es, dtype, f"cuda:{d}")
         bufs.append(b)
-    streams = [torch.cuda.current_stream(d).cuda_stream for d in devs]
+    home = [torch.cuda.current_stream(d) for d in devs]
+    streams = [h.cuda_stream for h in home]
 
     def views(r):
         b = bufs[r]
@@ -164,7 +173,15 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
     if diff and ref is not None:
         shadows = [torch.empty(recv_elems, dtype=dtype, device=f"cuda:{d}") for d in devs]
     reduces = case.kind in ("allreduce", "reducescatter")
+    overwrite = overwrite_after and not case.inplace
     for it in range(iters):
+        if fresh_streams:
+            # New caller streams every iteration, ordered after the previous ones.
+            fresh = [torch.cuda.Stream(device=d) for d in devs]
+            for i, d in enumerate(devs):
+                fresh[i].wait_stream(torch.cuda.current_stream(d))
+                torch.cuda.set_stream(fresh[i])
+            streams = [f.cuda_stream for f in fresh]
         sends, recvs = [], []
         for r, d in enumerate(devs):
             s, v = views(r)
@@ -176,12 +193,23 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
                     s.copy_(exact(r, s.numel(), it, seed, dtype, n, f"cuda:{d}"))
             sends.append(s)
             recvs.append(v)
-        inputs = [s.clone() for s in sends] if (diff or case.inplace) else sends
+        inputs = [s.clone() for s in sends] if (diff or case.inplace or overwrite) else sends
         if shadows is not None:
             # Stock NCCL first, into shadow buffers, through the real library.
             shadow_sends = [x.clone() for x in inputs]
             collective(ref, case.kind, shadow_sends, shadows, comms, streams, op=case.op, root=case.root)
+        if 0 <= delay_device < len(devs):
+            # Hold one GPU's caller stream before the call: every other rank
+            # must wait for its input, not read it early.
+            with torch.cuda.device(devs[delay_device]):
+                torch.cuda._sleep(int(delay_ms * 1.9e6))
         collective(nc, case.kind, sends, recvs, comms, streams, op=case.op, root=case.root)
+        if overwrite:
+            # Stream-ordered reuse of the inputs right after the call: safe
+            # only if the call's side streams joined the caller streams.
+            for r, d in enumerate(devs):
+                with torch.cuda.device(d):
+                    sends[r].view(torch.uint8).fill_(0x5A)
         for r, d in enumerate(devs):
             with torch.cuda.device(d):
                 got = recvs[r]
@@ -200,6 +228,11 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
                     want = expected(case, r, n, it, seed, dtype, f"cuda:{d}", [x.to(f"cuda:{d}") for x in inputs]
                                     if case.kind in ("allgather", "broadcast") or case.op != "sum" else None)
                     mism[r] += (got.view(torch.uint8) != want.view(torch.uint8)).sum()
+        if fresh_streams:
+            for i, d in enumerate(devs):
+                home[i].wait_stream(torch.cuda.current_stream(d))
+                torch.cuda.set_stream(home[i])
+            streams = [h.cuda_stream for h in home]
     for d in devs:
         torch.cuda.synchronize(d)
     total = int(sum(m.item() for m in mism))
@@ -245,6 +278,12 @@ def main(argv=None) -> int:
     p.add_argument("--corrupt-shift", type=int, default=0)
     p.add_argument("--filter", default="")
     p.add_argument("--no-boundary", action="store_true")
+    p.add_argument("--delay-input-device", type=int, default=-1,
+                   help="hold this rank's caller stream before every call")
+    p.add_argument("--delay-ms", type=float, default=20.0)
+    p.add_argument("--overwrite-after", action="store_true",
+                   help="overwrite the inputs on the caller streams right after every call")
+    p.add_argument("--fresh-streams", action="store_true", help="new caller streams every iteration")
     a = p.parse_args(argv)
     devs = list(range(a.gpus))
     nc = Nccl("interposer")
@@ -260,7 +299,8 @@ def main(argv=None) -> int:
     print("case\titers\tbytes\tmismatches\tstatus\tguard_bad\troute\tkind\tmode", flush=True)
     bad = 0
     for case in cases:
-        res = run_case(nc, ref, comms, devs, case, a.iters, a.seed, a.diff, a.corrupt_shift)
+        res = run_case(nc, ref, comms, devs, case, a.iters, a.seed, a.diff, a.corrupt_shift,
+                       a.delay_input_device, a.delay_ms, a.overwrite_after, a.fresh_streams)
         bad += res["status"] != "PASS"
         print("\t".join(str(res[k]) for k in ("case", "iters", "bytes", "mismatches", "status",
                                                 "guard_bad", "route", "kind", "mode")), flush=True)

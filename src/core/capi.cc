@@ -112,6 +112,29 @@ int nb_gate_clique(const nb_call_t* calls, int n, int flags, const char* env, in
   return int(d.reason);
 }
 
+// The clique gate with per-rank PreMulSum scalars (value, residence:
+// 1 host immediate, 0 device pointer).
+int nb_gate_clique_scalars(const nb_call_t* calls, int n, int flags, const char* env, int* algo,
+                           const double* scalars, const int* residence) {
+  std::vector<CallDesc> v;
+  for (int i = 0; i < n; ++i) {
+    CallDesc d = to_desc(calls[i]);
+    d.scalar = scalars[i];
+    d.scalar_residence = residence[i];
+    v.push_back(d);
+  }
+  CliqueState s;
+  s.known_clique = flags & 1;
+  s.capturing = flags & 2;
+  s.first_pass_done = flags & 4;
+  s.poisoned = flags & 8;
+  s.nccl_supported = !(flags & 16);
+  s.nvls_available = flags & 32;
+  const CliqueDecision d = gate_clique(v, s, EnvMap(env).policy());
+  if (algo) *algo = int(d.algo);
+  return int(d.reason);
+}
+
 struct nb_plan_stats_t {
   uint64_t ops, records, waits, data_ops, sm_bytes, ce_bytes, host_bytes;
   int lanes;

@@ -61,7 +61,7 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
       // A multicast object needs at least two devices.
       return k == Kind::AllReduce && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
-             (op == RedOp::Sum || op == RedOp::Avg);
+             (op == RedOp::Sum || op == RedOp::Avg || op == RedOp::PreMulSum);
     case Algo::RsPull: return k == Kind::ReduceScatter;
     case Algo::AgPull: return k == Kind::AllGather;
     case Algo::BcPull: return k == Kind::Broadcast;
@@ -74,7 +74,7 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
     case Algo::RsNvls:
       return k == Kind::ReduceScatter && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
-             (op == RedOp::Sum || op == RedOp::Avg);
+             (op == RedOp::Sum || op == RedOp::Avg || op == RedOp::PreMulSum);
     default: return false;
   }
 }
@@ -134,13 +134,18 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
   if (p.first_pass && !s.first_pass_done) return fallback(Reason::FirstPass);
   Algo algo = choose_algo(a, n, s.nvls_available, p, s.preferred[size_t(a.kind)]);
   // The multimem kernels move whole 16-byte vectors only: every buffer and
-  // every slot must be 16-byte aligned.
+  // every slot must be 16-byte aligned. They scale the switch's sum once, so
+  // a PreMulSum takes them only when every rank passed the same host scalar.
   const bool nvls = algo == Algo::ArNvls || algo == Algo::BcNvls || algo == Algo::AgNvls ||
                     algo == Algo::RsNvls;
   bool aligned = call_bytes(a) % 16 == 0;
   for (const CallDesc& c : calls)
     aligned = aligned && c.recv % 16 == 0 && (c.send % 16 == 0 || (c.kind == Kind::Broadcast && c.rank != c.root));
-  if (nvls && !aligned) {
+  bool uniform = true;
+  if (a.op == RedOp::PreMulSum)
+    for (const CallDesc& c : calls)
+      uniform = uniform && c.scalar_residence == 1 && a.scalar_residence == 1 && c.scalar == a.scalar;
+  if (nvls && (!aligned || !uniform)) {
     const Policy q = [&] {
       Policy x = p;
       x.nvls = NvlsMode::Off;
@@ -164,6 +169,7 @@ CliqueDesc describe_clique(const std::vector<CallDesc>& calls) {
   d.bytes = call_bytes(a);
   d.count = a.count;
   d.root = a.kind == Kind::Broadcast ? a.root : -1;
+  d.scalar = a.op == RedOp::PreMulSum ? a.scalar : 1.0;
   for (const CallDesc& c : calls)
     if (c.rank >= 0 && c.rank < kMaxRanks) d.in_place[c.rank] = call_in_place(c);
   return d;

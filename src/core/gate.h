@@ -60,6 +60,7 @@ struct CliqueDesc {
   size_t count = 0;
   int root = -1;         // Broadcast only (a rank)
   bool in_place[kMaxRanks] = {};
+  double scalar = 1.0;   // PreMulSum: the scalar every rank shares (NVLS routes)
 };
 CliqueDesc describe_clique(const std::vector<CallDesc>& calls);
 

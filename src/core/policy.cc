@@ -95,6 +95,7 @@ Policy policy_from_env(const EnvLookup& env) {
     p.nvls_movers = int(i);
   if (parse_int(env("NCCL_B200_NVLS_UNROLL"), &i) && (i == 4 || i == 8)) p.nvls_unroll = int(i);
   if (parse_bool(env("NCCL_B200_NVLS_TRACE"), &b)) p.nvls_trace = b;
+  if (parse_bool(env("NCCL_B200_NVLS_TMA"), &b)) p.nvls_tma = b;
   if (parse_bool(env("NCCL_B200_NVTX"), &b)) p.nvtx = b;
   if (parse_int(env("NCCL_B200_NVLS_THREADS"), &i) && (i == 512 || i == 640 || i == 768))
     p.nvls_threads = int(i);

@@ -32,6 +32,7 @@ struct Policy {
   int nvls_movers = 512;            // of those: switch-side workers (the rest copy)
   int nvls_unroll = 4;              // multimem requests in flight per switch-side thread
   bool nvls_trace = false;          // per-block phase timing in the NVLS kernels
+  bool nvls_tma = true;             // NVLS copier: TMA bulk pipeline (else SM copy warps)
   bool nvtx = false;                // NVTX range per custom submission
   Algo force_algo[size_t(Kind::Count)] = {Algo::Fallback, Algo::Fallback, Algo::Fallback,
                                           Algo::Fallback};  // Fallback = choose

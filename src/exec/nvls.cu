@@ -49,7 +49,10 @@ struct NvlsArgs {
   unsigned* status;          // mapped host word: nonzero = a wait expired
   unsigned base;             // progress epoch before this call
   unsigned skew;             // added to every wait target (bounded-wait test only)
-  int nranks, rank, dtype, avg;
+  int nranks, rank, dtype;
+  int scaled;                // multiply the switch's sum by `mul` (Avg, PreMulSum)
+  int tma;                   // copier group: TMA bulk pipeline (one warp) instead of SM copies
+  float mul;
   int movers;                // threads of a block that work through the switch
   int mode;                  // collective kind (xfer kernel)
   int root;                  // Broadcast
@@ -272,7 +275,7 @@ __device__ bool group_wait(const NvlsArgs& a, const Grp& g, int group, unsigned 
 // release of flag(own group, this rank) = v on every GPU.
 __device__ __forceinline__ void group_publish(const NvlsArgs& a, const Grp& g, unsigned v) {
   group_sync(g.mover, g.nt);
-  if (g.leader) {
+  if (g.leader && !*g.abort) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     mc_publish(a.mc_flags + flag_index(g.mover ? kMover : kCopier, a.rank), v);
   }
@@ -297,6 +300,186 @@ __device__ __forceinline__ void trace_end(const NvlsArgs& a, const Grp& g) {
   rec[4 + (g.mover ? 0 : 1)] += t - g.tr[3];
 }
 
+// ------------------------------------------------------------- TMA copier
+//
+// The copier group's data movement runs on the tensor memory accelerator:
+// one thread streams each copy through shared memory in 16 KiB chunks with
+// cp.async.bulk (global -> shared, completing on an mbarrier) and
+// cp.async.bulk (shared -> global, bulk groups), eight stages deep. Up to
+// 128 KiB per SM are in flight without occupying registers, which is what
+// HBM needs beside the switch traffic. No cluster multicast is used. The
+// scratch is also read and written by the switch (generic proxy), so the
+// thread fences the async proxy after acquiring a round and before
+// publishing one. Every wait is bounded by %globaltimer.
+constexpr int kStages = 8;
+constexpr unsigned kChunk = 16384;
+constexpr size_t kTmaSmem = size_t(kStages) * kChunk;
+
+struct Bulk {
+  bool on;
+  unsigned smem;   // shared address of stage 0
+  unsigned bar;    // shared address of the first of kStages mbarriers
+  char** dst;      // shared: destination of the chunk held by each stage
+  unsigned* size;  // shared: its size
+  unsigned long long issued, stored;
+};
+
+__device__ __forceinline__ unsigned shared_addr(const void* p) {
+  return unsigned(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void fence_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ bool bulk_ready(const Bulk& b, unsigned long long k) {
+  unsigned done;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(done)
+      : "r"(b.bar + 8u * unsigned(k % kStages)), "r"(unsigned((k / kStages) & 1))
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ void expire(const NvlsArgs& a, volatile int* abort) {
+  *reinterpret_cast<volatile unsigned*>(a.status) = 1u;
+  __threadfence_system();
+  *abort = 1;
+}
+
+// Issue the store of the oldest loaded chunk (waiting, bounded, for its load).
+__device__ bool bulk_retire(const NvlsArgs& a, Bulk& b, volatile int* abort) {
+  const unsigned long long k = b.stored;
+  const unsigned long long t0 = globaltimer();
+  while (!bulk_ready(b, k)) {
+    if (globaltimer() - t0 > a.timeout_ns) {
+      expire(a, abort);
+      return false;
+    }
+  }
+  const unsigned st = unsigned(k % kStages);
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(b.dst[st]),
+               "r"(b.smem + st * kChunk), "r"(b.size[st])
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  ++b.stored;
+  return true;
+}
+
+// Wait until at most `pending` of the most recent stores still read shared
+// memory (the instruction takes the count as an immediate).
+__device__ __forceinline__ void bulk_wait_read(unsigned pending) {
+  switch (pending) {
+    case 0: asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.bulk.wait_group.read 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.bulk.wait_group.read 5;" ::: "memory"); break;
+    case 6: asm volatile("cp.async.bulk.wait_group.read 6;" ::: "memory"); break;
+    default: asm volatile("cp.async.bulk.wait_group.read 7;" ::: "memory"); break;
+  }
+}
+
+// Queue the copy src -> dst (16-byte aligned, a multiple of 16 bytes).
+__device__ bool bulk_push(const NvlsArgs& a, Bulk& b, char* dst, const char* src,
+                          unsigned long long bytes, volatile int* abort) {
+  for (unsigned long long off = 0; off < bytes; off += kChunk) {
+    const unsigned size = unsigned(min((unsigned long long)kChunk, bytes - off));
+    const unsigned long long k = b.issued;
+    const unsigned st = unsigned(k % kStages);
+    if (k >= kStages) {
+      // The stage last held chunk k - kStages: its store must have been
+      // issued and must have finished reading shared memory.
+      const unsigned long long j = k - kStages;
+      while (b.stored <= j)
+        if (!bulk_retire(a, b, abort)) return false;
+      bulk_wait_read(unsigned(b.stored - 1 - j));
+    }
+    const unsigned bar = b.bar + 8u * st;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(size) : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            b.smem + st * kChunk),
+        "l"(src + off), "r"(size), "r"(bar)
+        : "memory");
+    b.dst[st] = dst + off;
+    b.size[st] = size;
+    ++b.issued;
+    while (b.stored < b.issued && bulk_ready(b, b.stored))
+      if (!bulk_retire(a, b, abort)) return false;
+  }
+  return true;
+}
+
+// Complete every queued copy: all stores issued and written to global
+// memory, and ordered before later generic-proxy accesses.
+__device__ bool bulk_drain(const NvlsArgs& a, Bulk& b, volatile int* abort) {
+  bool ok = true;
+  while (ok && b.stored < b.issued) ok = bulk_retire(a, b, abort);
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  fence_async_global();
+  return ok;
+}
+
+// Before leaving the kernel: wait (bounded) for loads still in flight, then
+// for every store.
+__device__ void bulk_finish(const NvlsArgs& a, Bulk& b) {
+  const unsigned long long t0 = globaltimer();
+  for (unsigned long long k = b.stored; k < b.issued; ++k)
+    while (!bulk_ready(b, k) && globaltimer() - t0 < a.timeout_ns) {
+    }
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// The copier group's view of its mover: the TMA pipeline (its leader alone
+// issues) or, when off, the SM copy loop over all copier threads.
+template <bool TMA>
+struct Copier {
+  Bulk b;
+  const NvlsArgs* a;
+  const Grp* g;
+  __device__ Copier(const NvlsArgs& args, const Grp& grp, unsigned char* dsmem,
+                    unsigned long long* bars, char** dsts, unsigned* sizes)
+      : a(&args), g(&grp) {
+    b.on = TMA && args.tma != 0;
+    b.smem = shared_addr(dsmem);
+    b.bar = shared_addr(bars);
+    b.dst = dsts;
+    b.size = sizes;
+    b.issued = b.stored = 0;
+    if (b.on && grp.leader && !grp.mover) {
+      for (int i = 0; i < kStages; ++i)
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b.bar + 8u * unsigned(i)) : "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+  }
+  // A round was acquired: later bulk loads must see what the switch wrote.
+  __device__ void acquired() {
+    if (b.on && g->leader) fence_async_global();
+  }
+  __device__ void copy(char* dst, const char* src, unsigned long long bytes) {
+    if (!b.on) {
+      copy16(dst, src, bytes, g->t, g->nt);
+      return;
+    }
+    if (!g->leader || *g->abort) return;
+    if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | bytes) & 15) != 0) {
+      copy16(dst, src, bytes, 0, 1);  // never taken: the gate admits 16-byte aligned calls only
+      return;
+    }
+    bulk_push(*a, b, dst, src, bytes, g->abort);
+  }
+  // Before publishing a step.
+  __device__ void flush() {
+    if (b.on && g->leader && !*g->abort) bulk_drain(*a, b, g->abort);
+  }
+  __device__ void finish() {
+    if (b.on && g->leader) bulk_finish(*a, b);
+  }
+};
+
 // AllReduce. Warp specialization: movers reduce through the switch
 // (NVLink-bound), copiers stream rounds in and out of the scratch
 // (HBM-bound). Rounds of R bytes cut into N slices; rank r owns slice r.
@@ -305,17 +488,20 @@ __device__ __forceinline__ void trace_end(const NvlsArgs& a, const Grp& g) {
 // A(s) reuses buffer s%3 after every rank's B(s-3) (implied by the wait
 // before C(s-2)); B(s) stores into every rank's buffer s%3 after that rank's
 // A(s), hence after its C(s-3). U: multimem requests in flight per thread.
-template <int U, int DT>
-__global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
+template <int U, int DT, bool TMA>
+__global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
+  extern __shared__ __align__(128) unsigned char dsmem[];
   __shared__ int abort_flag;
   __shared__ unsigned long long trace_sh[2][4];
+  __shared__ __align__(8) unsigned long long tma_bar[kStages];
+  __shared__ char* tma_dst[kStages];
+  __shared__ unsigned tma_size[kStages];
   if (threadIdx.x == 0) abort_flag = 0;
   const Grp g = make_group(a, &abort_flag, trace_sh);
   trace_begin(g);
   __syncthreads();
   const int n = a.nranks;
   const unsigned rounds = unsigned((a.bytes + a.round - 1) / a.round);
-  const float inv = 1.0f / float(n);
   if (g.mover) {
     for (unsigned s = 0; s < rounds; ++s) {
       if (!group_wait(a, g, kCopier, a.base + s + 1, -1)) return;
@@ -327,13 +513,15 @@ __global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_con
       strided<U>(
           unsigned(g.t), unsigned(g.nt), unsigned((hi - lo) / 16),
           [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
-          [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, a.avg ? scale(x, DT, inv) : x); });
+          [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, a.scaled ? scale(x, DT, a.mul) : x); });
       group_publish(a, g, a.base + s + 1);
     }
   } else {
+    Copier<TMA> cp(a, g, dsmem, tma_bar, tma_dst, tma_size);
     for (unsigned s = 0; s < rounds + 2; ++s) {
       if (s >= 2) {
-        if (!group_wait(a, g, kMover, a.base + s - 1, -1)) return;
+        if (!group_wait(a, g, kMover, a.base + s - 1, -1)) break;
+        cp.acquired();
         const unsigned i = s - 2;
         const unsigned long long rbase = i * a.round;
         const unsigned long long rlen = min(a.round, a.bytes - rbase);
@@ -341,7 +529,7 @@ __global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_con
         for (int q = 0; q < n; ++q) {
           unsigned long long lo, hi;
           portion(rlen, n, q, &lo, &hi);
-          copy16(a.recv + rbase + lo, buf + lo, hi - lo, g.t, g.nt);
+          cp.copy(a.recv + rbase + lo, buf + lo, hi - lo);
         }
       }
       if (s < rounds) {
@@ -351,11 +539,13 @@ __global__ void __launch_bounds__(768, 1) nvls_allreduce_kernel(const __grid_con
         for (int q = 0; q < n; ++q) {
           unsigned long long lo, hi;
           portion(rlen, n, q, &lo, &hi);
-          copy16(buf + lo, a.send + rbase + lo, hi - lo, g.t, g.nt);
+          cp.copy(buf + lo, a.send + rbase + lo, hi - lo);
         }
       }
+      cp.flush();
       group_publish(a, g, a.base + s + 1);
     }
+    cp.finish();
   }
   trace_end(a, g);
 }
@@ -379,16 +569,20 @@ __device__ __forceinline__ void flat_portion(unsigned long long len, unsigned lo
 //  Broadcast: the root's movers multicast round s (after every rank's
 //    C(s-3)); copiers copy round s out after the root's B(s). The root
 //    sends each byte once.
-template <int U, int DT>
-__global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant__ NvlsArgs a) {
+template <int U, int DT, bool TMA>
+__global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_xfer_kernel(const __grid_constant__ NvlsArgs a) {
+  extern __shared__ __align__(128) unsigned char dsmem[];
   __shared__ int abort_flag;
   __shared__ unsigned long long trace_sh[2][4];
+  __shared__ __align__(8) unsigned long long tma_bar[kStages];
+  __shared__ char* tma_dst[kStages];
+  __shared__ unsigned tma_size[kStages];
   if (threadIdx.x == 0) abort_flag = 0;
   const Grp g = make_group(a, &abort_flag, trace_sh);
   trace_begin(g);
   __syncthreads();
+  Copier<TMA> cp(a, g, dsmem, tma_bar, tma_dst, tma_size);
   const int n = a.nranks;
-  const float inv = 1.0f / float(n);
   const bool bc = a.mode == int(Kind::Broadcast);
   const bool rs = a.mode == int(Kind::ReduceScatter);
   const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)n) & ~31ull);
@@ -406,12 +600,13 @@ __global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant
         strided<U>(
             unsigned(g.t), unsigned(g.nt), unsigned((hi - lo) / 16),
             [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
-            [&](unsigned v, uint4 x) { __stcs(out + v, a.avg ? scale(x, DT, inv) : x); });
+            [&](unsigned v, uint4 x) { __stcs(out + v, a.scaled ? scale(x, DT, a.mul) : x); });
       } else {
-        if (s >= 3 && !group_wait(a, g, kMover, a.base + s - 2, -1)) return;
+        if (s >= 3 && !group_wait(a, g, kMover, a.base + s - 2, -1)) break;
+        cp.acquired();
         char* buf = a.uc + (s % 3) * a.buf_stride;
-        for (int q = 0; q < n; ++q)
-          copy16(buf + q * part + lo, a.send + q * a.slot + s * part + lo, hi - lo, g.t, g.nt);
+        for (int q = 0; q < n; ++q) cp.copy(buf + q * part + lo, a.send + q * a.slot + s * part + lo, hi - lo);
+        cp.flush();
       }
     } else if (g.mover) {
       if (bc && a.rank != a.root) break;  // only the root's movers send
@@ -423,40 +618,43 @@ __global__ void __launch_bounds__(768, 1) nvls_xfer_kernel(const __grid_constant
           [&](unsigned v) { return __ldcs(in + v); },
           [&](unsigned v, uint4 x) { mc_store(base + size_t(v) * 16, x); });
     } else {
-      if (!group_wait(a, g, kMover, a.base + s + 1, bc ? a.root : -1)) return;
+      if (!group_wait(a, g, kMover, a.base + s + 1, bc ? a.root : -1)) break;
+      cp.acquired();
       const char* buf = a.uc + (s % 3) * a.buf_stride;
       if (bc) {
-        copy16(a.recv + s * part + lo, buf + lo, hi - lo, g.t, g.nt);
+        cp.copy(a.recv + s * part + lo, buf + lo, hi - lo);
       } else {
-        for (int q = 0; q < n; ++q)
-          copy16(a.recv + q * a.slot + s * part + lo, buf + q * part + lo, hi - lo, g.t, g.nt);
+        for (int q = 0; q < n; ++q) cp.copy(a.recv + q * a.slot + s * part + lo, buf + q * part + lo, hi - lo);
       }
+      cp.flush();
     }
     group_publish(a, g, a.base + s + 1);
   }
+  if (!g.mover) cp.finish();
   trace_end(a, g);
 }
 
 // ------------------------------------------------------------------ host side
 
-template <int U>
+template <int U, bool TMA>
 const void* pick_dtype(bool ar, DType t) {
   constexpr int F = int(DType::F32), B = int(DType::BF16), H = int(DType::F16);
   switch (t) {
     case DType::BF16:
-      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, B>)
-                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, B>);
+      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, B, TMA>)
+                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, B, TMA>);
     case DType::F16:
-      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, H>)
-                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, H>);
+      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, H, TMA>)
+                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, H, TMA>);
     default:  // fp32, and the raw 16-byte copies of AllGather/Broadcast
-      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, F>)
-                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, F>);
+      return ar ? reinterpret_cast<const void*>(nvls_allreduce_kernel<U, F, TMA>)
+                : reinterpret_cast<const void*>(nvls_xfer_kernel<U, F, TMA>);
   }
 }
 
-const void* pick_kernel(bool ar, bool u8, DType t) {
-  return u8 ? pick_dtype<8>(ar, t) : pick_dtype<4>(ar, t);
+const void* pick_kernel(bool ar, bool u8, bool tma, DType t) {
+  if (tma) return u8 ? pick_dtype<8, true>(ar, t) : pick_dtype<4, true>(ar, t);
+  return u8 ? pick_dtype<8, false>(ar, t) : pick_dtype<4, false>(ar, t);
 }
 
 template <typename Fn>
@@ -521,7 +719,8 @@ struct Context {
   unsigned* status = nullptr;  // mapped pinned host word
   unsigned* status_dev = nullptr;
   unsigned long long epoch = 0;  // progress value every flag reached after the last call
-  std::vector<unsigned long long*> trace;  // per device: blocks x 4 phase-time records
+  std::vector<unsigned long long*> trace;  // per device: blocks x 8 phase-time records
+  bool tma_ok = true;  // every device admits the TMA copier's shared memory
   int blocks = 0;
   bool broken = false;
 };
@@ -654,6 +853,15 @@ bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why
     if (cudaMalloc(&tr, tr_bytes) != cudaSuccess || cudaMemset(tr, 0, tr_bytes) != cudaSuccess)
       return fail("trace records");
     c->trace.push_back(tr);
+    // The TMA copier stages through 128 KiB of dynamic shared memory.
+    for (int ar = 0; ar < 2; ++ar)
+      for (int u8 = 0; u8 < 2; ++u8)
+        for (DType t : {DType::F32, DType::BF16, DType::F16})
+          if (cudaFuncSetAttribute(pick_kernel(ar, u8, true, t), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(kTmaSmem)) != cudaSuccess) {
+            cudaGetLastError();
+            c->tma_ok = false;
+          }
   }
   for (int i = 0; i < n; ++i)
     if (cudaSetDevice(devices[i]) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
@@ -694,12 +902,12 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.nranks = b.nranks;
   a.rank = r;
   a.dtype = int(plan.desc.dtype);
-  a.avg = plan.desc.op == RedOp::Avg;
+  a.scaled = plan.desc.op == RedOp::Avg || plan.desc.op == RedOp::PreMulSum;
+  a.mul = plan.desc.op == RedOp::Avg ? 1.0f / float(b.nranks) : float(plan.desc.scalar);
   a.mode = int(plan.desc.kind);
   a.root = plan.desc.root;
   a.slot = plan.desc.bytes;  // AG send slot / RS receive slot
   a.trace = p.nvls_trace ? c->trace[size_t(r)] : nullptr;
-  (void)dev;
   const bool ar = plan.desc.kind == Kind::AllReduce;
   // The largest progress value this call publishes (every rank the same):
   // the next call's epoch.
@@ -712,12 +920,17 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
     if (part == 0) return cudaErrorInvalidValue;
     steps = (plan.desc.bytes + part - 1) / part;
   }
-  const int threads = p.nvls_threads;
-  a.movers = std::min(p.nvls_movers, threads - 128);
+  // TMA copier: the movers plus one copier warp, with the staging buffers
+  // in dynamic shared memory; SM copier: the configured split.
+  a.tma = p.nvls_tma && c->tma_ok ? 1 : 0;
+  const int threads = a.tma ? std::min(p.nvls_movers, 608) + 32 : p.nvls_threads;
+  a.movers = a.tma ? threads - 32 : std::min(p.nvls_movers, threads - 128);
+  const size_t smem = a.tma ? kTmaSmem : 0;
   void* argv[] = {&a};
-  const void* fn = pick_kernel(ar, p.nvls_unroll >= 8, plan.desc.dtype);
+  const void* fn = pick_kernel(ar, p.nvls_unroll >= 8, a.tma != 0, plan.desc.dtype);
+  (void)dev;
   const cudaError_t e =
-      cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(unsigned(threads)), argv, 0, s);
+      cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(unsigned(threads)), argv, smem, s);
   if (r == b.nranks - 1) c->epoch += steps;
   return e;
 }

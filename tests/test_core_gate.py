@@ -141,6 +141,27 @@ def test_nvls_only_for_sum_and_avg_of_floats():
     assert c.gate_clique(calls, c.KNOWN | c.FIRST_PASS_DONE | c.NVLS) == ("None", "ar_nvls")
 
 
+def test_nvls_premulsum_needs_one_host_scalar():
+    import ctypes as C
+    L = c.lib()
+    L.nb_gate_clique_scalars.argtypes = [C.POINTER(c.Call), C.c_int, C.c_int, C.c_char_p,
+                                         C.POINTER(C.c_int), C.POINTER(C.c_double), C.POINTER(C.c_int)]
+    inv = {v: k for k, v in c.ALGO.items()}
+
+    def gate(scalars, residence):
+        calls = clique_calls(4, dtype="bfloat16", op="premulsum")
+        arr = (c.Call * 4)(*calls)
+        algo = C.c_int(-1)
+        r = L.nb_gate_clique_scalars(arr, 4, c.KNOWN | c.FIRST_PASS_DONE | c.NVLS, b"", C.byref(algo),
+                                     (C.c_double * 4)(*scalars), (C.c_int * 4)(*residence))
+        return c.REASONS[r], inv[algo.value]
+    # One shared host scalar (e.g. 1/N): the switch's sum is scaled once.
+    assert gate([0.25] * 4, [1] * 4) == ("None", "ar_nvls")
+    # Per-rank scalars, or a scalar in device memory: the fused P2P fold.
+    assert gate([0.25, 0.5, 0.25, 0.25], [1] * 4) == ("None", "ar_twoshot")
+    assert gate([0.25] * 4, [1, 0, 1, 1]) == ("None", "ar_twoshot")
+
+
 def test_forced_algorithm():
     calls = clique_calls(8)
     env = {"NCCL_B200_ALGO": "ar=twoshot,bc=pull"}

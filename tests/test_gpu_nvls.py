@@ -24,18 +24,32 @@ comms = nc.comm_init_all(devs)
 streams = [torch.cuda.current_stream(d).cuda_stream for d in devs]
 out = []
 for dtype in (torch.float32, torch.bfloat16):
-    for op in ("sum", "avg"):
+    for op in ("sum", "avg", "premulsum"):
         for count in ((16 << 20), (100 << 20) + 4 * 1024):
             lim = 15 if dtype == torch.bfloat16 else 1 << 18
             xs = [torch.randint(-lim, lim + 1, (count,), device=f"cuda:{{d}}").to(dtype) for d in devs]
             ys = [torch.empty_like(x) for x in xs]
+            ops = None
+            if op == "premulsum":  # one host scalar shared by every rank
+                name = "float32" if dtype == torch.float32 else "bfloat16"
+                ops = [nc.premul_sum(0.5, name, c) for c in comms]
             for it in range(2):
-                collective(nc, "allreduce", xs, ys, comms, streams, op=op)
+                if ops is None:
+                    collective(nc, "allreduce", xs, ys, comms, streams, op=op)
+                else:
+                    with nc.group():
+                        for i, c in enumerate(comms):
+                            nc.all_reduce(xs[i], ys[i], c, streams[i], ops[i])
             for d in devs:
                 torch.cuda.synchronize(d)
+            if ops is not None:
+                for o, c in zip(ops, comms):
+                    nc.redop_destroy(o, c)
             ref = sum(x.to("cuda:0").float() for x in xs)
             if op == "avg":
                 ref = ref / n
+            if op == "premulsum":
+                ref = ref * 0.5
             ok = all(torch.equal(y.to("cuda:0"), ref.to(dtype)) for y in ys)
             out.append("ok" if ok else "bad")
 print("RESULT", supported, ",".join(out), nc.custom_calls(ALGO["ar_nvls"]))

@@ -51,3 +51,18 @@ def test_stress_differential_against_stock_nccl():
     rc, rows, log = run(["--gpus", "2", "--iters", "2", "--scale", "8", "--diff", "--no-boundary",
                          "--filter", "oop"])
     assert rc == 0, log
+
+
+def test_stress_ordering_controls():
+    """A delayed input producer on the last rank, inputs overwritten right
+    after every call, and new caller streams every iteration: all cases
+    must still PASS (reference counterparts: STRESS_DELAY_INPUT_DEVICE,
+    STRESS_TEST_OVERWRITE_AFTER_GROUP, V4_FRESH_STREAMS)."""
+    need_gpus(2)
+    n = min(4, gpu_count())
+    rc, rows, log = run(["--gpus", str(n), "--iters", "3", "--scale", "4", "--no-boundary",
+                         "--filter", "float32", "--delay-input-device", str(n - 1), "--delay-ms", "20",
+                         "--overwrite-after", "--fresh-streams"])
+    assert rc == 0, log
+    assert rows and all(r[4] == "PASS" for r in rows), log
+    assert any(r[6] == "custom" for r in rows), log
