@@ -91,7 +91,7 @@ Policy policy_from_env(const EnvLookup& env) {
   }
   if (parse_int(env("NCCL_B200_NVLS_MIN_RANKS"), &i) && i >= 1) p.nvls_min_ranks = int(i);
   if (parse_size(env("NCCL_B200_NVLS_ROUND"), &z) && z >= kMiB) p.nvls_round_bytes = z;
-  if (parse_int(env("NCCL_B200_NVLS_MOVERS"), &i) && i >= 128 && i <= 896 && i % 128 == 0)
+  if (parse_int(env("NCCL_B200_NVLS_MOVERS"), &i) && i >= 128 && i <= 736 && i % 32 == 0)
     p.nvls_movers = int(i);
   if (parse_int(env("NCCL_B200_NVLS_UNROLL"), &i) && (i == 4 || i == 8)) p.nvls_unroll = int(i);
   if (parse_bool(env("NCCL_B200_NVLS_TRACE"), &b)) p.nvls_trace = b;
