@@ -85,6 +85,11 @@ int nb_emu_plan(int algo, int kind, int dtype, int op, int nranks, uint64_t coun
   Runtime& rtm = rt();
   Plan plan;
   build_plan(Algo(algo), d, rtm.policy, sh, plan);
+  // Gang ops (NVLS, the Broadcast chain) wait on their counterparts inside
+  // the kernel; virtual ranks on one GPU would run them as separate launches
+  // that wait on one another, which is never done.
+  for (const PlanOp& op : plan.ops)
+    if (op.kind == OpKind::NvlsReduce) return int(cudaErrorNotSupported);
   int dev = 0;
   cudaGetDevice(&dev);
   Binding b;

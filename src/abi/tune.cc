@@ -53,6 +53,7 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
     case Kind::AllGather:
       if (nvls && n >= 2) v.push_back({Algo::AgNvls, 0, 0, 0, 0});
       add(Algo::AgPull, 0);
+      add(Algo::AgPush, 0);
       add(Algo::AgPull, 10000);
       break;
     case Kind::Broadcast:
@@ -63,6 +64,7 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
       }
       add(Algo::BcPull, 0);
       add(Algo::BcPull, 10000);
+      v.push_back({Algo::BcRing, 0, 0, 0, 0});
       if (n >= 3) {
         add(Algo::BcChain, 10000, 32, 0);
         add(Algo::BcChain, 10000, 64, 0);

@@ -71,6 +71,8 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
     case Algo::BcChain: return k == Kind::Broadcast;
     case Algo::BcNvls: return k == Kind::Broadcast && nvls_available && nranks >= 2;
     case Algo::AgNvls: return k == Kind::AllGather && nvls_available && nranks >= 2;
+    case Algo::AgPush: return k == Kind::AllGather;
+    case Algo::BcRing: return k == Kind::Broadcast && nranks >= 2;
     case Algo::RsNvls:
       return k == Kind::ReduceScatter && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&

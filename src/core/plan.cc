@@ -17,6 +17,7 @@ void Needs::merge(const Needs& o) {
   phase_events = std::max(phase_events, o.phase_events);
   nvls_bytes = std::max(nvls_bytes, o.nvls_bytes);
   temp_bytes = std::max(temp_bytes, o.temp_bytes);
+  ring = ring || o.ring;
 }
 
 void slice_of(size_t bytes, int parts, int i, size_t* off, size_t* len) {
@@ -451,7 +452,9 @@ void plan_staged(Builder& b, const CliqueDesc& d, const Shares& s, bool allreduc
 // AllGather: rank r pulls every rank's slot into slot q of its output (its
 // own slot too, unless in place). Optional copy-engine and host shares take
 // the middle and the suffix of each peer slot.
-void plan_ag_pull(Builder& b, const CliqueDesc& d, const Shares& s) {
+// push: rank r's kernel stores its own slot into every rank's output (remote
+// stores over NVLink) instead of loading every peer's slot (remote loads).
+void plan_ag_pull(Builder& b, const CliqueDesc& d, const Shares& s, bool push = false) {
   const int n = b.n();
   b.prologue();
   const size_t slot = d.bytes;
@@ -462,11 +465,12 @@ void plan_ag_pull(Builder& b, const CliqueDesc& d, const Shares& s) {
     Loc dst[kMaxRanks], src[kMaxRanks];
     size_t len[kMaxRanks];
     int k = 0;
-    for (int q = 0; q < n; ++q) {
+    for (int i = 0; i < n; ++i) {
+      const int q = push ? (r + i) % n : i;  // pushes start at the own slot, then r+1, r+2, ...
       if (q == r && d.in_place[r]) continue;
       b.touch({Strm::Caller, uint8_t(r), 0}, q);
-      dst[k] = recv_at(r, size_t(q) * slot);
-      src[k] = send_at(q, 0);
+      dst[k] = push ? recv_at(q, size_t(r) * slot) : recv_at(r, size_t(q) * slot);
+      src[k] = push ? send_at(r, 0) : send_at(q, 0);
       // The own slot is a local copy: all of it goes through the SM kernel.
       len[k] = q == r ? slot : sm;
       ++k;
@@ -706,6 +710,22 @@ void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p) {
   b.join();
 }
 
+// Broadcast push chain (exec/ring.cu): one gang op per rank on its caller
+// stream after every rank's input is ready; inside, each rank forwards
+// pieces to its successor as they arrive (in-kernel progress words).
+void plan_bc_ring(Builder& b, const CliqueDesc& d) {
+  const int n = b.n();
+  b.prologue();
+  for (int r = 0; r < n; ++r) {
+    const StreamId cs{Strm::Caller, uint8_t(r), 0};
+    for (int q = 0; q < n; ++q) b.touch(cs, q);
+    b.nvls(cs, r, d.bytes);
+  }
+  b.plan().needs.ring = true;
+  b.plan().sm_bytes += d.bytes * size_t(n - 1);
+  b.join();
+}
+
 // One rank: every collective except a scaled one (PreMulSum) is a copy of
 // the input into the output, done by the copy engine on the caller stream
 // (a device-to-device copy streams HBM at the copy engine's full rate).
@@ -730,6 +750,8 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
     case Algo::ArNvls: plan_ar_nvls(b, d, p); break;
     case Algo::RsPull: plan_rs_pull(b, d, s); break;
     case Algo::AgPull: plan_ag_pull(b, d, s); break;
+    case Algo::AgPush: plan_ag_pull(b, d, s, true); break;
+    case Algo::BcRing: plan_bc_ring(b, d); break;
     case Algo::BcPull: plan_bc_pull(b, d, s); break;
     case Algo::BcScatter: plan_bc_scatter(b, d, s); break;
     case Algo::ArStaged: plan_staged(b, d, s, true); break;

@@ -98,6 +98,7 @@ struct Needs {
   uint16_t phase_events = 0;   // Phase(dev, index) indices per rank
   size_t nvls_bytes = 0;       // multicast scratch per GPU
   size_t temp_bytes = 0;       // device scratch per GPU (staged routes)
+  bool ring = false;           // progress words for the in-kernel chain
   void merge(const Needs& o);
 };
 

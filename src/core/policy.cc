@@ -64,6 +64,8 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else if (a == "nvls" && *kind == Kind::Broadcast) *algo = Algo::BcNvls;
   else if (a == "nvls" && *kind == Kind::AllGather) *algo = Algo::AgNvls;
   else if (a == "nvls" && *kind == Kind::ReduceScatter) *algo = Algo::RsNvls;
+  else if (a == "push" && *kind == Kind::AllGather) *algo = Algo::AgPush;
+  else if (a == "ring" && *kind == Kind::Broadcast) *algo = Algo::BcRing;
   else return false;
   return true;
 }
@@ -96,6 +98,8 @@ Policy policy_from_env(const EnvLookup& env) {
   if (parse_int(env("NCCL_B200_NVLS_UNROLL"), &i) && (i == 4 || i == 8)) p.nvls_unroll = int(i);
   if (parse_bool(env("NCCL_B200_NVLS_TRACE"), &b)) p.nvls_trace = b;
   if (parse_bool(env("NCCL_B200_NVLS_TMA"), &b)) p.nvls_tma = b;
+  if (parse_size(env("NCCL_B200_RING_CHUNK"), &z) && z >= 4096 && z <= (64u << 20) && z % 32 == 0)
+    p.ring_chunk = z;
   if (parse_bool(env("NCCL_B200_NVTX"), &b)) p.nvtx = b;
   if (parse_int(env("NCCL_B200_NVLS_THREADS"), &i) && (i == 512 || i == 640 || i == 768))
     p.nvls_threads = int(i);

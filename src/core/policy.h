@@ -33,6 +33,7 @@ struct Policy {
   int nvls_unroll = 4;              // multimem requests in flight per switch-side thread
   bool nvls_trace = false;          // per-block phase timing in the NVLS kernels
   bool nvls_tma = true;             // NVLS copier: TMA bulk pipeline (else SM copy warps)
+  size_t ring_chunk = 256 * 1024;   // Broadcast chain: bytes per block per step
   bool nvtx = false;                // NVTX range per custom submission
   Algo force_algo[size_t(Kind::Count)] = {Algo::Fallback, Algo::Fallback, Algo::Fallback,
                                           Algo::Fallback};  // Fallback = choose

@@ -49,6 +49,8 @@ enum class Algo : uint8_t {
   BcNvls,      // the root multicasts through the switch (multimem.st)
   AgNvls,      // every rank multicasts its slot through the switch
   RsNvls,      // every rank multimem.ld_reduces its own slot
+  AgPush,      // every rank stores its slot into every rank's output
+  BcRing,      // pipelined push chain with in-kernel progress words
   Count
 };
 

@@ -17,7 +17,8 @@ SMALL = {"NCCL_B200_MIN_HOST_BYTES": "4096", "NCCL_B200_HOST_PIECE": "262144",
 CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", "allgather"),
          ("bc_pull", "broadcast"), ("bc_scatter", "broadcast"), ("ar_staged", "allreduce"),
          ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ar_nvls", "allreduce"),
-         ("bc_nvls", "broadcast"), ("ag_nvls", "allgather"), ("rs_nvls", "reducescatter")]
+         ("bc_nvls", "broadcast"), ("ag_nvls", "allgather"), ("rs_nvls", "reducescatter"),
+         ("ag_push", "allgather"), ("bc_ring", "broadcast")]
 
 
 def test_baseline_cpu_plumbing_config():

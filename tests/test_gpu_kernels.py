@@ -138,7 +138,7 @@ def test_copy_segments_alignment():
 
 CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", "allgather"),
          ("bc_pull", "broadcast"), ("bc_scatter", "broadcast"), ("ar_staged", "allreduce"),
-         ("rs_staged", "reducescatter"), ("bc_chain", "broadcast")]
+         ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ag_push", "allgather")]
 
 
 @pytest.mark.parametrize("algo,kind", CASES)

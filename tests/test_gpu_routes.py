@@ -1,0 +1,95 @@
+"""Routes forced through the environment, in child processes, against a
+torch reference: the AllGather push route and the Broadcast push chain
+(in-kernel progress words), out of place and in place, every root, odd
+sizes and bf16; and the chain's bounded wait (a progress target nothing
+reaches: the waiting kernels give up, record the status and return)."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+from conftest import REPO, need_gpus
+
+pytestmark = pytest.mark.gpu
+
+CHILD = r"""
+import sys, torch
+sys.path.insert(0, {repo!r}); sys.path.insert(0, {repo!r} + "/tests")
+from scc26_nccl_shim_b200.parallel.nccl import Nccl
+from scc26_nccl_shim_b200._core import ALGO
+from test_gpu_abi import run_kind
+n = {n}
+devs = list(range(n))
+nc = Nccl("interposer")
+comms = nc.comm_init_all(devs)
+for c in ((24 << 20) // 4, (24 << 20) // 4 + 3, 1000003):
+    for inplace in (False, True):
+        run_kind(nc, "allgather", comms, devs, c, inplace=inplace)
+    for root in sorted({{0, n - 1, n // 2}}):
+        run_kind(nc, "broadcast", comms, devs, c * 2 + 1, root=root)
+        run_kind(nc, "broadcast", comms, devs, c, inplace=True, root=root)
+run_kind(nc, "allgather", comms, devs, (24 << 20) // 4, dtype=torch.bfloat16)
+run_kind(nc, "broadcast", comms, devs, (24 << 20) // 4, dtype=torch.bfloat16, root=n - 1)
+print("RESULT", nc.custom_calls(ALGO["ag_push"]), nc.custom_calls(ALGO["bc_ring"]))
+for c in comms:
+    nc.comm_destroy(c)
+"""
+
+
+@pytest.mark.parametrize("n", [2, 3, 4, 8])
+def test_forced_push_routes(n):
+    need_gpus(n)
+    env = dict(os.environ, NCCL_B200_ALGO="ag=push,bc=ring", NCCL_B200_TUNE="0",
+               NCCL_B200_FIRST_PASS="0", NCCL_B200_AG_MIN="1K", NCCL_B200_BC_MIN="1K",
+               NCCL_B200_RING_CHUNK="64K")
+    r = subprocess.run([sys.executable, "-c", CHILD.format(repo=REPO, n=n)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    assert int(line[1]) >= 7 and int(line[2]) >= 8, line
+
+
+TIMEOUT_CHILD = r"""
+import sys, ctypes as C, torch
+sys.path.insert(0, {repo!r})
+from scc26_nccl_shim_b200.parallel.nccl import Nccl, collective, NcclError
+nc = Nccl("interposer")
+devs = [0, 1, 2]
+arr = (C.c_int * 3)(*devs)
+comms = nc.comm_init_all(devs)
+xs = [torch.full((16 << 20,), float(d + 1), device=f"cuda:{{d}}") for d in devs]
+ys = [torch.empty_like(x) for x in xs]
+s = [torch.cuda.current_stream(d).cuda_stream for d in devs]
+out = []
+for i in range(3):
+    try:
+        collective(nc, "broadcast", xs, ys, comms, s, root=0)
+        for d in devs: torch.cuda.synchronize(d)
+        out.append("ok" if all(torch.equal(y, xs[0].to(y.device)) for y in ys) else "stale")
+    except NcclError as e:
+        for d in devs: torch.cuda.synchronize(d)
+        out.append("err%d" % e.code)
+    out.append("s%d" % nc.shim.nb_ring_status(arr, 3))
+print("RESULT", ",".join(out), nc.shim.nb_poisoned())
+"""
+
+
+def test_ring_bounded_wait_reports_timeout():
+    """Three GPUs (the middle rank of the chain waits): with a progress target
+    nothing reaches, the middle rank's kernel gives up after 200 ms and sets
+    the status word; the next call reports ncclUnhandledCudaError and
+    poisons the custom paths; the call after runs on NCCL. No GPU faults."""
+    need_gpus(3)
+    env = dict(os.environ, NCCL_B200_ALGO="bc=ring", NCCL_B200_TUNE="0", NCCL_B200_FIRST_PASS="0",
+               NCCL_B200_TEST_NVLS_SKEW="1000", NCCL_B200_TIMEOUT_MS="200")
+    r = subprocess.run([sys.executable, "-c", TIMEOUT_CHILD.format(repo=REPO)], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    seq = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    calls = seq[1].split(",")
+    # call 1: the middle rank's wait expires (status 1; its successor is stale)
+    assert calls[1] == "s1", calls
+    assert calls[2] == "err1", calls
+    assert calls[4] == "ok", calls
+    assert seq[2] == "1"
