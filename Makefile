@@ -13,7 +13,7 @@ CORE_SRC := $(wildcard src/core/*.cc)
 EXEC_SRC := $(wildcard src/exec/*.cc)
 ABI_SRC := $(wildcard src/abi/*.cc)
 CU_SRC := $(wildcard src/kernels/*.cu) $(wildcard src/exec/*.cu)
-HDRS := $(wildcard src/*/*.h)
+HDRS := $(wildcard src/*/*.h) $(wildcard src/*/*.cuh)
 
 BUILD_ID := $(shell cat $(CORE_SRC) $(EXEC_SRC) $(ABI_SRC) $(CU_SRC) $(HDRS) | sha256sum | cut -c1-16)
 

@@ -27,6 +27,7 @@
 #include "core/plan.h"
 #include "exec/calib.h"
 #include "exec/nvls.h"
+#include "exec/pushred.h"
 #include "exec/ring.h"
 
 #ifndef NB_BUILD_ID
@@ -719,6 +720,7 @@ size_t nb_summary_text(char* buf, size_t cap) {
 int nb_nvls_supported(const int* devices, int n) { return nvls_supported(devices, n) ? 1 : 0; }
 unsigned nb_nvls_status(const int* devices, int n) { return nvls_status(devices, n); }
 unsigned nb_ring_status(const int* devices, int n) { return ring_status(devices, n); }
+unsigned nb_pushred_status(const int* devices, int n) { return pushred_status(devices, n); }
 int nb_nvls_trace(const int* devices, int n, int rank, double* out6, int reset) {
   return nvls_trace_read(devices, n, rank, out6, reset != 0);
 }

@@ -42,10 +42,12 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
       add(Algo::ArStaged, 0, 128, 2);
       add(Algo::ArStaged, 0, 256, 2);
       if (nvls && n >= 2) v.push_back({Algo::ArNvls, 0, 0, 0, 0});
+      v.push_back({Algo::ArPush, 0, 0, 0, 0});
       break;
     case Kind::ReduceScatter:
       if (nvls && n >= 2) v.push_back({Algo::RsNvls, 0, 0, 0, 0});
       add(Algo::RsPull, 0);
+      v.push_back({Algo::RsPush, 0, 0, 0, 0});
       add(Algo::RsStaged, 0, 64, 3);
       add(Algo::RsStaged, 0, 128, 2);
       add(Algo::RsStaged, 0, 256, 2);

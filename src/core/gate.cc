@@ -73,6 +73,10 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
     case Algo::AgNvls: return k == Kind::AllGather && nvls_available && nranks >= 2;
     case Algo::AgPush: return k == Kind::AllGather;
     case Algo::BcRing: return k == Kind::Broadcast && nranks >= 2;
+    case Algo::RsPush:
+    case Algo::ArPush:
+      return k == (a == Algo::RsPush ? Kind::ReduceScatter : Kind::AllReduce) && nranks >= 2 &&
+             (t == DType::F32 || t == DType::F16 || t == DType::BF16);
     case Algo::RsNvls:
       return k == Kind::ReduceScatter && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&

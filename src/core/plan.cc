@@ -18,6 +18,7 @@ void Needs::merge(const Needs& o) {
   nvls_bytes = std::max(nvls_bytes, o.nvls_bytes);
   temp_bytes = std::max(temp_bytes, o.temp_bytes);
   ring = ring || o.ring;
+  pushred = pushred || o.pushred;
 }
 
 void slice_of(size_t bytes, int parts, int i, size_t* off, size_t* len) {
@@ -726,6 +727,22 @@ void plan_bc_ring(Builder& b, const CliqueDesc& d) {
   b.join();
 }
 
+// Push-reduce ReduceScatter / AllReduce (exec/pushred.cu): one gang op per
+// rank on its caller stream after every rank's input is ready.
+void plan_pushred(Builder& b, const CliqueDesc& d) {
+  const int n = b.n();
+  b.prologue();
+  for (int r = 0; r < n; ++r) {
+    const StreamId cs{Strm::Caller, uint8_t(r), 0};
+    for (int q = 0; q < n; ++q) b.touch(cs, q);
+    b.nvls(cs, r, d.bytes);
+  }
+  b.plan().needs.pushred = true;
+  const size_t moved = d.kind == Kind::AllReduce ? d.bytes * size_t(2 * (n - 1)) : d.bytes * size_t(n - 1) * size_t(n);
+  b.plan().sm_bytes += moved;
+  b.join();
+}
+
 // One rank: every collective except a scaled one (PreMulSum) is a copy of
 // the input into the output, done by the copy engine on the caller stream
 // (a device-to-device copy streams HBM at the copy engine's full rate).
@@ -752,6 +769,7 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
     case Algo::AgPull: plan_ag_pull(b, d, s); break;
     case Algo::AgPush: plan_ag_pull(b, d, s, true); break;
     case Algo::BcRing: plan_bc_ring(b, d); break;
+    case Algo::RsPush: case Algo::ArPush: plan_pushred(b, d); break;
     case Algo::BcPull: plan_bc_pull(b, d, s); break;
     case Algo::BcScatter: plan_bc_scatter(b, d, s); break;
     case Algo::ArStaged: plan_staged(b, d, s, true); break;

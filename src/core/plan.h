@@ -99,6 +99,7 @@ struct Needs {
   size_t nvls_bytes = 0;       // multicast scratch per GPU
   size_t temp_bytes = 0;       // device scratch per GPU (staged routes)
   bool ring = false;           // progress words for the in-kernel chain
+  bool pushred = false;        // scratch and progress words of the push-reduce engine
   void merge(const Needs& o);
 };
 

@@ -66,6 +66,8 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else if (a == "nvls" && *kind == Kind::ReduceScatter) *algo = Algo::RsNvls;
   else if (a == "push" && *kind == Kind::AllGather) *algo = Algo::AgPush;
   else if (a == "ring" && *kind == Kind::Broadcast) *algo = Algo::BcRing;
+  else if (a == "push" && *kind == Kind::ReduceScatter) *algo = Algo::RsPush;
+  else if (a == "push" && *kind == Kind::AllReduce) *algo = Algo::ArPush;
   else return false;
   return true;
 }

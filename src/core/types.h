@@ -51,6 +51,8 @@ enum class Algo : uint8_t {
   RsNvls,      // every rank multimem.ld_reduces its own slot
   AgPush,      // every rank stores its slot into every rank's output
   BcRing,      // pipelined push chain with in-kernel progress words
+  RsPush,      // senders store into owners' scratch; owners fold (stores only)
+  ArPush,      // RsPush, then owners store the result into every output
   Count
 };
 

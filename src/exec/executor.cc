@@ -5,6 +5,7 @@
 #include <cstring>
 
 #include "exec/nvls.h"
+#include "exec/pushred.h"
 #include "exec/ring.h"
 #include "kernels/kernels.h"
 
@@ -232,6 +233,7 @@ bool Executor::ensure(const Needs& needs, const int* devices, int n, std::string
     return false;
   if (needs.nvls_bytes > 0 && !nvls_ensure(devices, n, needs.nvls_bytes, why)) return false;
   if (needs.ring && !ring_ensure(devices, n, why)) return false;
+  if (needs.pushred && !pushred_ensure(devices, n, why)) return false;
   return true;
 }
 
@@ -342,6 +344,7 @@ cudaError_t Executor::submit(const PlanOp& op, const Plan& plan, const Binding& 
     case OpKind::NvlsReduce:
       launches_.fetch_add(1, std::memory_order_relaxed);
       if (plan.algo == Algo::BcRing) return ring_launch(op, plan, b, policy_, s);
+      if (plan.algo == Algo::RsPush || plan.algo == Algo::ArPush) return pushred_launch(op, plan, b, policy_, s);
       return nvls_launch(op, plan, b, policy_, s, dev);
     default:
       return cudaErrorNotSupported;

@@ -18,7 +18,8 @@ CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", 
          ("bc_pull", "broadcast"), ("bc_scatter", "broadcast"), ("ar_staged", "allreduce"),
          ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ar_nvls", "allreduce"),
          ("bc_nvls", "broadcast"), ("ag_nvls", "allgather"), ("rs_nvls", "reducescatter"),
-         ("ag_push", "allgather"), ("bc_ring", "broadcast")]
+         ("ag_push", "allgather"), ("bc_ring", "broadcast"), ("rs_push", "reducescatter"),
+         ("ar_push", "allreduce")]
 
 
 def test_baseline_cpu_plumbing_config():

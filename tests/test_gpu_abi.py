@@ -59,8 +59,9 @@ def run_kind(nc, kind, comms, devs, count, dtype=torch.float32, op="sum", inplac
     for r in range(n):
         if kind == "allreduce":
             ref = inputs[0].float()
-            for x in inputs[1:]:
-                ref = ref + x.float()
+            for x in inputs[1:]:  # rank order, fp32, like the fused fold
+                ref = {"max": torch.maximum, "min": torch.minimum,
+                       "prod": torch.mul}.get(op, torch.add)(ref, x.float())
             ref = (ref / n if op == "avg" else ref).to(dtype)
         elif kind == "reducescatter":
             ref = inputs[0][r * count:(r + 1) * count].float()

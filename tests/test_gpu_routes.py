@@ -50,6 +50,45 @@ def test_forced_push_routes(n):
     assert int(line[1]) >= 7 and int(line[2]) >= 8, line
 
 
+PR_CHILD = r"""
+import sys, torch
+sys.path.insert(0, {repo!r}); sys.path.insert(0, {repo!r} + "/tests")
+from scc26_nccl_shim_b200.parallel.nccl import Nccl
+from scc26_nccl_shim_b200._core import ALGO
+from test_gpu_abi import run_kind
+n = {n}
+devs = list(range(n))
+nc = Nccl("interposer")
+comms = nc.comm_init_all(devs)
+for c in ((40 << 20) // 4, (40 << 20) // 4 + 5, 3000011):
+    for inplace in (False, True):
+        run_kind(nc, "allreduce", comms, devs, c, inplace=inplace)
+    rs = c - c % 4
+    run_kind(nc, "reducescatter", comms, devs, rs // n - (rs // n) % 4)
+    run_kind(nc, "reducescatter", comms, devs, rs // n - (rs // n) % 4, inplace=True)
+for dt in (torch.bfloat16, torch.float16):
+    run_kind(nc, "allreduce", comms, devs, (24 << 20) // 4, dtype=dt)
+    run_kind(nc, "reducescatter", comms, devs, (24 << 20) // 4 // n // 8 * 8, dtype=dt)
+for op in ("avg", "max", "min", "prod"):
+    run_kind(nc, "allreduce", comms, devs, (16 << 20) // 4 + 7, op=op)
+print("RESULT", nc.custom_calls(ALGO["ar_push"]), nc.custom_calls(ALGO["rs_push"]))
+for c in comms:
+    nc.comm_destroy(c)
+"""
+
+
+@pytest.mark.parametrize("n", [2, 3, 4, 8])
+def test_forced_push_reduce(n):
+    need_gpus(n)
+    env = dict(os.environ, NCCL_B200_ALGO="ar=push,rs=push", NCCL_B200_TUNE="0",
+               NCCL_B200_FIRST_PASS="0", NCCL_B200_AR_MIN="1K", NCCL_B200_RS_MIN="1K")
+    r = subprocess.run([sys.executable, "-c", PR_CHILD.format(repo=REPO, n=n)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    assert int(line[1]) >= 12 and int(line[2]) >= 8, line
+
+
 TIMEOUT_CHILD = r"""
 import sys, ctypes as C, torch
 sys.path.insert(0, {repo!r})
