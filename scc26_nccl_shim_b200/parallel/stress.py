@@ -284,7 +284,11 @@ def main(argv=None) -> int:
     p.add_argument("--overwrite-after", action="store_true",
                    help="overwrite the inputs on the caller streams right after every call")
     p.add_argument("--fresh-streams", action="store_true", help="new caller streams every iteration")
+    p.add_argument("--algo", default="", help="force routes, e.g. ar=push,rs=push,ag=push,bc=ring "
+                   "(the library reads it once, when it loads)")
     a = p.parse_args(argv)
+    if a.algo:
+        os.environ["NCCL_B200_ALGO"] = a.algo
     devs = list(range(a.gpus))
     nc = Nccl("interposer")
     ref = Nccl("nccl") if a.diff else None

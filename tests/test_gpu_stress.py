@@ -66,3 +66,16 @@ def test_stress_ordering_controls():
     assert rc == 0, log
     assert rows and all(r[4] == "PASS" for r in rows), log
     assert any(r[6] == "custom" for r in rows), log
+
+
+@pytest.mark.parametrize("algo", ["ar=push,rs=push,ag=push,bc=ring", "ar=nvls,rs=nvls,ag=nvls,bc=nvls"])
+def test_stress_gang_routes(algo):
+    """The in-kernel-synchronized routes under the back-to-back harness on
+    up to four GPUs, with the ordering controls on."""
+    need_gpus(2)
+    n = min(4, gpu_count())
+    rc, rows, log = run(["--gpus", str(n), "--iters", "3", "--scale", "4", "--no-boundary",
+                         "--filter", "_", "--algo", algo, "--overwrite-after", "--fresh-streams"],
+                        env={"NCCL_B200_NVLS": "on"})
+    assert rc == 0, log
+    assert rows and all(r[4] == "PASS" for r in rows), log
