@@ -41,8 +41,8 @@ namespace {
 
 using namespace kfold;
 
-constexpr int kDepth = 3;                  // rounds of scratch per (sender, block)
-constexpr unsigned long long kPiece = 65536;  // C: bytes per block per round per segment
+constexpr int kDepth = 2;                   // rounds of scratch per (sender, block)
+constexpr unsigned long long kPiece = 262144;  // C: bytes per block per round per segment
 
 struct PrArgs {
   const char* send;
@@ -191,14 +191,25 @@ __global__ void __launch_bounds__(512, 1) pushred_kernel(const __grid_constant__
       src[q] = q == r ? a.send + a.seg_off[r] + cs : a.scratch[r] + slot_off(q, j);
     const unsigned nv = unsigned(len / 16);
     const int ndst = a.allreduce ? N : 1;
-    for (unsigned v = t; v < nv; v += nt) {
-      uint4 x[N];
+    // About eight 16-byte loads in flight per thread (the sources are local).
+    constexpr int U = 8 / N > 0 ? 8 / N : 1;
+    for (unsigned v0 = t; v0 < nv; v0 += nt * U) {
+      uint4 x[U][N];
 #pragma unroll
-      for (int q = 0; q < N; ++q) x[q] = reinterpret_cast<const uint4*>(src[q])[v];
-      const uint4 y = fold_vec<T, N>(x, a.op, a.nranks, s);
-      for (int d = 0; d < ndst; ++d) {
-        const int q = a.allreduce ? (r + d) % N : r;  // own output first, then r+1, ...
-        reinterpret_cast<uint4*>(a.recv[q] + a.out_off + cs)[v] = y;
+      for (int u = 0; u < U; ++u)
+        if (v0 + u * nt < nv) {
+#pragma unroll
+          for (int q = 0; q < N; ++q) x[u][q] = reinterpret_cast<const uint4*>(src[q])[v0 + u * nt];
+        }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const unsigned v = v0 + u * nt;
+        if (v >= nv) break;
+        const uint4 y = fold_vec<T, N>(x[u], a.op, a.nranks, s);
+        for (int d = 0; d < ndst; ++d) {
+          const int q = a.allreduce ? (r + d) % N : r;  // own output first, then r+1, ...
+          reinterpret_cast<uint4*>(a.recv[q] + a.out_off + cs)[v] = y;
+        }
       }
     }
     // Trailing elements of a segment that do not fill a vector.
