@@ -744,13 +744,17 @@ void plan_pushred(Builder& b, const CliqueDesc& d) {
 }
 
 // One rank: every collective except a scaled one (PreMulSum) is a copy of
-// the input into the output, done by the copy engine on the caller stream
-// (a device-to-device copy streams HBM at the copy engine's full rate).
+// the input into the output on the caller stream: the SM copy kernel, which
+// takes the TMA bulk path for a large copy within one GPU.
 void plan_single(Builder& b, const CliqueDesc& d) {
   b.prologue();
   const StreamId cl{Strm::Caller, 0, 0};
   b.touch(cl, 0);
-  if (!d.in_place[0]) b.ce_copy(cl, recv_at(0, 0), send_at(0, 0), d.bytes);
+  if (!d.in_place[0]) {
+    const Loc dst = recv_at(0, 0), src = send_at(0, 0);
+    const size_t len = d.bytes;
+    b.sm_copy(cl, &dst, &src, &len, 1);
+  }
   b.join();
 }
 

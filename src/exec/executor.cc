@@ -303,10 +303,16 @@ cudaError_t Executor::submit(const PlanOp& op, const Plan& plan, const Binding& 
     case OpKind::SmCopy: {
       CopyLaunch c;
       c.nseg = op.nsrc;
+      c.local = true;
+      const auto on_device = [&](const Loc& l) {
+        return (l.buf == Buf::Send || l.buf == Buf::Recv || l.buf == Buf::Temp) &&
+               b.device[l.dev] == b.device[op.stream.dev];
+      };
       for (int i = 0; i < op.nsrc; ++i) {
         c.src[i] = bind_loc(op.src[i], b);
         c.dst[i] = bind_loc(op.dst[i], b);
         c.len[i] = op.len[i];
+        c.local = c.local && on_device(op.src[i]) && on_device(op.dst[i]);
       }
       launches_.fetch_add(1, std::memory_order_relaxed);
       return launch_copy(c, shape_for(op.bytes, sm_count(dev), policy_.blocks_per_sm, policy_.threads), s);

@@ -148,6 +148,107 @@ __global__ void __launch_bounds__(512, VB == 32 ? 1 : 2) reduce_kernel(const __g
   }
 }
 
+// Local bulk copy on the tensor memory accelerator: one thread per block
+// streams 32 KiB chunks through four shared-memory stages with cp.async.bulk
+// (global -> shared completing on an mbarrier, shared -> global in bulk
+// groups), so 128 KiB per SM are in flight without occupying registers.
+// Both buffers are this GPU's own memory (no peer memory, no cluster
+// multicast). Every wait is bounded by %globaltimer.
+constexpr int kTmaStages = 4;
+constexpr unsigned kTmaChunk = 32768;
+constexpr size_t kTmaCopySmem = size_t(kTmaStages) * kTmaChunk;
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool mbar_done(unsigned bar, unsigned parity) {
+  unsigned done;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__global__ void __launch_bounds__(32, 1) tma_copy_kernel(const char* src, char* dst, unsigned long long len,
+                                                         unsigned long long timeout_ns) {
+  extern __shared__ __align__(128) unsigned char stage[];
+  __shared__ __align__(8) unsigned long long bars[kTmaStages];
+  const unsigned long long body = len & ~15ull;
+  const unsigned long long nchunks = (body + kTmaChunk - 1) / kTmaChunk;
+  if (threadIdx.x == 0) {
+    const unsigned smem = unsigned(__cvta_generic_to_shared(stage));
+    const unsigned bar0 = unsigned(__cvta_generic_to_shared(bars));
+    for (int i = 0; i < kTmaStages; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8u * unsigned(i)) : "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // This block's chunks: blockIdx.x, blockIdx.x + gridDim.x, ...; the i-th
+    // of them uses stage i % kTmaStages.
+    unsigned long long mine = nchunks > blockIdx.x ? (nchunks - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    unsigned long long issued = 0, stored = 0;
+    const unsigned long long t0 = now_ns();
+    bool ok = true;
+    auto chunk_off = [&](unsigned long long i) { return (blockIdx.x + i * gridDim.x) * (unsigned long long)kTmaChunk; };
+    auto retire = [&]() {
+      const unsigned st = unsigned(stored % kTmaStages);
+      while (!mbar_done(bar0 + 8u * st, unsigned((stored / kTmaStages) & 1)))
+        if (now_ns() - t0 > timeout_ns) return false;
+      const unsigned long long off = chunk_off(stored);
+      const unsigned size = unsigned(min((unsigned long long)kTmaChunk, body - off));
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + off),
+                   "r"(smem + st * kTmaChunk), "r"(size)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      ++stored;
+      return true;
+    };
+    while (ok && issued < mine) {
+      if (issued >= kTmaStages) {
+        const unsigned long long j = issued - kTmaStages;  // the stage's previous chunk
+        while (ok && stored <= j) ok = retire();
+        // That chunk's store must have finished reading shared memory; the
+        // stores issued after it may still be reading.
+        switch (unsigned(stored - 1 - j)) {
+          case 0: asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); break;
+          case 1: asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); break;
+          case 2: asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory"); break;
+          default: asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); break;
+        }
+      }
+      if (!ok) break;
+      const unsigned st = unsigned(issued % kTmaStages);
+      const unsigned long long off = chunk_off(issued);
+      const unsigned size = unsigned(min((unsigned long long)kTmaChunk, body - off));
+      const unsigned bar = bar0 + 8u * st;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(size) : "memory");
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem + st * kTmaChunk),
+          "l"(src + off), "r"(size), "r"(bar)
+          : "memory");
+      ++issued;
+      // Store every chunk whose load already landed, so stores start early.
+      while (ok && stored < issued &&
+             mbar_done(bar0 + 8u * unsigned(stored % kTmaStages), unsigned((stored / kTmaStages) & 1)))
+        ok = retire();
+    }
+    while (ok && stored < issued) ok = retire();
+    // On a timeout, let loads still in flight land before the block exits.
+    for (unsigned long long k = stored; !ok && k < issued; ++k)
+      while (!mbar_done(bar0 + 8u * unsigned(k % kTmaStages), unsigned((k / kTmaStages) & 1)) &&
+             now_ns() - t0 < 2 * timeout_ns) {
+      }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  }
+  // Bytes after the last whole 16-byte unit.
+  if (blockIdx.x == 0)
+    for (unsigned long long i = body + threadIdx.x; i < len; i += blockDim.x) dst[i] = src[i];
+}
+
 // Tiles are interleaved across segments (tile t belongs to segment t % nseg)
 // so that at any moment every source is being read: pulls from several peers
 // spread over all their links instead of queueing on one peer at a time.
@@ -293,6 +394,27 @@ cudaError_t launch_reduce(const ReduceLaunch& r, LaunchShape shape, cudaStream_t
 
 cudaError_t launch_copy(const CopyLaunch& c, LaunchShape shape, cudaStream_t stream) {
   if (c.nseg < 1 || c.nseg > kMaxRanks) return cudaErrorInvalidValue;
+  // One large copy within this GPU's memory: the TMA bulk copy.
+  if (c.local && c.nseg == 1 && c.len[0] >= (4u << 20) &&
+      ((reinterpret_cast<uintptr_t>(c.src[0]) | reinterpret_cast<uintptr_t>(c.dst[0])) & 15) == 0) {
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    static bool opted[64] = {};
+    if (e == cudaSuccess && dev < 64 && !opted[dev]) {
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tma_copy_kernel),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTmaCopySmem));
+      opted[dev] = e == cudaSuccess;
+    }
+    if (e != cudaSuccess) return e;
+    const unsigned long long timeout_ns = 2000000000ull;
+    const char* src = static_cast<const char*>(c.src[0]);
+    char* dst = static_cast<char*>(c.dst[0]);
+    unsigned long long len = c.len[0];
+    void* argv[] = {&src, &dst, &len, const_cast<unsigned long long*>(&timeout_ns)};
+    return cudaLaunchKernel(reinterpret_cast<const void*>(tma_copy_kernel), dim3(unsigned(sms)), dim3(32),
+                            argv, kTmaCopySmem, stream);
+  }
   KCopyArgs k{};
   k.nseg = c.nseg;
   unsigned long long tiles = 0;

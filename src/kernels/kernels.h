@@ -36,6 +36,7 @@ struct CopyLaunch {
   void* dst[kMaxRanks] = {};
   size_t len[kMaxRanks] = {};
   int nseg = 0;
+  bool local = false;  // every buffer is in the launching GPU's own device memory
 };
 
 struct LaunchShape {

@@ -62,7 +62,9 @@ def run_kind(nc, kind, comms, devs, count, dtype=torch.float32, op="sum", inplac
             for x in inputs[1:]:  # rank order, fp32, like the fused fold
                 ref = {"max": torch.maximum, "min": torch.minimum,
                        "prod": torch.mul}.get(op, torch.add)(ref, x.float())
-            ref = (ref / n if op == "avg" else ref).to(dtype)
+            if op == "avg":  # a true division (torch's tensor / scalar multiplies by 1/n)
+                ref = torch.div(ref, torch.full_like(ref, float(n)))
+            ref = ref.to(dtype)
         elif kind == "reducescatter":
             ref = inputs[0][r * count:(r + 1) * count].float()
             for x in inputs[1:]:
@@ -87,6 +89,9 @@ def test_one_rank_clique(nc):
         run_kind(nc, kind, comms, devs, c, inplace=True)
         after = sum(nc.custom_calls(a) for a in ALGO.values() if a)
         assert after > before, kind
+    # A length that ends inside a 16-byte unit (the bulk copy's byte tail).
+    run_kind(nc, "allreduce", comms, devs, count + 1, dtype=torch.bfloat16)
+    run_kind(nc, "broadcast", comms, devs, (48 << 20) // 4 + 3, dtype=torch.bfloat16)
     nc.comm_destroy(comms[0])
 
 
