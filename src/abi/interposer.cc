@@ -700,6 +700,19 @@ int nb_fallbacks(int reason) {
   return reason >= 0 && reason < int(Reason::Count) ? int(rt().summary.fallbacks(Reason(reason))) : -1;
 }
 int nb_poisoned() { return rt().poisoned ? 1 : 0; }
+// The blocking-configuration check of InitRankConfig for a config built from
+// NCCL's initializer with the given fields overridden (size 0: keep the
+// initializer's; null config when use_config is 0). 1 = a blocking
+// communicator the interposer may drive.
+int nb_blocking_config(int use_config, size_t size, unsigned magic, unsigned version, int blocking) {
+  if (!use_config) return blocking_configuration(nullptr) ? 1 : 0;
+  ncclConfig_t c = NCCL_CONFIG_INITIALIZER;
+  if (size) c.size = size;
+  c.magic = magic;
+  c.version = version;
+  c.blocking = blocking;
+  return blocking_configuration(&c) ? 1 : 0;
+}
 uint64_t nb_kernel_launches() { return rt().exec.kernel_launches(); }
 const char* nb_build_id() { return build_id(); }
 int nb_nccl_version() {
