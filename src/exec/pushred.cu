@@ -4,9 +4,10 @@
 // Rank q owns segment q (AllReduce: slice q of the buffer; ReduceScatter:
 // slot q). Every rank runs one kernel (one block per SM, cooperative launch)
 // with two warp groups that progress independently:
-//   sender  : for each owner q != r, stores its own input's piece of segment q
-//             into q's scratch (P2P stores into q's memory), then publishes
-//             "filled" to q;
+//   sender  : stores its own input's piece of segment q into q's scratch for
+//             every owner q != r (P2P stores into q's memory), drains the
+//             store stream once per round (one system fence), then publishes
+//             "filled" to every owner;
 //   reducer : once every sender filled this piece of its own segment, folds
 //             the pieces in rank order (its own input in place r) with fp32
 //             accumulation, writes the result to its output (AllReduce: to
@@ -139,16 +140,20 @@ __global__ void __launch_bounds__(512, 1) pushred_kernel(const __grid_constant__
   if (sender) {
     for (unsigned j = 0; j < a.rounds; ++j) {
       const unsigned long long k = (unsigned long long)j * gridDim.x + blockIdx.x;
+      // Every owner consumed round j - kDepth (this round's scratch slots).
+      if (j >= kDepth) {
+        if (t == 0) {
+          const unsigned* w[kMaxRanks];
+          int c = 0;
+          for (int i = 1; i < N; ++i) w[c++] = a.consumed[r] + flag_idx((r + i) % N);
+          leader_wait(a, w, c, a.base + j - kDepth + 1, abort);
+        }
+        bar(gid, nt);
+        if (*abort) return;
+      }
+      // Push this round's piece to every owner, then drain the stores once.
       for (int i = 1; i < N; ++i) {
         const int q = (r + i) % N;
-        if (j >= kDepth) {
-          if (t == 0) {
-            const unsigned* w = a.consumed[r] + flag_idx(q);
-            leader_wait(a, &w, 1, a.base + j - kDepth + 1, abort);
-          }
-          bar(gid, nt);
-          if (*abort) return;
-        }
         const unsigned long long cs = k * kPiece;
         const unsigned long long len = cs < a.seg_len[q] ? min(kPiece, a.seg_len[q] - cs) : 0;
         // Whole 16-byte units; a trailing partial vector goes element-wise.
@@ -157,11 +162,11 @@ __global__ void __launch_bounds__(512, 1) pushred_kernel(const __grid_constant__
         const char* src = a.send + a.seg_off[q] + cs;
         push_copy(dst, src, body, t, nt);
         for (unsigned long long e = body + t; e < len; e += nt) dst[e] = src[e];
-        bar(gid, nt);
-        if (t == 0) {
-          asm volatile("fence.acq_rel.sys;" ::: "memory");
-          release(a.filled[q] + flag_idx(r), a.base + j + 1);
-        }
+      }
+      bar(gid, nt);
+      if (t == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int i = 1; i < N; ++i) release(a.filled[(r + i) % N] + flag_idx(r), a.base + j + 1);
       }
     }
     return;
