@@ -11,9 +11,9 @@
 // simulate_plan runs the data ops on host memory in a random topological
 // order, using the host fold for every reduction.
 //
-// Parity: the reference relies on TLA+ (tla/*.tla) plus GPU stress runs and
-// has no CPU test of its planner (SURVEY of shim.cu:15-16 "designed to be
-// CPU-testable, but no such test ships").
+// Parity: the reference relies on TLA+ (tla/*.tla) plus GPU stress runs; its
+// planner layers are written to be CPU-testable (shim.cu:15-16) but no CPU
+// test of them ships.
 #pragma once
 
 #include <cstdint>

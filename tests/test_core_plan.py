@@ -23,7 +23,7 @@ CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", 
 
 
 def test_baseline_cpu_plumbing_config():
-    """2 simulated ranks, fp32 AllReduce(sum) of 1,048,576
+    """The CPU plumbing configuration: 2 simulated ranks, fp32 AllReduce(sum) of 1,048,576
     uniform[-1,1] elements from seed 0, split into NVLink (SM), copy-engine
     and pinned-host shares; the host-lane fold is bit-exact against a serial
     host sum (the oracle folds rank 0 + rank 1 in fp32)."""

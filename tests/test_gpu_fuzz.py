@@ -1,4 +1,4 @@
-"""BASELINE config 5 (scaled): one ncclGroupStart/End batch of 64 seeded
+"""The mixed-group benchmark configuration (scaled): one ncclGroupStart/End batch of 64 seeded
 calls with log-uniform sizes and random collectives, dtypes and reduce ops,
 including operations the interposer does not handle. The mixed group must
 fall back to libnccl as a whole, in order, with correct results, and the
