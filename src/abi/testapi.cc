@@ -42,6 +42,7 @@ int nb_emu_reduce(const void* const* srcs, int nsrc, void* const* dsts, int ndst
 int nb_emu_copy(const void* const* srcs, void* const* dsts, const uint64_t* lens, int nseg, void* stream) {
   CopyLaunch c;
   c.nseg = nseg;
+  c.local = true;  // virtual ranks: every buffer is on the current GPU
   size_t total = 0;
   for (int i = 0; i < nseg && i < kMaxRanks; ++i) {
     c.src[i] = srcs[i];

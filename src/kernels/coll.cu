@@ -22,6 +22,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "kernels/fold.cuh"
 #include "kernels/kernels.h"
@@ -400,11 +401,12 @@ cudaError_t launch_copy(const CopyLaunch& c, LaunchShape shape, cudaStream_t str
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    static bool opted[64] = {};
-    if (e == cudaSuccess && dev < 64 && !opted[dev]) {
+    // The kernel's shared-memory opt-in, once per device (repeating it is harmless).
+    static std::atomic<bool> opted[64];
+    if (e == cudaSuccess && (dev >= 64 || !opted[dev].load(std::memory_order_acquire))) {
       e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tma_copy_kernel),
                                cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTmaCopySmem));
-      opted[dev] = e == cudaSuccess;
+      if (e == cudaSuccess && dev < 64) opted[dev].store(true, std::memory_order_release);
     }
     if (e != cudaSuccess) return e;
     const unsigned long long timeout_ns = 2000000000ull;

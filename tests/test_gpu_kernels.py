@@ -136,6 +136,27 @@ def test_copy_segments_alignment():
         assert torch.equal(out[d:d + n], base[s:s + n])
 
 
+@pytest.mark.parametrize("nbytes,src_off,dst_off", [
+    (4 << 20, 0, 0),                       # the smallest bulk copy
+    ((64 << 20) + 5, 0, 256),              # a byte tail after the last 16-byte unit
+    ((100 << 20) + 16, 16, 48),            # 16-byte aligned, not 32
+    ((8 << 20) + 3, 1, 7),                 # misaligned: the SM copy loop instead
+])
+def test_single_local_copy(nbytes, src_off, dst_off):
+    """One large copy within a GPU (the TMA bulk copy when both ends are
+    16-byte aligned) against torch's copy, with guard bytes around it."""
+    need_gpus(1)
+    from scc26_nccl_shim_b200.ops import emu
+    g = torch.Generator(device="cuda:0").manual_seed(nbytes % 1000)
+    base = torch.randint(0, 256, (nbytes + src_off + 64,), dtype=torch.uint8, device="cuda:0",
+                         generator=g)
+    out = torch.full((nbytes + dst_off + 64,), 0xA5, dtype=torch.uint8, device="cuda:0")
+    emu.copy([base[src_off:]], [out[dst_off:]], [nbytes])
+    torch.cuda.synchronize()
+    assert torch.equal(out[dst_off:dst_off + nbytes], base[src_off:src_off + nbytes])
+    assert bool((out[:dst_off] == 0xA5).all()) and bool((out[dst_off + nbytes:] == 0xA5).all())
+
+
 CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", "allgather"),
          ("bc_pull", "broadcast"), ("bc_scatter", "broadcast"), ("ar_staged", "allreduce"),
          ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ag_push", "allgather")]
