@@ -28,6 +28,7 @@
 #include "exec/calib.h"
 #include "exec/nvls.h"
 #include "exec/pushred.h"
+#include "kernels/kernels.h"
 #include "exec/ring.h"
 
 #ifndef NB_BUILD_ID
@@ -253,6 +254,13 @@ bool runtime_checks(Runtime& r, const std::vector<Call>& calls, const CliqueInfo
 Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
   Runtime& r = rt();
   std::lock_guard<std::mutex> lk(r.exec_mu);
+  if (!r.poisoned && tma_copy_status() != 0) {
+    // An earlier bulk copy gave up on a bounded wait: its output is not to be
+    // trusted, and neither are the custom routes from here on.
+    r.poisoned = true;
+    r.summary.count_timeout();
+    std::fprintf(stderr, "[nccl-b200] a bulk copy timed out; custom paths disabled for this process\n");
+  }
   CliqueState st;
   st.poisoned = r.poisoned;
   st.nccl_supported = r.nccl_supported;

@@ -23,6 +23,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 
 #include "kernels/fold.cuh"
 #include "kernels/kernels.h"
@@ -154,7 +155,9 @@ __global__ void __launch_bounds__(512, VB == 32 ? 1 : 2) reduce_kernel(const __g
 // (global -> shared completing on an mbarrier, shared -> global in bulk
 // groups), so 128 KiB per SM are in flight without occupying registers.
 // Both buffers are this GPU's own memory (no peer memory, no cluster
-// multicast). Every wait is bounded by %globaltimer.
+// multicast). Every wait is bounded by %globaltimer; a wait that expires
+// sets a status word in mapped host memory (tma_copy_status) and the block
+// stops after its copies in flight have landed.
 constexpr int kTmaStages = 4;
 constexpr unsigned kTmaChunk = 32768;
 constexpr size_t kTmaCopySmem = size_t(kTmaStages) * kTmaChunk;
@@ -176,7 +179,7 @@ __device__ __forceinline__ bool mbar_done(unsigned bar, unsigned parity) {
 }
 
 __global__ void __launch_bounds__(32, 1) tma_copy_kernel(const char* src, char* dst, unsigned long long len,
-                                                         unsigned long long timeout_ns) {
+                                                         unsigned long long timeout_ns, unsigned* status) {
   extern __shared__ __align__(128) unsigned char stage[];
   __shared__ __align__(8) unsigned long long bars[kTmaStages];
   const unsigned long long body = len & ~15ull;
@@ -238,6 +241,10 @@ __global__ void __launch_bounds__(32, 1) tma_copy_kernel(const char* src, char* 
         ok = retire();
     }
     while (ok && stored < issued) ok = retire();
+    if (!ok) {
+      *reinterpret_cast<volatile unsigned*>(status) = 1u;
+      __threadfence_system();
+    }
     // On a timeout, let loads still in flight land before the block exits.
     for (unsigned long long k = stored; !ok && k < issued; ++k)
       while (!mbar_done(bar0 + 8u * unsigned(k % kTmaStages), unsigned((k / kTmaStages) & 1)) &&
@@ -393,6 +400,38 @@ cudaError_t launch_reduce(const ReduceLaunch& r, LaunchShape shape, cudaStream_t
                           dim3(unsigned(shape.threads)), argv, 0, stream);
 }
 
+namespace {
+std::mutex g_tma_status_mu;
+unsigned* g_tma_status_host = nullptr;
+unsigned* g_tma_status_dev = nullptr;
+
+// The bulk copy's status word: pinned, mapped host memory (portable across
+// devices), allocated once.
+unsigned* tma_status_word() {
+  std::lock_guard<std::mutex> lk(g_tma_status_mu);
+  if (!g_tma_status_host) {
+    unsigned* h = nullptr;
+    unsigned* d = nullptr;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&h), sizeof(unsigned),
+                      cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess)
+      return nullptr;
+    if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), h, 0) != cudaSuccess) {
+      cudaFreeHost(h);
+      return nullptr;
+    }
+    *h = 0;
+    g_tma_status_host = h;
+    g_tma_status_dev = d;
+  }
+  return g_tma_status_dev;
+}
+}  // namespace
+
+unsigned tma_copy_status() {
+  std::lock_guard<std::mutex> lk(g_tma_status_mu);
+  return g_tma_status_host ? *static_cast<volatile unsigned*>(g_tma_status_host) : 0u;
+}
+
 cudaError_t launch_copy(const CopyLaunch& c, LaunchShape shape, cudaStream_t stream) {
   if (c.nseg < 1 || c.nseg > kMaxRanks) return cudaErrorInvalidValue;
   // One large copy within this GPU's memory: the TMA bulk copy.
@@ -409,11 +448,13 @@ cudaError_t launch_copy(const CopyLaunch& c, LaunchShape shape, cudaStream_t str
       if (e == cudaSuccess && dev < 64) opted[dev].store(true, std::memory_order_release);
     }
     if (e != cudaSuccess) return e;
+    unsigned* status = tma_status_word();
+    if (!status) return cudaErrorMemoryAllocation;
     const unsigned long long timeout_ns = 2000000000ull;
     const char* src = static_cast<const char*>(c.src[0]);
     char* dst = static_cast<char*>(c.dst[0]);
     unsigned long long len = c.len[0];
-    void* argv[] = {&src, &dst, &len, const_cast<unsigned long long*>(&timeout_ns)};
+    void* argv[] = {&src, &dst, &len, const_cast<unsigned long long*>(&timeout_ns), &status};
     return cudaLaunchKernel(reinterpret_cast<const void*>(tma_copy_kernel), dim3(unsigned(sms)), dim3(32),
                             argv, kTmaCopySmem, stream);
   }

@@ -49,6 +49,10 @@ struct LaunchShape {
 cudaError_t launch_reduce(const ReduceLaunch& a, LaunchShape shape, cudaStream_t stream);
 cudaError_t launch_copy(const CopyLaunch& a, LaunchShape shape, cudaStream_t stream);
 
+// Nonzero once a bounded wait of the TMA bulk copy expired (that copy is
+// incomplete); the runner then stops using its own routes.
+unsigned tma_copy_status();
+
 // Grid for `bytes` of work on a device with `sm_count` SMs.
 LaunchShape shape_for(size_t bytes, int sm_count, int blocks_per_sm, int threads);
 
