@@ -47,6 +47,13 @@ def test_mixed_64_call_group_falls_back_in_order():
             per.append((s, v))
         bufs.append(per)
     before = sum(nc.custom_calls(a) for a in ALGO.values() if a)
+    for d in devs:
+        torch.cuda.synchronize(d)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in devs]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in devs]
+    for i, d in enumerate(devs):
+        with torch.cuda.device(d):
+            starts[i].record(torch.cuda.current_stream(d))
     with nc.group():
         for (kind, dtype, op, count), per in zip(calls, bufs):
             for r, comm in enumerate(comms):
@@ -66,8 +73,14 @@ def test_mixed_64_call_group_falls_back_in_order():
                                        C.c_void_p(comm), C.c_void_p(streams[r]))
                     nc._fn("ncclRecv")(C.c_void_p(v.data_ptr()), C.c_size_t(count), dt, r,
                                        C.c_void_p(comm), C.c_void_p(streams[r]))
+    for i, d in enumerate(devs):
+        with torch.cuda.device(d):
+            stops[i].record(torch.cuda.current_stream(d))
     for d in devs:
         torch.cuda.synchronize(d)
+    # Aggregate device time of the whole group (max over GPUs), for the log.
+    print("mixed group of", len(calls), "calls per rank:",
+          round(max(a.elapsed_time(b) for a, b in zip(starts, stops)), 3), "ms")
     assert sum(nc.custom_calls(a) for a in ALGO.values() if a) == before
     for (kind, dtype, op, count), per in zip(calls, bufs):
         ins = [p[0].to("cuda:0") for p in per]
