@@ -26,6 +26,31 @@ Consume(k, r): destination r's H2D of piece k, after Fold(k), in order per
 (r, lane) stream. Invariants: CorrectOutputs (every consumed piece reads the
 value folded from piece k's own inputs) and ProducedBeforeConsumed. The
 broken variant skips the LaneFree wait.
+
+PushReduce (one block index of the push-reduce engine, exec/pushred.cu):
+N ranks, R rounds, D scratch rounds per (sender, owner). Sender s, round j:
+Write(s) stores its pieces into every owner's slot (s, j % D) once every
+owner consumed round j - D (unless SkipConsumedWait), then Publish(s) sets
+filled[q][s] = j + 1 for every owner. Owner q: Wait(q) until every sender's
+filled reached j + 1, Read(q) reads the N - 1 slots (non-atomically with
+respect to senders: a sender may write between Wait and Read), Consume(q)
+sets consumed[s][q] = j + 1. Invariants: NoStaleRead (every slot an owner
+reads holds the round it expects) and no deadlock (every reachable state
+without a successor has all ranks past round R). The broken variant skips
+the consumed wait and must read a slot that was already overwritten.
+
+NvlsAllReduce (one block index of the NVLS AllReduce, exec/nvls.cu): each
+rank has B round buffers of N slices. Copier of rank r, step s: if s >= 2,
+wait until every rank's mover published s - 1 (B(s-2) done everywhere),
+then C(s-2) reads its own buffer (s-2) % B, all slices; if s < R, A(s)
+writes its input round s into buffer s % B (all slices); publish s + 1.
+Mover of rank r, step s < R: wait until every rank's copier published s + 1
+(A(s) done everywhere), ReadB reads slice r of buffer s % B on every rank
+(the switch's ld_reduce), WriteB writes the reduced slice r into every
+rank's buffer s % B (the multicast store), publish s + 1. Invariants:
+every ld_reduce reads round s inputs, every copy-out reads round s results,
+no deadlock. Broken variants: two buffers instead of three, or a mover that
+waits only for its own copier.
 """
 from __future__ import annotations
 
@@ -41,25 +66,35 @@ class Result:
     trace: list | None = None
 
 
-def _bfs(init, actions, invariants, max_states=2_000_000):
+def _bfs(init, actions, invariants, max_states=2_000_000, done=None):
+    """Breadth-first over every reachable state. With `done`, a state with no
+    successor that is not done is reported as the violation "Deadlock"."""
     seen = {init: None}
     q = deque([init])
+
+    def trace_to(s):
+        trace = []
+        cur = s
+        while cur is not None:
+            trace.append(cur)
+            cur = seen[cur]
+        return list(reversed(trace))
+
     while q:
         s = q.popleft()
         for name, inv in invariants:
             if not inv(s):
-                trace = []
-                cur = s
-                while cur is not None:
-                    trace.append(cur)
-                    cur = seen[cur]
-                return Result(False, len(seen), name, list(reversed(trace)))
+                return Result(False, len(seen), name, trace_to(s))
+        succ = 0
         for t in actions(s):
+            succ += 1
             if t not in seen:
                 seen[t] = s
                 if len(seen) > max_states:
                     raise RuntimeError("state space too large")
                 q.append(t)
+        if done is not None and succ == 0 and not done(s):
+            return Result(False, len(seen), "Deadlock", trace_to(s))
     return Result(True, len(seen))
 
 
@@ -198,3 +233,118 @@ def check_host_lane_reuse(pieces=5, lanes=4, sources=1, dests=1, skip_reuse_wait
 
     return _bfs(init, actions, [("CorrectOutputs", correct_outputs),
                                 ("ProducedBeforeConsumed", produced_before_consumed)])
+
+
+# --------------------------------------------------------------------------
+# PushReduce (progress words of the push-reduce engine)
+# --------------------------------------------------------------------------
+
+def check_push_reduce(nranks=3, rounds=4, depth=2, skip_consumed_wait=False) -> Result:
+    """State: sj[s] (sender round), sphase[s] (0 write, 1 publish), rj[q]
+    (owner round), rphase[q] (0 wait, 1 read, 2 consume), filled[q][s],
+    consumed[s][q], slot[q][s][d] (round number held, -1 empty), stale
+    (an owner read a wrong round)."""
+    N, R, D = nranks, rounds, depth
+    init = (tuple([0] * N), tuple([0] * N), tuple([0] * N), tuple([0] * N),
+            tuple(tuple([0] * N) for _ in range(N)), tuple(tuple([0] * N) for _ in range(N)),
+            tuple(tuple(tuple([-1] * D) for _ in range(N)) for _ in range(N)), False)
+
+    def setv(t, i, v):
+        return t[:i] + (v,) + t[i + 1:]
+
+    def actions(st):
+        sj, sph, rj, rph, filled, consumed, slot, stale = st
+        for s in range(N):
+            j = sj[s]
+            if j >= R:
+                continue
+            if sph[s] == 0:
+                if not skip_consumed_wait and j >= D and \
+                        not all(consumed[s][q] >= j - D + 1 for q in range(N) if q != s):
+                    continue
+                ns = tuple(tuple(tuple(j if (qq != s and ss == s and d == j % D) else slot[qq][ss][d]
+                                       for d in range(D)) for ss in range(N)) for qq in range(N))
+                yield (sj, setv(sph, s, 1), rj, rph, filled, consumed, ns, stale)
+            else:
+                nf = tuple(tuple(j + 1 if (qq != s and ss == s) else filled[qq][ss] for ss in range(N))
+                           for qq in range(N))
+                yield (setv(sj, s, j + 1), setv(sph, s, 0), rj, rph, nf, consumed, slot, stale)
+        for q in range(N):
+            j = rj[q]
+            if j >= R:
+                continue
+            if rph[q] == 0:
+                if all(filled[q][s] >= j + 1 for s in range(N) if s != q):
+                    yield (sj, sph, rj, setv(rph, q, 1), filled, consumed, slot, stale)
+            elif rph[q] == 1:
+                bad = any(slot[q][s][j % D] != j for s in range(N) if s != q)
+                yield (sj, sph, rj, setv(rph, q, 2), filled, consumed, slot, stale or bad)
+            else:
+                nc = tuple(tuple(j + 1 if (ss != q and qq == q) else consumed[ss][qq] for qq in range(N))
+                           for ss in range(N))
+                yield (sj, sph, setv(rj, q, j + 1), setv(rph, q, 0), filled, nc, slot, stale)
+
+    def done(st):
+        return all(x >= R for x in st[0]) and all(x >= R for x in st[2])
+
+    return _bfs(init, actions, [("NoStaleRead", lambda st: not st[7])], done=done)
+
+
+# --------------------------------------------------------------------------
+# NvlsAllReduce (progress words of the NVLS AllReduce kernel)
+# --------------------------------------------------------------------------
+
+def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True) -> Result:
+    """State: cs[r], cph[r] (copier step, 0 wait/copy-out, 1 copy-in+publish),
+    ms[r], mph[r] (mover step, 0 wait, 1 read, 2 write+publish), cflag[r],
+    mflag[r], buf[r][b][q] = (round, 0 input | 1 reduced) or None, bad."""
+    N, R, B = nranks, rounds, bufs
+    empty = tuple(tuple(tuple(None for _ in range(N)) for _ in range(B)) for _ in range(N))
+    init = (tuple([0] * N), tuple([0] * N), tuple([0] * N), tuple([0] * N),
+            tuple([0] * N), tuple([0] * N), empty, False)
+
+    def setv(t, i, v):
+        return t[:i] + (v,) + t[i + 1:]
+
+    def setbuf(buf, ranks, b, slices, val):
+        return tuple(tuple(tuple(val if (r in ranks and bb == b and q in slices) else buf[r][bb][q]
+                                 for q in range(N)) for bb in range(B)) for r in range(N))
+
+    def actions(st):
+        cs, cph, ms, mph, cflag, mflag, buf, bad = st
+        for r in range(N):
+            s_ = cs[r]
+            if s_ < R + 2:
+                if cph[r] == 0:
+                    if s_ >= 2:
+                        if not all(mflag[q] >= s_ - 1 for q in range(N)):
+                            pass
+                        else:
+                            i = s_ - 2
+                            wrong = any(buf[r][i % B][q] != (i, 1) for q in range(N))
+                            yield (cs, setv(cph, r, 1), ms, mph, cflag, mflag, buf, bad or wrong)
+                    else:
+                        yield (cs, setv(cph, r, 1), ms, mph, cflag, mflag, buf, bad)
+                else:
+                    nb = setbuf(buf, {r}, s_ % B, set(range(N)), (s_, 0)) if s_ < R else buf
+                    yield (setv(cs, r, s_ + 1), setv(cph, r, 0), ms, mph, setv(cflag, r, s_ + 1), mflag,
+                           nb, bad)
+            s_ = ms[r]
+            if s_ < R:
+                if mph[r] == 0:
+                    ready = all(cflag[q] >= s_ + 1 for q in range(N)) if mover_waits_all else \
+                        cflag[r] >= s_ + 1
+                    if ready:
+                        yield (cs, cph, ms, setv(mph, r, 1), cflag, mflag, buf, bad)
+                elif mph[r] == 1:
+                    wrong = any(buf[q][s_ % B][r] != (s_, 0) for q in range(N))
+                    yield (cs, cph, ms, setv(mph, r, 2), cflag, mflag, buf, bad or wrong)
+                else:
+                    nb = setbuf(buf, set(range(N)), s_ % B, {r}, (s_, 1))
+                    yield (cs, cph, setv(ms, r, s_ + 1), setv(mph, r, 0), cflag, setv(mflag, r, s_ + 1),
+                           nb, bad)
+
+    def done(st):
+        return all(x >= R + 2 for x in st[0]) and all(x >= R for x in st[2])
+
+    return _bfs(init, actions, [("RoundsInOrder", lambda st: not st[7])], done=done)

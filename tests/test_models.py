@@ -45,7 +45,38 @@ def test_host_lane_reuse_fold_broken(sources, dests):
     assert not r.ok
 
 
+@pytest.mark.parametrize("n,rounds,depth", [(2, 4, 2), (3, 4, 2), (3, 5, 1), (4, 3, 2)])
+def test_push_reduce_holds(n, rounds, depth):
+    """The push-reduce engine's progress words: no owner reads a scratch slot
+    that a sender already refilled, and no reachable deadlock."""
+    r = m.check_push_reduce(nranks=n, rounds=rounds, depth=depth)
+    assert r.ok, (r.violation, r.trace)
+
+
+@pytest.mark.parametrize("n", [2, 3])
+def test_push_reduce_broken_reads_stale(n):
+    r = m.check_push_reduce(nranks=n, rounds=4, depth=2, skip_consumed_wait=True)
+    assert not r.ok and r.violation == "NoStaleRead"
+
+
+@pytest.mark.parametrize("n,rounds,bufs", [(2, 4, 3), (2, 6, 3), (3, 4, 3), (3, 4, 2)])
+def test_nvls_allreduce_holds(n, rounds, bufs):
+    """The NVLS AllReduce's copier/mover progress words, with three round
+    buffers (the kernel's) and with two (also safe: A(s) reuses a buffer only
+    after every rank's B(s-2), which the wait before C(s-2) already needs)."""
+    r = m.check_nvls_allreduce(nranks=n, rounds=rounds, bufs=bufs)
+    assert r.ok, (r.violation, r.trace)
+
+
+@pytest.mark.parametrize("n", [2, 3])
+def test_nvls_allreduce_broken_mover_waits_own_copier_only(n):
+    r = m.check_nvls_allreduce(nranks=n, rounds=4, mover_waits_all=False)
+    assert not r.ok and r.violation == "RoundsInOrder"
+
+
 def test_tla_sources_present():
     for f in ["GroupFallbackN.tla", "HostLaneReuseN.tla", "GroupFallbackN.cfg",
-              "GroupFallbackN-broken.cfg", "HostLaneReuseN.cfg", "HostLaneReuseN-broken.cfg"]:
+              "GroupFallbackN-broken.cfg", "HostLaneReuseN.cfg", "HostLaneReuseN-broken.cfg",
+              "PushReduceN.tla", "PushReduceN.cfg", "PushReduceN-broken.cfg",
+              "NvlsAllReduceN.tla", "NvlsAllReduceN.cfg", "NvlsAllReduceN-broken.cfg"]:
         assert os.path.exists(os.path.join(REPO, "tla", f)), f
