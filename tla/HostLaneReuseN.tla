@@ -8,7 +8,7 @@
 (* ranks then copies the output (or, for S = 1, the source's bounce) into   *)
 (* its buffer (H2D, in order per destination and lane). A fold reads piece  *)
 (* k only if every bounce still holds piece k; otherwise it yields -1.      *)
-EXTENDS Naturals, FiniteSets
+EXTENDS Integers, FiniteSets
 
 CONSTANTS Pieces, Lanes, S, D, SkipReuseWait
 VARIABLES produced, folded, consumed, bounce, out, output
