@@ -126,7 +126,9 @@ void resolve_all() {
 
 Shares shares_for(Algo a, int n, const CallDesc& c) {
   Runtime& r = rt();
-  Shares s = n >= 1 && n <= kMaxRanks && r.calib[n].valid ? shares_from(r.calib[n], a, n) : Shares{};
+  Shares s = n >= 1 && n <= kMaxRanks && r.calib[n].valid
+                 ? shares_from(r.calib[n], a, n, small_message(r.calib[n], logical_bytes(c)))
+                 : Shares{};
   if (r.policy.host_share_ppm >= 0) s.host_ppm = r.policy.host_share_ppm;
   if (r.policy.ce_share_ppm >= 0) s.ce_ppm = r.policy.ce_share_ppm;
   if (n <= 1 || a == Algo::ArNvls) s.host_ppm = s.ce_ppm = 0;
@@ -158,12 +160,19 @@ void prewarm(const int* devices, int n) {
     }
     r.calib[n] = c;
     if (c.valid) {
-      char line[200];
+      char line[320];
       std::snprintf(line, sizeof line, "routes n=%d allreduce=%s allgather=%s(ce=%d) reducescatter=%s "
                     "broadcast=%s(ce=%d)", n, algo_name(Algo(c.preferred[0])),
                     algo_name(Algo(c.preferred[1])), c.ce_ppm[1], algo_name(Algo(c.preferred[2])),
                     algo_name(Algo(c.preferred[3])), c.ce_ppm[3]);
       r.summary.note(line);
+      if (c.small_below_mib > 0) {
+        std::snprintf(line, sizeof line, "routes n=%d below %d MiB: allreduce=%s allgather=%s "
+                      "reducescatter=%s broadcast=%s", n, c.small_below_mib,
+                      algo_name(Algo(c.small_pref[0])), algo_name(Algo(c.small_pref[1])),
+                      algo_name(Algo(c.small_pref[2])), algo_name(Algo(c.small_pref[3])));
+        r.summary.note(line);
+      }
     }
   }
   Shares s = shares_for(Algo::ArTwoShot, n, CallDesc{});
@@ -285,7 +294,8 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
       if (stream_capturing(static_cast<cudaStream_t>(c.stream), c.desc.device)) st.capturing = true;
     st.nvls_available = r.policy.nvls != NvlsMode::Off && nvls_supported(info.devices, info.nranks);
     if (r.calib[info.nranks].valid)
-      for (int k = 0; k < int(Kind::Count); ++k) st.preferred[k] = Algo(r.calib[info.nranks].preferred[k]);
+      for (int k = 0; k < int(Kind::Count); ++k)
+        st.preferred[k] = tuned_route(r.calib[info.nranks], k, logical_bytes(descs[0]));
   }
   const CliqueDecision d = gate_clique(descs, st, r.policy);
   reason = d.reason;

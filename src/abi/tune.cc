@@ -6,6 +6,8 @@
 // copy-engine data movement.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <string>
 #include <vector>
@@ -111,100 +113,118 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
          cudaEventCreate(&e0[size_t(i)]) == cudaSuccess && cudaEventCreate(&e1[size_t(i)]) == cudaSuccess;
   }
   const bool nvls = r.policy.nvls != NvlsMode::Off && nvls_supported(devices, n);
-  for (int kk = 0; ok && kk < int(Kind::Count); ++kk) {
-    const Kind kind = Kind(kk);
-    CliqueDesc d;
-    d.kind = kind;
-    d.dtype = DType::F32;
-    d.op = RedOp::Sum;
-    d.nranks = n;
-    d.bytes = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? bytes / size_t(n) : bytes;
-    d.count = d.bytes / 4;
-    d.root = 0;
-    Binding b;
-    b.nranks = n;
-    b.fold.dtype = DType::F32;
-    b.fold.op = RedOp::Sum;
-    b.fold.nranks = n;
-    for (int i = 0; i < n; ++i) {
-      b.device[i] = devices[i];
-      b.stream[i] = streams[size_t(i)];
-      b.send[i] = send[size_t(i)];
-      b.recv[i] = recv[size_t(i)];
+  // Two tuning sizes: the large one (the policy's) and a small one; the
+  // small choice serves messages below their geometric mean.
+  const size_t unit = size_t(n) * 256;
+  const size_t small_bytes = std::max(unit, (size_t(64) << 20) / unit * unit);
+  const bool two_sizes = bytes >= 4 * small_bytes;
+  for (int pass = 0; pass < (two_sizes ? 2 : 1); ++pass) {
+    const size_t size = pass == 0 ? bytes : small_bytes;
+    for (int kk = 0; ok && kk < int(Kind::Count); ++kk) {
+      const Kind kind = Kind(kk);
+      CliqueDesc d;
+      d.kind = kind;
+      d.dtype = DType::F32;
+      d.op = RedOp::Sum;
+      d.nranks = n;
+      d.bytes = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? size / size_t(n) : size;
+      d.count = d.bytes / 4;
+      d.root = 0;
+      Binding b;
+      b.nranks = n;
+      b.fold.dtype = DType::F32;
+      b.fold.op = RedOp::Sum;
+      b.fold.nranks = n;
+      for (int i = 0; i < n; ++i) {
+        b.device[i] = devices[i];
+        b.stream[i] = streams[size_t(i)];
+        b.send[i] = send[size_t(i)];
+        b.recv[i] = recv[size_t(i)];
+      }
+      double best_ms = 1e30, best_real_ms = 1e30;
+      Candidate best{Algo::Fallback, -1, -1, 0, 0};
+      for (const Candidate& c : candidates(kind, n, nvls, *out)) {
+        Shares s;
+        s.ce_ppm = c.ce_ppm;
+        s.host_ppm = c.host_ppm;
+        s.stage_piece = size_t(c.piece_mib) << 20;
+        s.stage_depth = c.depth;
+        Plan plan;
+        build_plan(c.algo, d, r.policy, s, plan);
+        std::string why;
+        if (!r.exec.ensure(plan.needs, devices, n, &why)) {
+          cudaGetLastError();
+          continue;
+        }
+        bool good = true;
+        float ms = 0;
+        for (int rep = 0; rep < 2 && good; ++rep) {  // rep 0 warms up
+          for (int i = 0; i < n; ++i) {
+            cudaSetDevice(devices[i]);
+            cudaEventRecord(e0[size_t(i)], streams[size_t(i)]);
+          }
+          const int runs = rep ? 3 : 1;
+          for (int k = 0; k < runs && good; ++k) {
+            cudaError_t err = cudaSuccess;
+            good = r.exec.execute(plan, b, &err, nullptr) == ExecStatus::Ok;
+          }
+          float worst = 0;
+          for (int i = 0; i < n && good; ++i) {
+            cudaSetDevice(devices[i]);
+            cudaEventRecord(e1[size_t(i)], streams[size_t(i)]);
+          }
+          for (int i = 0; i < n && good; ++i) {
+            cudaSetDevice(devices[i]);
+            float t = 0;
+            good = cudaEventSynchronize(e1[size_t(i)]) == cudaSuccess &&
+                   cudaEventElapsedTime(&t, e0[size_t(i)], e1[size_t(i)]) == cudaSuccess;
+            worst = t > worst ? t : worst;
+          }
+          ms = worst / float(runs);
+        }
+        if (!good) {
+          cudaGetLastError();
+          r.exec.drain(devices, n);
+          continue;
+        }
+        char line[160];
+        const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? size : d.bytes;
+        std::snprintf(line, sizeof line,
+                      "tune %s n=%d bytes=%zu %s ce_ppm=%d host_ppm=%d piece_mib=%d depth=%d busbw_gbs=%.1f",
+                      kind_name(kind), n, logical, algo_name(c.algo), c.ce_ppm, c.host_ppm, c.piece_mib,
+                      c.depth, logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
+        r.summary.note(line);
+        // An event-ordered chain pays a cross-GPU event wait per piece and hop,
+        // so its rate drops as messages outgrow the tuning size (measured at 4
+        // ranks: equal to the in-kernel push chain at 4 GiB, 10 % behind at
+        // 8 GiB); it must win by 3 % to be chosen.
+        const float score = c.algo == Algo::BcChain ? ms * 1.03f : ms;
+        if (score < best_ms) {
+          best_ms = score;
+          best_real_ms = ms;
+          best = c;
+        }
+      }
+      if (best.algo != Algo::Fallback && pass == 1) {
+        out->small_pref[kk] = int(best.algo);
+        out->small_ce_ppm[kk] = best.ce_ppm;
+        out->small_host_ppm[kk] = best.host_ppm;
+        out->small_piece_mib[kk] = best.piece_mib;
+        out->small_depth[kk] = best.depth;
+      } else if (best.algo != Algo::Fallback) {
+        out->preferred[kk] = int(best.algo);
+        out->ce_ppm[kk] = best.ce_ppm;
+        out->host_ppm[kk] = best.host_ppm;
+        out->stage_piece_mib[kk] = best.piece_mib;
+        out->stage_depth[kk] = best.depth;
+        const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? size : d.bytes;
+        out->route_gbs[kk] = logical / (best_real_ms * 1e-3) / 1e9 * busbw_factor(kind, n);
+      }
     }
-    double best_ms = 1e30, best_real_ms = 1e30;
-    Candidate best{Algo::Fallback, -1, -1, 0, 0};
-    for (const Candidate& c : candidates(kind, n, nvls, *out)) {
-      Shares s;
-      s.ce_ppm = c.ce_ppm;
-      s.host_ppm = c.host_ppm;
-      s.stage_piece = size_t(c.piece_mib) << 20;
-      s.stage_depth = c.depth;
-      Plan plan;
-      build_plan(c.algo, d, r.policy, s, plan);
-      std::string why;
-      if (!r.exec.ensure(plan.needs, devices, n, &why)) {
-        cudaGetLastError();
-        continue;
-      }
-      bool good = true;
-      float ms = 0;
-      for (int rep = 0; rep < 2 && good; ++rep) {  // rep 0 warms up
-        for (int i = 0; i < n; ++i) {
-          cudaSetDevice(devices[i]);
-          cudaEventRecord(e0[size_t(i)], streams[size_t(i)]);
-        }
-        const int runs = rep ? 3 : 1;
-        for (int k = 0; k < runs && good; ++k) {
-          cudaError_t err = cudaSuccess;
-          good = r.exec.execute(plan, b, &err, nullptr) == ExecStatus::Ok;
-        }
-        float worst = 0;
-        for (int i = 0; i < n && good; ++i) {
-          cudaSetDevice(devices[i]);
-          cudaEventRecord(e1[size_t(i)], streams[size_t(i)]);
-        }
-        for (int i = 0; i < n && good; ++i) {
-          cudaSetDevice(devices[i]);
-          float t = 0;
-          good = cudaEventSynchronize(e1[size_t(i)]) == cudaSuccess &&
-                 cudaEventElapsedTime(&t, e0[size_t(i)], e1[size_t(i)]) == cudaSuccess;
-          worst = t > worst ? t : worst;
-        }
-        ms = worst / float(runs);
-      }
-      if (!good) {
-        cudaGetLastError();
-        r.exec.drain(devices, n);
-        continue;
-      }
-      char line[160];
-      const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? bytes : d.bytes;
-      std::snprintf(line, sizeof line,
-                    "tune %s n=%d %s ce_ppm=%d host_ppm=%d piece_mib=%d depth=%d busbw_gbs=%.1f",
-                    kind_name(kind), n, algo_name(c.algo), c.ce_ppm, c.host_ppm, c.piece_mib,
-                    c.depth, logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
-      r.summary.note(line);
-      // An event-ordered chain pays a cross-GPU event wait per piece and hop,
-      // so its rate drops as messages outgrow the tuning size (measured at 4
-      // ranks: equal to the in-kernel push chain at 4 GiB, 10 % behind at
-      // 8 GiB); it must win by 3 % to be chosen.
-      const float score = c.algo == Algo::BcChain ? ms * 1.03f : ms;
-      if (score < best_ms) {
-        best_ms = score;
-        best_real_ms = ms;
-        best = c;
-      }
-    }
-    if (best.algo != Algo::Fallback) {
-      out->preferred[kk] = int(best.algo);
-      out->ce_ppm[kk] = best.ce_ppm;
-      out->host_ppm[kk] = best.host_ppm;
-      out->stage_piece_mib[kk] = best.piece_mib;
-      out->stage_depth[kk] = best.depth;
-      const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? bytes : d.bytes;
-      out->route_gbs[kk] = logical / (best_real_ms * 1e-3) / 1e9 * busbw_factor(kind, n);
-    }
+  }
+  if (two_sizes) {
+    const double mean = std::sqrt(double(small_bytes) * double(bytes));
+    out->small_below_mib = int(mean / double(1 << 20));
   }
   for (int i = 0; i < n; ++i) {
     cudaSetDevice(devices[i]);

@@ -7,7 +7,17 @@
 
 namespace nb {
 
-Shares shares_from(const CalibResult& c, Algo a, int n) {
+bool small_message(const CalibResult& c, size_t logical) {
+  return c.small_below_mib > 0 && logical < (size_t(c.small_below_mib) << 20);
+}
+
+Algo tuned_route(const CalibResult& c, int kind, size_t logical) {
+  if (kind < 0 || kind >= 4) return Algo::Fallback;
+  if (small_message(c, logical) && c.small_pref[kind] != 0) return Algo(c.small_pref[kind]);
+  return Algo(c.preferred[kind]);
+}
+
+Shares shares_from(const CalibResult& c, Algo a, int n, bool small) {
   Shares s;
   if (!c.valid || n < 2 || c.nvlink_sm_gbs <= 0) return s;
   const double N = double(n);
@@ -44,8 +54,16 @@ Shares shares_from(const CalibResult& c, Algo a, int n) {
                        a == Algo::BcScatter;
   if (ce_algo && c.nvlink_mix_gbs > 1.03 * bnv && c.mix_ce_fraction > 0)
     s.ce_ppm = int(std::min(0.5, c.mix_ce_fraction) * 10000.0);
-  // A measured route choice overrides the model for that route.
+  // A measured route choice overrides the model for that route (the
+  // small-size choice for a small message, when it is this route).
   for (int k = 0; k < 4; ++k) {
+    if (small && c.small_pref[k] == int(a)) {
+      if (c.small_ce_ppm[k] >= 0) s.ce_ppm = c.small_ce_ppm[k];
+      if (c.small_host_ppm[k] >= 0) s.host_ppm = c.small_host_ppm[k];
+      if (c.small_piece_mib[k] > 0) s.stage_piece = size_t(c.small_piece_mib[k]) << 20;
+      if (c.small_depth[k] > 0) s.stage_depth = c.small_depth[k];
+      continue;
+    }
     if (c.preferred[k] != int(a)) continue;
     if (c.ce_ppm[k] >= 0) s.ce_ppm = c.ce_ppm[k];
     if (c.host_ppm[k] >= 0) s.host_ppm = c.host_ppm[k];
@@ -70,7 +88,14 @@ std::string calib_to_json(const CalibResult& c, const std::string& key) {
                   k, c.preferred[k], k, c.ce_ppm[k], k, c.host_ppm[k], k, c.stage_piece_mib[k], k,
                   c.stage_depth[k]);
     s += buf;
+    std::snprintf(buf, sizeof buf,
+                  ", \"spref%d\": %d, \"sce%d\": %d, \"shost%d\": %d, \"spiece%d\": %d, \"sdepth%d\": %d",
+                  k, c.small_pref[k], k, c.small_ce_ppm[k], k, c.small_host_ppm[k], k,
+                  c.small_piece_mib[k], k, c.small_depth[k]);
+    s += buf;
   }
+  std::snprintf(buf, sizeof buf, ", \"small_below_mib\": %d", c.small_below_mib);
+  s += buf;
   return s + "}\n";
 }
 
@@ -106,6 +131,15 @@ bool calib_from_json(const std::string& text, const std::string& key, CalibResul
     if (json_number(text, ("host" + K).c_str(), &v)) c.host_ppm[k] = int(v);
     if (json_number(text, ("piece" + K).c_str(), &v)) c.stage_piece_mib[k] = int(v);
     if (json_number(text, ("depth" + K).c_str(), &v)) c.stage_depth[k] = int(v);
+    if (json_number(text, ("spref" + K).c_str(), &v)) c.small_pref[k] = int(v);
+    if (json_number(text, ("sce" + K).c_str(), &v)) c.small_ce_ppm[k] = int(v);
+    if (json_number(text, ("shost" + K).c_str(), &v)) c.small_host_ppm[k] = int(v);
+    if (json_number(text, ("spiece" + K).c_str(), &v)) c.small_piece_mib[k] = int(v);
+    if (json_number(text, ("sdepth" + K).c_str(), &v)) c.small_depth[k] = int(v);
+  }
+  {
+    double v = 0;
+    if (json_number(text, "small_below_mib", &v)) c.small_below_mib = int(v);
   }
   c.valid = true;
   *out = c;

@@ -36,9 +36,24 @@ struct CalibResult {
   int stage_piece_mib[4] = {0, 0, 0, 0};
   int stage_depth[4] = {0, 0, 0, 0};
   double route_gbs[4] = {0, 0, 0, 0};  // busbw of the chosen route at the tuning size
+  // The same, tuned at a small size: used for messages below small_below_mib
+  // (0 = no small-size choice). Pipelined routes pay a start-up that only
+  // large messages amortize, so the best route differs with size.
+  int small_pref[4] = {0, 0, 0, 0};
+  int small_ce_ppm[4] = {-1, -1, -1, -1};
+  int small_host_ppm[4] = {-1, -1, -1, -1};
+  int small_piece_mib[4] = {0, 0, 0, 0};
+  int small_depth[4] = {0, 0, 0, 0};
+  int small_below_mib = 0;
 };
 
-Shares shares_from(const CalibResult& c, Algo a, int n);
+// Whether a message of `logical` bytes takes the small-size choice.
+bool small_message(const CalibResult& c, size_t logical);
+// The tuned route of `kind` for a message of `logical` bytes (Fallback when
+// untuned).
+Algo tuned_route(const CalibResult& c, int kind, size_t logical);
+// Byte shares of route `a`; `small` selects the small-size tuning's shares.
+Shares shares_from(const CalibResult& c, Algo a, int n, bool small = false);
 std::string calib_to_json(const CalibResult& c, const std::string& key);
 bool calib_from_json(const std::string& text, const std::string& key, CalibResult* out);
 

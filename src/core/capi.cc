@@ -371,6 +371,24 @@ void nb_shares_from(double sm, double ce, double mix, double ce_frac, double d2h
   *ce_ppm = s.ce_ppm;
 }
 
+// The size-aware route choice after a JSON round trip: AllReduce tuned to
+// `pref` at the large size and `small_pref` below `below_mib`; returns the
+// route for a message of `logical` bytes and the small choice's CE share.
+int nb_calib_small(int pref, int small_pref, int below_mib, uint64_t logical, int* small_ce) {
+  CalibResult c;
+  c.valid = true;
+  c.nvlink_sm_gbs = 700;
+  c.preferred[0] = pref;
+  c.ce_ppm[0] = 1111;
+  c.small_pref[0] = small_pref;
+  c.small_ce_ppm[0] = 2222;
+  c.small_below_mib = below_mib;
+  CalibResult d;
+  if (!calib_from_json(calib_to_json(c, "k"), "k", &d)) return -1;
+  *small_ce = shares_from(d, Algo(small_pref), 2, small_message(d, size_t(logical))).ce_ppm;
+  return int(tuned_route(d, 0, size_t(logical)));
+}
+
 int nb_calib_roundtrip(double sm, const char* key, double* back) {
   CalibResult c;
   c.valid = true;

@@ -160,6 +160,21 @@ def test_calibration_cache_roundtrip_and_key():
     assert abs(back.value - 712.125) < 1e-3
 
 
+def test_size_aware_route_choice():
+    L = c.lib()
+    L.nb_calib_small.argtypes = [C.c_int, C.c_int, C.c_int, C.c_uint64, C.POINTER(C.c_int)]
+    ce = C.c_int(-5)
+    staged, twoshot = c.ALGO["ar_staged"], c.ALGO["ar_twoshot"]
+    # Below the crossover the small-size winner, with its own shares...
+    assert L.nb_calib_small(staged, twoshot, 512, 32 << 20, C.byref(ce)) == twoshot
+    assert ce.value == 2222
+    # ...at and above it the large-size winner.
+    assert L.nb_calib_small(staged, twoshot, 512, 512 << 20, C.byref(ce)) == staged
+    assert L.nb_calib_small(staged, twoshot, 512, 8 << 30, C.byref(ce)) == staged
+    # No small-size tuning: always the large-size winner.
+    assert L.nb_calib_small(staged, 0, 0, 32 << 20, C.byref(ce)) == staged
+
+
 def u64s(*v):
     return (C.c_uint64 * len(v))(*v)
 
