@@ -97,6 +97,12 @@ bool Executor::ensure_device(int dev, std::string* why) {
 bool Executor::setup(const int* devices, int n, std::string* why) {
   for (int i = 0; i < n; ++i)
     if (!ensure_device(devices[i], why)) return false;
+  // The bulk copy's status word is pinned host memory: allocate it here, at
+  // init, rather than at a first copy that may run beside a stream capture.
+  if (!tma_copy_prepare()) {
+    if (why) *why = "bulk copy status word";
+    return false;
+  }
   for (int i = 0; i < n; ++i)
     for (int j = 0; j < n; ++j) {
       if (i == j) continue;

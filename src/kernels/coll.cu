@@ -427,6 +427,8 @@ unsigned* tma_status_word() {
 }
 }  // namespace
 
+bool tma_copy_prepare() { return tma_status_word() != nullptr; }
+
 unsigned tma_copy_status() {
   std::lock_guard<std::mutex> lk(g_tma_status_mu);
   return g_tma_status_host ? *static_cast<volatile unsigned*>(g_tma_status_host) : 0u;

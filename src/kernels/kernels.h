@@ -52,6 +52,8 @@ cudaError_t launch_copy(const CopyLaunch& a, LaunchShape shape, cudaStream_t str
 // Nonzero once a bounded wait of the TMA bulk copy expired (that copy is
 // incomplete); the runner then stops using its own routes.
 unsigned tma_copy_status();
+// Allocates the status word (once); false when pinned host memory is unavailable.
+bool tma_copy_prepare();
 
 // Grid for `bytes` of work on a device with `sm_count` SMs.
 LaunchShape shape_for(size_t bytes, int sm_count, int blocks_per_sm, int threads);
