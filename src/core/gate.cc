@@ -58,6 +58,7 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
   switch (a) {
     case Algo::ArTwoShot: return k == Kind::AllReduce;
     case Algo::ArNvls:
+    case Algo::ArHybrid:
       // A multicast object needs at least two devices.
       return k == Kind::AllReduce && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
@@ -143,7 +144,7 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
   // every slot must be 16-byte aligned. They scale the switch's sum once, so
   // a PreMulSum takes them only when every rank passed the same host scalar.
   const bool nvls = algo == Algo::ArNvls || algo == Algo::BcNvls || algo == Algo::AgNvls ||
-                    algo == Algo::RsNvls;
+                    algo == Algo::RsNvls || algo == Algo::ArHybrid;
   bool aligned = call_bytes(a) % 16 == 0;
   for (const CallDesc& c : calls)
     aligned = aligned && c.recv % 16 == 0 && (c.send % 16 == 0 || (c.kind == Kind::Broadcast && c.rank != c.root));

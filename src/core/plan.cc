@@ -151,14 +151,15 @@ class Builder {
     op.len[0] = op.bytes = bytes;
     p_.ops.push_back(op);
   }
-  void nvls(StreamId s, int r, size_t bytes) {
+  void nvls(StreamId s, int r, size_t bytes, size_t off = 0, uint16_t grid = 0) {
     PlanOp op;
     op.kind = OpKind::NvlsReduce;
     op.stream = s;
     op.nsrc = op.ndst = 1;
-    op.src[0] = send_at(r, 0);
-    op.dst[0] = recv_at(r, 0);
+    op.src[0] = send_at(r, off);
+    op.dst[0] = recv_at(r, off);
     op.len[0] = op.bytes = bytes;
+    op.grid = grid;
     p_.ops.push_back(op);
     use(s);
   }
@@ -253,14 +254,20 @@ void all_ranks(int n, int* ranks) {
 // Optional copy-engine share: a middle part of each slice is reduced into the
 // owner's output only, then pushed to the peers by the owner's copy engine.
 // Optional host share: the slice's suffix goes through the host lanes.
-void plan_ar_twoshot(Builder& b, const CliqueDesc& d, const Shares& s) {
+// Over [base, base + total) of the buffers (the whole message by default;
+// the hybrid route runs it on the part the switch does not take). `wrap`
+// emits the prologue and the join.
+void plan_ar_twoshot(Builder& b, const CliqueDesc& d, const Shares& s, size_t base = 0,
+                     size_t total = ~size_t(0), bool wrap = true) {
   const int n = b.n();
-  b.prologue();
+  if (total == ~size_t(0)) total = d.bytes;
+  if (wrap) b.prologue();
   int ranks[kMaxRanks];
   all_ranks(n, ranks);
   size_t off[kMaxRanks], len[kMaxRanks], host[kMaxRanks], ce[kMaxRanks];
   for (int r = 0; r < n; ++r) {
-    slice_of(d.bytes, n, r, &off[r], &len[r]);
+    slice_of(total, n, r, &off[r], &len[r]);
+    off[r] += base;
     host[r] = n > 1 ? host_share(len[r], s.host_ppm, b.policy()) : 0;
     ce[r] = n > 1 ? ce_share(len[r] - host[r], s.ce_ppm) : 0;
   }
@@ -311,7 +318,7 @@ void plan_ar_twoshot(Builder& b, const CliqueDesc& d, const Shares& s) {
     }
     b.host_stage(ranks, src, n, ranks, dst, n, host[r], true);
   }
-  b.join();
+  if (wrap) b.join();
 }
 
 // ReduceScatter: rank r reduces slot r of every rank's input into its output.
@@ -727,6 +734,29 @@ void plan_bc_ring(Builder& b, const CliqueDesc& d) {
   b.join();
 }
 
+// Hybrid AllReduce: the first share of the message through the switch (an
+// NVLS gang on `hybrid_blocks` SMs per GPU, launched first), the rest by the
+// two-shot P2P kernel, which the remaining SMs run at the same time; both
+// shares cross NVLink concurrently. The split point is 4 KiB aligned.
+void plan_ar_hybrid(Builder& b, const CliqueDesc& d, const Policy& p, const Shares& s) {
+  const int n = b.n();
+  b.prologue();
+  const size_t nv = d.bytes / 10000 * size_t(p.hybrid_nvls_ppm) / 4096 * 4096;
+  for (int r = 0; r < n; ++r) {
+    const StreamId as{Strm::Aux, uint8_t(r), 0};
+    for (int q = 0; q < n; ++q) b.touch(as, q);
+    if (nv) b.nvls(as, r, nv, 0, uint16_t(p.hybrid_blocks));
+  }
+  if (nv) {
+    b.plan().needs.nvls_bytes = p.nvls_round_bytes;
+    b.plan().sm_bytes += nv * size_t(n);
+  }
+  Shares none = s;
+  none.host_ppm = none.ce_ppm = 0;
+  plan_ar_twoshot(b, d, none, nv, d.bytes - nv, false);
+  b.join();
+}
+
 // Push-reduce ReduceScatter / AllReduce (exec/pushred.cu): one gang op per
 // rank on its caller stream after every rank's input is ready.
 void plan_pushred(Builder& b, const CliqueDesc& d) {
@@ -774,6 +804,7 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
     case Algo::AgPush: plan_ag_pull(b, d, s, true); break;
     case Algo::BcRing: plan_bc_ring(b, d); break;
     case Algo::RsPush: case Algo::ArPush: plan_pushred(b, d); break;
+    case Algo::ArHybrid: plan_ar_hybrid(b, d, p, s); break;
     case Algo::BcPull: plan_bc_pull(b, d, s); break;
     case Algo::BcScatter: plan_bc_scatter(b, d, s); break;
     case Algo::ArStaged: plan_staged(b, d, s, true); break;

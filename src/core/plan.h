@@ -77,8 +77,10 @@ inline Loc temp_at(int r, size_t off) { return {Buf::Temp, uint8_t(r), 0, off}; 
 // SmCopy: for each segment i, dst[i][0,len[i]) := src[i][0,len[i]), one kernel.
 // SmReduce: v := op-fold of src[0..nsrc) in index order; every dst[j] := v.
 // HostReduce: the same fold on the CPU over pinned-host buffers.
-// NvlsReduce: one rank's share of an NVLS AllReduce; the N NvlsReduce ops
-// of a plan form a gang that synchronizes inside the kernel.
+// NvlsReduce: one rank's share of a gang collective (NVLS, push chain,
+// push-reduce); the N NvlsReduce ops of a plan form a gang that synchronizes
+// inside the kernel. For AllReduce it covers [src[0].off, +bytes) of every
+// rank's buffers; for the other kinds the whole message.
 enum class OpKind : uint8_t { Record, Wait, CeCopy, SmCopy, SmReduce, HostReduce, NvlsReduce };
 struct PlanOp {
   OpKind kind = OpKind::Record;
@@ -89,6 +91,7 @@ struct PlanOp {
   Loc dst[kMaxRanks];
   size_t len[kMaxRanks] = {};
   size_t bytes = 0;
+  uint16_t grid = 0;  // gang ops: blocks per GPU (0 = one per SM)
 };
 
 // Resources a plan needs; the executor allocates them before submitting.

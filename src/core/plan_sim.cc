@@ -193,10 +193,12 @@ void accesses_of(const PlanOp& op, const SimLayout& lay, const CliqueDesc& d,
       for (int i = 0; i < op.ndst; ++i) add(op.dst[i], op.bytes, true);
       break;
     case OpKind::NvlsReduce:
-      // The gang reads every rank's input and writes every rank's output.
+      // The gang reads every rank's input and writes every rank's output
+      // (for AllReduce, over the op's range).
       for (int q = 0; q < n; ++q) {
-        add(send_at(q, 0), d.bytes, false);
-        add(recv_at(q, 0), d.bytes, true);
+        const bool ranged = d.kind == Kind::AllReduce;
+        add(send_at(q, ranged ? op.src[0].off : 0), ranged ? op.bytes : d.bytes, false);
+        add(recv_at(q, ranged ? op.dst[0].off : 0), ranged ? op.bytes : d.bytes, true);
       }
       break;
     default:
@@ -340,10 +342,18 @@ std::string simulate_plan(const Plan& plan, const SimLayout& lay, const FoldPara
   std::vector<uint8_t> tmp;
   for (int v : order) {
     if (v == g.gang) {
-      // The whole NVLS collective for every rank at once.
-      const size_t bytes = plan.desc.bytes;
-      auto send = [&](int q) { return arenas[size_t(q)].data() + lay.send_off[q]; };
-      auto recv = [&](int q) { return arenas[size_t(q)].data() + lay.recv_off[q]; };
+      // The whole gang collective for every rank at once (an AllReduce gang
+      // over its ops' range).
+      size_t bytes = plan.desc.bytes, goff = 0;
+      if (plan.desc.kind == Kind::AllReduce)
+        for (const PlanOp& op : plan.ops)
+          if (op.kind == OpKind::NvlsReduce) {
+            bytes = op.bytes;
+            goff = op.src[0].off;
+            break;
+          }
+      auto send = [&](int q) { return arenas[size_t(q)].data() + lay.send_off[q] + goff; };
+      auto recv = [&](int q) { return arenas[size_t(q)].data() + lay.recv_off[q] + goff; };
       switch (plan.desc.kind) {
         case Kind::AllReduce: {
           tmp.assign(bytes, 0);

@@ -68,6 +68,7 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else if (a == "ring" && *kind == Kind::Broadcast) *algo = Algo::BcRing;
   else if (a == "push" && *kind == Kind::ReduceScatter) *algo = Algo::RsPush;
   else if (a == "push" && *kind == Kind::AllReduce) *algo = Algo::ArPush;
+  else if (a == "hybrid" && *kind == Kind::AllReduce) *algo = Algo::ArHybrid;
   else return false;
   return true;
 }
@@ -102,6 +103,8 @@ Policy policy_from_env(const EnvLookup& env) {
   if (parse_bool(env("NCCL_B200_NVLS_TMA"), &b)) p.nvls_tma = b;
   if (parse_size(env("NCCL_B200_RING_CHUNK"), &z) && z >= 4096 && z <= (64u << 20) && z % 32 == 0)
     p.ring_chunk = z;
+  if (parse_int(env("NCCL_B200_HYBRID_NVLS_PPM"), &i) && i >= 1000 && i <= 9000) p.hybrid_nvls_ppm = int(i);
+  if (parse_int(env("NCCL_B200_HYBRID_BLOCKS"), &i) && i >= 8 && i <= 1024) p.hybrid_blocks = int(i);
   if (parse_bool(env("NCCL_B200_NVTX"), &b)) p.nvtx = b;
   if (parse_int(env("NCCL_B200_NVLS_THREADS"), &i) && (i == 512 || i == 640 || i == 768))
     p.nvls_threads = int(i);

@@ -34,6 +34,9 @@ struct Policy {
   bool nvls_trace = false;          // per-block phase timing in the NVLS kernels
   bool nvls_tma = true;             // NVLS copier: TMA bulk pipeline (else SM copy warps)
   size_t ring_chunk = 256 * 1024;   // Broadcast chain: bytes per block per step
+  int hybrid_nvls_ppm = 6000;       // hybrid AllReduce: NVLS share of the message (per 10000)
+  int hybrid_blocks = 74;           // hybrid AllReduce: NVLS blocks per GPU (the rest of the SMs
+                                    // run the two-shot kernel)
   bool nvtx = false;                // NVTX range per custom submission
   Algo force_algo[size_t(Kind::Count)] = {Algo::Fallback, Algo::Fallback, Algo::Fallback,
                                           Algo::Fallback};  // Fallback = choose

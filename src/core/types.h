@@ -53,6 +53,7 @@ enum class Algo : uint8_t {
   BcRing,      // pipelined push chain with in-kernel progress words
   RsPush,      // senders store into owners' scratch; owners fold (stores only)
   ArPush,      // RsPush, then owners store the result into every output
+  ArHybrid,    // NVLS on part of the SMs for one share, two-shot P2P for the rest
   Count
 };
 

@@ -885,14 +885,21 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
     return cudaErrorLaunchTimeout;
   }
   if (plan.desc.bytes % 16 != 0) return cudaErrorInvalidValue;
+  const bool ar = plan.desc.kind == Kind::AllReduce;
+  // An AllReduce gang covers the op's range of the buffers (the hybrid
+  // route gives the switch a leading share); the other kinds the message.
+  const size_t off = ar ? op.src[0].off : 0;
+  const size_t range = ar ? op.bytes : plan.desc.bytes;
+  if (off % 16 != 0 || range % 16 != 0) return cudaErrorInvalidValue;
+  const unsigned grid = op.grid ? std::min<unsigned>(op.grid, unsigned(c->blocks)) : unsigned(c->blocks);
   NvlsArgs a{};
-  a.send = static_cast<const char*>(b.send[r]);
-  a.recv = static_cast<char*>(b.recv[r]);
+  a.send = static_cast<const char*>(b.send[r]) + off;
+  a.recv = static_cast<char*>(b.recv[r]) + off;
   a.uc = c->uc[size_t(r)];
   a.mc = c->mc[size_t(r)];
   a.uc_flags = reinterpret_cast<unsigned*>(a.uc + 3 * c->stride);
   a.mc_flags = reinterpret_cast<unsigned*>(a.mc + 3 * c->stride);
-  a.bytes = plan.desc.bytes;
+  a.bytes = range;
   a.round = c->round;
   a.buf_stride = c->stride;
   a.timeout_ns = p.device_timeout_ns;
@@ -908,7 +915,6 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.root = plan.desc.root;
   a.slot = plan.desc.bytes;  // AG send slot / RS receive slot
   a.trace = p.nvls_trace ? c->trace[size_t(r)] : nullptr;
-  const bool ar = plan.desc.kind == Kind::AllReduce;
   // The largest progress value this call publishes (every rank the same):
   // the next call's epoch.
   unsigned long long steps = 0;
@@ -930,7 +936,7 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   const void* fn = pick_kernel(ar, p.nvls_unroll >= 8, a.tma != 0, plan.desc.dtype);
   (void)dev;
   const cudaError_t e =
-      cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(unsigned(threads)), argv, smem, s);
+      cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(unsigned(threads)), argv, smem, s);
   if (r == b.nranks - 1) c->epoch += steps;
   return e;
 }

@@ -157,3 +157,36 @@ def test_nvls_bounded_wait_reports_timeout():
     assert seq[4] == "err1", seq
     assert seq[6] == "ok", seq
     assert line[2] == "1"
+
+
+HYBRID_CHILD = r"""
+import sys, torch
+sys.path.insert(0, {repo!r}); sys.path.insert(0, {repo!r} + "/tests")
+from scc26_nccl_shim_b200.parallel.nccl import Nccl
+from scc26_nccl_shim_b200._core import ALGO
+from test_gpu_abi import run_kind
+n = {n}
+devs = list(range(n))
+nc = Nccl("interposer")
+comms = nc.comm_init_all(devs)
+for c in ((64 << 20) // 4, (100 << 20) // 4 + 4, (48 << 20) // 4):
+    run_kind(nc, "allreduce", comms, devs, c)
+    run_kind(nc, "allreduce", comms, devs, c, inplace=True)
+run_kind(nc, "allreduce", comms, devs, (64 << 20) // 2, dtype=torch.bfloat16)
+run_kind(nc, "allreduce", comms, devs, (64 << 20) // 4, op="avg")
+print("RESULT", nc.custom_calls(ALGO["ar_hybrid"]))
+"""
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_nvls_hybrid_allreduce(n):
+    """The hybrid AllReduce: a leading share through the switch on part of the
+    SMs while the two-shot P2P kernel reduces the rest on the other SMs."""
+    need_gpus(n)
+    env = dict(os.environ, NCCL_B200_NVLS="on", NCCL_B200_ALGO="ar=hybrid", NCCL_B200_TUNE="0",
+               NCCL_B200_FIRST_PASS="0")
+    r = subprocess.run([sys.executable, "-c", HYBRID_CHILD.format(repo=REPO, n=n)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    assert int(line[1]) >= 8, line
