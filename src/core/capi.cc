@@ -352,6 +352,16 @@ double nb_policy_value(const char* env, const char* field) {
   if (f == "timeout_ns") return double(p.device_timeout_ns);
   if (f == "force_ar") return double(int(p.force_algo[0]));
   if (f == "force_bc") return double(int(p.force_algo[3]));
+  if (f == "force_ag") return double(int(p.force_algo[1]));
+  if (f == "force_rs") return double(int(p.force_algo[2]));
+  if (f == "ring_chunk") return double(p.ring_chunk);
+  if (f == "hybrid_nvls_ppm") return p.hybrid_nvls_ppm;
+  if (f == "hybrid_blocks") return p.hybrid_blocks;
+  if (f == "nvls_tma") return p.nvls_tma;
+  if (f == "nvls_trace") return p.nvls_trace;
+  if (f == "nvtx") return p.nvtx;
+  if (f == "nvls_movers") return p.nvls_movers;
+  if (f == "tune_bytes") return double(p.tune_bytes);
   return -1;
 }
 

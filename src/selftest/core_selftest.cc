@@ -48,6 +48,7 @@ int nb_gate_clique(const nb_call_t* calls, int n, int flags, const char* env, in
 int nb_fault_policy(const char* spec, int nranks, uint64_t bytes, uint64_t* at, uint64_t* first_data);
 int nb_summary_sample(char* out, size_t cap);
 int nb_calib_roundtrip(double sm, const char* key, double* back);
+int nb_calib_small(int pref, int small_pref, int below_mib, uint64_t logical, int* small_ce);
 }
 
 namespace {
@@ -206,6 +207,9 @@ int main(int argc, char** argv) {
   nb_summary_sample(buf, 16);  // truncating copy
   double back = 0;
   nb_calib_roundtrip(123.5, "GPU-x|driver|nccl", &back);
+  int ce = 0;
+  for (uint64_t logical : {uint64_t(1) << 20, uint64_t(600) << 20, uint64_t(8) << 30})
+    nb_calib_small(7, 1, 512, logical, &ce);
   std::printf("%s\n", failures ? "FAILED" : "OK");
   return failures ? 1 : 0;
 }

@@ -185,3 +185,24 @@ def test_policy_parsing():
     assert c.policy_value({"NCCL_B200_HOST_PIECE": "1000"}, "host_piece") == 16 << 20  # not 16B-aligned
     assert c.policy_value({"NCCL_B200_TIMEOUT_MS": "250"}, "timeout_ns") == 250e6
     assert c.policy_value({"NCCL_B200_ALGO": "bc=scatter"}, "force_bc") == c.ALGO["bc_scatter"]
+
+
+def test_policy_parsing_of_engine_knobs():
+    A = c.ALGO
+    env = {"NCCL_B200_ALGO": "ar=hybrid,ag=push,rs=push,bc=ring"}
+    assert c.policy_value(env, "force_ar") == A["ar_hybrid"]
+    assert c.policy_value(env, "force_ag") == A["ag_push"]
+    assert c.policy_value(env, "force_rs") == A["rs_push"]
+    assert c.policy_value(env, "force_bc") == A["bc_ring"]
+    assert c.policy_value({"NCCL_B200_RING_CHUNK": "64K"}, "ring_chunk") == 64 << 10
+    assert c.policy_value({"NCCL_B200_RING_CHUNK": "100"}, "ring_chunk") == 256 << 10  # not a 32-byte multiple
+    assert c.policy_value({"NCCL_B200_HYBRID_NVLS_PPM": "5000"}, "hybrid_nvls_ppm") == 5000
+    assert c.policy_value({"NCCL_B200_HYBRID_NVLS_PPM": "9500"}, "hybrid_nvls_ppm") == 6000
+    assert c.policy_value({"NCCL_B200_HYBRID_BLOCKS": "100"}, "hybrid_blocks") == 100
+    assert c.policy_value({}, "nvls_tma") == 1
+    assert c.policy_value({"NCCL_B200_NVLS_TMA": "0"}, "nvls_tma") == 0
+    assert c.policy_value({"NCCL_B200_NVLS_TRACE": "1", "NCCL_B200_NVTX": "on"}, "nvls_trace") == 1
+    assert c.policy_value({"NCCL_B200_NVTX": "on"}, "nvtx") == 1
+    assert c.policy_value({"NCCL_B200_NVLS_MOVERS": "384"}, "nvls_movers") == 384
+    assert c.policy_value({"NCCL_B200_NVLS_MOVERS": "400"}, "nvls_movers") == 512  # not a warp multiple
+    assert c.policy_value({}, "tune_bytes") == 4 << 30
