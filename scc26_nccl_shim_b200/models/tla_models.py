@@ -51,6 +51,14 @@ rank's buffer s % B (the multicast store), publish s + 1. Invariants:
 every ld_reduce reads round s inputs, every copy-out reads round s results,
 no deadlock. Broken variants: two buffers instead of three, or a mover that
 waits only for its own copier.
+
+BroadcastChain (one block index of the push chain, exec/ring.cu): ranks
+0 -> 1 -> ... -> N-1 (rank 0 the root), S steps. The root stores piece k
+into rank 1's output and publishes flag[1] = k + 1. Rank r in 1..N-2 waits
+until flag[r] >= k + 1 (unless SkipWait), reads piece k from its own output,
+stores it into rank r+1's output and publishes flag[r+1] = k + 1. Invariants:
+every forwarded piece had arrived (ForwardedArrived), no deadlock, and at
+the end every output holds every piece.
 """
 from __future__ import annotations
 
@@ -348,3 +356,42 @@ def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True) -> Re
         return all(x >= R + 2 for x in st[0]) and all(x >= R for x in st[2])
 
     return _bfs(init, actions, [("RoundsInOrder", lambda st: not st[7])], done=done)
+
+
+# --------------------------------------------------------------------------
+# BroadcastChain (progress words of the Broadcast push chain)
+# --------------------------------------------------------------------------
+
+def check_broadcast_chain(nranks=4, steps=3, skip_wait=False) -> Result:
+    """State: k[r] (next step of rank r), ph[r] (0 wait, 1 read, 2 write),
+    flag[r], got[r] (bitmask of pieces in rank r's output), bad."""
+    N, S = nranks, steps
+    full = (1 << S) - 1
+    init = (tuple([0] * N), tuple([0] * N), tuple([0] * N), tuple([full] + [0] * (N - 1)), False)
+
+    def setv(t, i, v):
+        return t[:i] + (v,) + t[i + 1:]
+
+    def actions(st):
+        k, ph, flag, got, bad = st
+        for r in range(N - 1):  # the last rank only receives
+            j = k[r]
+            if j >= S:
+                continue
+            if ph[r] == 0:
+                if r == 0 or skip_wait or flag[r] >= j + 1:
+                    yield (k, setv(ph, r, 1), flag, got, bad)
+            elif ph[r] == 1:
+                yield (k, setv(ph, r, 2), flag, got, bad or not (got[r] >> j) & 1)
+            else:
+                ng = setv(got, r + 1, got[r + 1] | (((got[r] >> j) & 1) << j))
+                yield (setv(k, r, j + 1), setv(ph, r, 0), setv(flag, r + 1, j + 1), ng, bad)
+
+    def done(st):
+        return all(x >= S for x in st[0][:N - 1])
+
+    def complete(st):
+        return not done(st) or all(g == full for g in st[3])
+
+    return _bfs(init, actions, [("ForwardedArrived", lambda st: not st[4]),
+                                ("AllPiecesDelivered", complete)], done=done)

@@ -74,9 +74,23 @@ def test_nvls_allreduce_broken_mover_waits_own_copier_only(n):
     assert not r.ok and r.violation == "RoundsInOrder"
 
 
+@pytest.mark.parametrize("n,steps", [(2, 3), (3, 3), (4, 3), (5, 2)])
+def test_broadcast_chain_holds(n, steps):
+    """The push chain's progress words: a rank forwards only pieces it has
+    received, every output ends with every piece, no deadlock."""
+    r = m.check_broadcast_chain(nranks=n, steps=steps)
+    assert r.ok, (r.violation, r.trace)
+
+
+def test_broadcast_chain_broken_forwards_early():
+    r = m.check_broadcast_chain(nranks=3, steps=2, skip_wait=True)
+    assert not r.ok and r.violation == "ForwardedArrived"
+
+
 def test_tla_sources_present():
     for f in ["GroupFallbackN.tla", "HostLaneReuseN.tla", "GroupFallbackN.cfg",
               "GroupFallbackN-broken.cfg", "HostLaneReuseN.cfg", "HostLaneReuseN-broken.cfg",
               "PushReduceN.tla", "PushReduceN.cfg", "PushReduceN-broken.cfg",
-              "NvlsAllReduceN.tla", "NvlsAllReduceN.cfg", "NvlsAllReduceN-broken.cfg"]:
+              "NvlsAllReduceN.tla", "NvlsAllReduceN.cfg", "NvlsAllReduceN-broken.cfg",
+              "BroadcastChainN.tla", "BroadcastChainN.cfg", "BroadcastChainN-broken.cfg"]:
         assert os.path.exists(os.path.join(REPO, "tla", f)), f
