@@ -97,12 +97,20 @@ extern "C" int nb_staged_allreduce_noalloc(const void* const* sends, void* const
   size_t es = 0;
   const void* kernel = nullptr;
   switch (dtype) {
-    case 7: es = 2; kernel = reinterpret_cast<const void*>(staged_fold_noalloc_kernel<__half>); break;
-    case 8: es = 4; kernel = reinterpret_cast<const void*>(staged_fold_noalloc_kernel<float>); break;
-    case 10: es = 2; kernel = reinterpret_cast<const void*>(staged_fold_noalloc_kernel<__nv_bfloat16>); break;
+    case NB_NOALLOC_FLOAT16: es = 2; kernel = reinterpret_cast<const void*>(staged_fold_noalloc_kernel<__half>); break;
+    case NB_NOALLOC_FLOAT32: es = 4; kernel = reinterpret_cast<const void*>(staged_fold_noalloc_kernel<float>); break;
+    case NB_NOALLOC_BFLOAT16:
+      es = 2;
+      kernel = reinterpret_cast<const void*>(staged_fold_noalloc_kernel<__nv_bfloat16>);
+      break;
     default:
-      set_err(err, errcap, "bad arguments: dtype must be float16, float32 or bfloat16");
+      set_err(err, errcap, "bad arguments: dtype must be ncclFloat16, ncclFloat32 or ncclBfloat16");
       return -1;
+  }
+  // A count whose byte size wraps would pass the capacity check below.
+  if (count > ~0ull / es) {
+    set_err(err, errcap, "bad arguments: count * element size overflows 64 bits");
+    return -1;
   }
   const unsigned long long bytes = count * es;
   // Slices on 32-byte boundaries, the last takes the remainder (the largest).
@@ -124,8 +132,13 @@ extern "C" int nb_staged_allreduce_noalloc(const void* const* sends, void* const
     return int(e);
   }
   int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) {
+    set_err(err, errcap, "cannot query the current device's SM count");
+    return int(e);
+  }
+  if (sms < 1) sms = 1;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   for (int r = 0; r < nranks; ++r) {
     const unsigned long long off = base * (unsigned long long)r;
@@ -137,7 +150,10 @@ extern "C" int nb_staged_allreduce_noalloc(const void* const* sends, void* const
       e = cudaMemcpyAsync(static_cast<unsigned char*>(scratch) + (unsigned long long)(j++) * largest,
                           static_cast<const unsigned char*>(sends[q]) + off, len,
                           cudaMemcpyDeviceToDevice, s);
-      if (e != cudaSuccess) return int(e);
+      if (e != cudaSuccess) {
+        set_err(err, errcap, "cudaMemcpyAsync into the static scratch failed");
+        return int(e);
+      }
     }
     FoldArgs a{};
     a.local = static_cast<const unsigned char*>(sends[r]) + off;
@@ -151,7 +167,10 @@ extern "C" int nb_staged_allreduce_noalloc(const void* const* sends, void* const
     const unsigned blocks = unsigned(want < (unsigned long long)(sms * 4) ? (want ? want : 1) : sms * 4);
     void* argv[] = {&a};
     e = cudaLaunchKernel(kernel, dim3(blocks), dim3(512), argv, 0, s);
-    if (e != cudaSuccess) return int(e);
+    if (e != cudaSuccess) {
+      set_err(err, errcap, "launch of the staged fold failed");
+      return int(e);
+    }
   }
   return 0;
 }

@@ -20,8 +20,11 @@
 // output: exactly the staged route's numerics (bit-identical to it).
 //
 // Limits and sharing:
-//  * The scratch is a 32 MiB file-scope device array; every GPU on which the
-//    entry point runs holds it until the process exits. A call is refused
+//  * The scratch is a 32 MiB file-scope device array. With CUDA's default lazy
+//    module loading only a GPU on which the entry point runs holds it, until
+//    the process exits; with CUDA_MODULE_LOADING=EAGER the whole module loads
+//    with the context, so every GPU the process (or an application that
+//    preloads the interposer) initializes reserves the 32 MiB. A call is refused
 //    (return value -2, message in `err`) when (nranks - 1) times the largest
 //    slice exceeds 32 MiB.
 //  * Every call shares that one array and it keeps the last call's contents;
@@ -39,9 +42,17 @@
 
 extern "C" {
 
-// dtype: the interposer's type code (7 float16, 8 float32, 10 bfloat16).
+enum {
+  NB_NOALLOC_FLOAT16 = 6,   // ncclFloat16
+  NB_NOALLOC_FLOAT32 = 7,   // ncclFloat32
+  NB_NOALLOC_BFLOAT16 = 9,  // ncclBfloat16
+};
+
+// dtype: an ncclDataType_t value -- ncclFloat16 (6), ncclFloat32 (7) or
+// ncclBfloat16 (9); the named constants below carry the same values.
 // Returns 0 on success, -1 on bad arguments, -2 when the message is too large
-// for the static scratch, or a CUDA error code.
+// for the static scratch, or a CUDA error code; every non-zero return leaves
+// a message in `err` (when errcap > 0).
 int nb_staged_allreduce_noalloc(const void* const* sends, void* const* recvs, int nranks,
                                 uint64_t count, int dtype, void* stream, char* err, size_t errcap);
 

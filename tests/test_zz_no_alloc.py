@@ -1,6 +1,7 @@
 """The allocation-free staged AllReduce entry point, called through its exported
 C symbol, against the library's existing staged AllReduce (the virtual-rank
-plan runner, whose scratch the executor allocates). Callers that cannot
+plan runner, whose scratch the executor allocates) and against a torch fp32
+fold in rank order. The dtype argument is an ncclDataType_t value. Callers that cannot
 allocate device memory (allocator hooks, capture-sensitive code, hosts that
 own all device memory) use this entry point; it stages through a fixed
 file-scope device array instead. Two calls in a row must both match, which
@@ -29,7 +30,9 @@ def entry():
     return fn, int(L.nb_noalloc_scratch_bytes())
 
 
-DTYPE_CODE = {torch.float32: 8, torch.float16: 7, torch.bfloat16: 10}
+# ncclDataType_t values (nccl.h): ncclFloat16 = 6, ncclFloat32 = 7, ncclBfloat16 = 9.
+DTYPE_CODE = {torch.float32: 7, torch.float16: 6, torch.bfloat16: 9}
+NCCL_FLOAT64 = 8
 
 
 def data(n, count, dtype, seed):
@@ -56,9 +59,14 @@ def test_noalloc_matches_staged_route(dtype, n):
         assert rc == 0, (rc, err.value)
         ref = [torch.empty_like(sends[0]) for _ in range(n)]
         emu.plan("ar_staged", "allreduce", sends, ref)
+        fold = sends[0].float()
+        for q in range(1, n):
+            fold = fold + sends[q].float()
+        fold = fold.to(dtype)
         torch.cuda.synchronize()
         for r in range(n):
             assert torch.equal(ours[r], ref[r]), (call, r)
+            assert torch.equal(ours[r], fold), (call, r)
 
 
 def test_noalloc_rejects_oversized_messages():
@@ -70,6 +78,21 @@ def test_noalloc_rejects_oversized_messages():
     x = [torch.zeros(8, device="cuda:0") for _ in range(n)]
     err = C.create_string_buffer(256)
     ptrs = (C.c_void_p * n)(*[t.data_ptr() for t in x])
-    rc = fn(ptrs, ptrs, n, count, 8, C.c_void_p(0), err, 256)
+    rc = fn(ptrs, ptrs, n, count, DTYPE_CODE[torch.float32], C.c_void_p(0), err, 256)
     assert rc == -2
     assert b"static scratch holds" in err.value
+
+
+def test_noalloc_rejects_bad_dtype_and_overflowing_count():
+    need_gpus(1)
+    fn, cap = entry()
+    n = 2
+    x = [torch.zeros(8, device="cuda:0") for _ in range(n)]
+    err = C.create_string_buffer(256)
+    ptrs = (C.c_void_p * n)(*[t.data_ptr() for t in x])
+    # ncclFloat64 is not one of the entry point's types.
+    assert fn(ptrs, ptrs, n, 8, NCCL_FLOAT64, C.c_void_p(0), err, 256) == -1
+    assert b"ncclFloat32" in err.value
+    # A count whose byte size wraps 64 bits is refused before any arithmetic.
+    assert fn(ptrs, ptrs, n, (1 << 63) + 1, DTYPE_CODE[torch.float32], C.c_void_p(0), err, 256) == -1
+    assert b"overflows" in err.value
