@@ -71,12 +71,22 @@ def args_parser():
 # Parent: torchrun plumbing and the child process
 # --------------------------------------------------------------------------
 
+def reference_source() -> str | None:
+    """The reference shim's source file, under BASELINE.json's reference_path."""
+    try:
+        with open(os.path.join(REPO, "BASELINE.json")) as f:
+            root = json.load(f).get("reference_path")
+    except (OSError, ValueError):
+        return None
+    return os.path.join(root, "shim", "nccl_collectives_shim.cu") if root else None
+
+
 def ensure_reference() -> str | None:
     """Build the unmodified reference shim (its README's nvcc line) if missing."""
     if os.path.exists(REF_LIB):
         return None
-    src = "/root/reference/shim/nccl_collectives_shim.cu"
-    if not os.path.exists(src):
+    src = reference_source()
+    if not src or not os.path.exists(src):
         return "reference source not present on this machine and baseline/_ref not built"
     import hashlib
     import nvidia.nccl  # type: ignore

@@ -72,13 +72,25 @@ class Result:
     states: int
     violation: str | None = None
     trace: list | None = None
+    checked: tuple = ()          # names of the invariants this run checked
+    deadlock_checked: bool = False
 
 
-def _bfs(init, actions, invariants, max_states=2_000_000, done=None):
+def _bfs(init, actions, invariants, max_states=2_000_000, done=None, only=None):
     """Breadth-first over every reachable state. With `done`, a state with no
-    successor that is not done is reported as the violation "Deadlock"."""
+    successor that is not done is reported as the violation "Deadlock".
+    `only` restricts the check to the named invariants (a configuration's
+    INVARIANTS list); naming one the model does not have is an error."""
+    if only is not None:
+        have = {name for name, _ in invariants}
+        missing = [x for x in only if x not in have]
+        if missing:
+            raise ValueError(f"the model has no invariant {missing}")
+        invariants = [(name, inv) for name, inv in invariants if name in only]
     seen = {init: None}
     q = deque([init])
+    names = tuple(name for name, _ in invariants)
+    dl = done is not None
 
     def trace_to(s):
         trace = []
@@ -92,7 +104,7 @@ def _bfs(init, actions, invariants, max_states=2_000_000, done=None):
         s = q.popleft()
         for name, inv in invariants:
             if not inv(s):
-                return Result(False, len(seen), name, trace_to(s))
+                return Result(False, len(seen), name, trace_to(s), names, dl)
         succ = 0
         for t in actions(s):
             succ += 1
@@ -102,8 +114,8 @@ def _bfs(init, actions, invariants, max_states=2_000_000, done=None):
                     raise RuntimeError("state space too large")
                 q.append(t)
         if done is not None and succ == 0 and not done(s):
-            return Result(False, len(seen), "Deadlock", trace_to(s))
-    return Result(True, len(seen))
+            return Result(False, len(seen), "Deadlock", trace_to(s), names, dl)
+    return Result(True, len(seen), checked=names, deadlock_checked=dl)
 
 
 # --------------------------------------------------------------------------
@@ -135,7 +147,7 @@ def group_end(state, nranks):
     return (seen, fwd if run else fwd + pend, (), pt, uns, True, run)
 
 
-def check_group_fallback(nranks=2, max_calls=5, skip_unsupported_flush=False) -> Result:
+def check_group_fallback(nranks=2, max_calls=5, skip_unsupported_flush=False, only=None) -> Result:
     ops = group_fallback_ops(nranks)
     init = ((), (), (), False, False, False, False)
 
@@ -171,7 +183,7 @@ def check_group_fallback(nranks=2, max_calls=5, skip_unsupported_flush=False) ->
             ("BufferedOrder", buffered_order), ("Complete", complete)]
     if skip_unsupported_flush:
         invs = [("OrderedPrefix", ordered_prefix)]
-    return _bfs(init, actions, invs)
+    return _bfs(init, actions, invs, only=only)
 
 
 # --------------------------------------------------------------------------
@@ -179,7 +191,7 @@ def check_group_fallback(nranks=2, max_calls=5, skip_unsupported_flush=False) ->
 # --------------------------------------------------------------------------
 
 def check_host_lane_reuse(pieces=5, lanes=4, sources=1, dests=1, skip_reuse_wait=False,
-                          fold=None) -> Result:
+                          fold=None, only=None) -> Result:
     """State: produced[k][q], folded[k], consumed[k][r], bounce[q][lane],
     out[lane], output[k][r]. Values are piece numbers (0 = empty)."""
     fold = sources > 1 if fold is None else fold
@@ -240,14 +252,14 @@ def check_host_lane_reuse(pieces=5, lanes=4, sources=1, dests=1, skip_reuse_wait
         return all(all((k, q) in produced for q in range(sources)) for (k, _) in consumed)
 
     return _bfs(init, actions, [("CorrectOutputs", correct_outputs),
-                                ("ProducedBeforeConsumed", produced_before_consumed)])
+                                ("ProducedBeforeConsumed", produced_before_consumed)], only=only)
 
 
 # --------------------------------------------------------------------------
 # PushReduce (progress words of the push-reduce engine)
 # --------------------------------------------------------------------------
 
-def check_push_reduce(nranks=3, rounds=4, depth=2, skip_consumed_wait=False) -> Result:
+def check_push_reduce(nranks=3, rounds=4, depth=2, skip_consumed_wait=False, only=None) -> Result:
     """State: sj[s] (sender round), sphase[s] (0 write, 1 publish), rj[q]
     (owner round), rphase[q] (0 wait, 1 read, 2 consume), filled[q][s],
     consumed[s][q], slot[q][s][d] (round number held, -1 empty), stale
@@ -295,14 +307,14 @@ def check_push_reduce(nranks=3, rounds=4, depth=2, skip_consumed_wait=False) -> 
     def done(st):
         return all(x >= R for x in st[0]) and all(x >= R for x in st[2])
 
-    return _bfs(init, actions, [("NoStaleRead", lambda st: not st[7])], done=done)
+    return _bfs(init, actions, [("NoStaleRead", lambda st: not st[7])], done=done, only=only)
 
 
 # --------------------------------------------------------------------------
 # NvlsAllReduce (progress words of the NVLS AllReduce kernel)
 # --------------------------------------------------------------------------
 
-def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True) -> Result:
+def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, only=None) -> Result:
     """State: cs[r], cph[r] (copier step, 0 wait/copy-out, 1 copy-in+publish),
     ms[r], mph[r] (mover step, 0 wait, 1 read, 2 write+publish), cflag[r],
     mflag[r], buf[r][b][q] = (round, 0 input | 1 reduced) or None, bad."""
@@ -355,14 +367,14 @@ def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True) -> Re
     def done(st):
         return all(x >= R + 2 for x in st[0]) and all(x >= R for x in st[2])
 
-    return _bfs(init, actions, [("RoundsInOrder", lambda st: not st[7])], done=done)
+    return _bfs(init, actions, [("RoundsInOrder", lambda st: not st[7])], done=done, only=only)
 
 
 # --------------------------------------------------------------------------
 # BroadcastChain (progress words of the Broadcast push chain)
 # --------------------------------------------------------------------------
 
-def check_broadcast_chain(nranks=4, steps=3, skip_wait=False) -> Result:
+def check_broadcast_chain(nranks=4, steps=3, skip_wait=False, only=None) -> Result:
     """State: k[r] (next step of rank r), ph[r] (0 wait, 1 read, 2 write),
     flag[r], got[r] (bitmask of pieces in rank r's output), bad."""
     N, S = nranks, steps
@@ -394,4 +406,114 @@ def check_broadcast_chain(nranks=4, steps=3, skip_wait=False) -> Result:
         return not done(st) or all(g == full for g in st[3])
 
     return _bfs(init, actions, [("ForwardedArrived", lambda st: not st[4]),
-                                ("AllPiecesDelivered", complete)], done=done)
+                                ("AllPiecesDelivered", complete)], done=done, only=only)
+
+
+# --------------------------------------------------------------------------
+# The committed TLC configurations drive the checkers
+# --------------------------------------------------------------------------
+
+# Spec module -> (checker, {cfg constant: checker keyword}).
+SPECS = {
+    "GroupFallbackN": (check_group_fallback, {"N": "nranks", "MaxCalls": "max_calls",
+                                              "SkipUnsupportedFlush": "skip_unsupported_flush"}),
+    "HostLaneReuseN": (check_host_lane_reuse, {"Pieces": "pieces", "Lanes": "lanes", "S": "sources",
+                                               "D": "dests", "SkipReuseWait": "skip_reuse_wait"}),
+    "PushReduceN": (check_push_reduce, {"N": "nranks", "R": "rounds", "D": "depth",
+                                        "SkipConsumedWait": "skip_consumed_wait"}),
+    "NvlsAllReduceN": (check_nvls_allreduce, {"N": "nranks", "R": "rounds", "B": "bufs",
+                                              "MoverWaitsAll": "mover_waits_all"}),
+    "BroadcastChainN": (check_broadcast_chain, {"N": "nranks", "S": "steps", "SkipWait": "skip_wait"}),
+}
+
+
+@dataclass
+class Cfg:
+    constants: dict
+    invariants: list
+    check_deadlock: bool
+    specification: str
+
+
+def _value(tok: str):
+    if tok in ("TRUE", "FALSE"):
+        return tok == "TRUE"
+    return int(tok)
+
+
+def parse_cfg(text: str) -> Cfg:
+    """The subset of TLC's configuration language the committed files use:
+    SPECIFICATION, CONSTANT(S) name = value, INVARIANT(S) names, CHECK_DEADLOCK."""
+    consts, invs, deadlock, spec = {}, [], True, ""
+    section = None
+    for raw in text.splitlines():
+        line = raw.split("\\*")[0].strip()
+        if not line:
+            continue
+        head, _, rest = line.partition(" ")
+        if head in ("CONSTANT", "CONSTANTS"):
+            section, line = "const", rest.strip()
+        elif head in ("INVARIANT", "INVARIANTS"):
+            section, line = "inv", rest.strip()
+        elif head == "SPECIFICATION":
+            spec, section = rest.strip(), None
+            continue
+        elif head == "CHECK_DEADLOCK":
+            deadlock, section = _value(rest.strip()), None
+            continue
+        if not line:
+            continue
+        if section == "const":
+            name, eq, val = line.partition("=")
+            if not eq:
+                raise ValueError(f"constant without a value: {raw!r}")
+            consts[name.strip()] = _value(val.strip())
+        elif section == "inv":
+            invs.extend(line.split())
+        else:
+            raise ValueError(f"unrecognized line: {raw!r}")
+    return Cfg(consts, invs, deadlock, spec)
+
+
+def parse_tla(text: str) -> tuple:
+    """(module name, declared constants, names of the defined operators)."""
+    import re
+    m = re.search(r"-+\s*MODULE\s+(\w+)", text)
+    decl = re.search(r"^CONSTANTS?\s+([^\n]+)", text, re.M)
+    consts = [c.strip() for c in decl.group(1).split(",")] if decl else []
+    defs = set(re.findall(r"^(\w+)(?:\([^)]*\))?\s*==", text, re.M))
+    return (m.group(1) if m else None), consts, defs
+
+
+def check_cfg(cfg_path: str) -> tuple:
+    """Run the checker of a committed configuration with exactly its
+    constants. Verifies first that the configuration and its spec agree with
+    the checker: the same constants as the spec declares, invariants the spec
+    defines and the checker checks, and the same deadlock setting.
+    Returns (Cfg, Result)."""
+    import os
+    cfg_text = open(cfg_path).read()
+    cfg = parse_cfg(cfg_text)
+    base = os.path.basename(cfg_path)
+    module = base.split(".")[0].replace("-broken", "")
+    tla_path = os.path.join(os.path.dirname(cfg_path), module + ".tla")
+    name, declared, defined = parse_tla(open(tla_path).read())
+    if name != module:
+        raise ValueError(f"{tla_path}: module {name}, expected {module}")
+    checker, kw = SPECS[module]
+    if set(cfg.constants) != set(declared) or set(declared) != set(kw):
+        raise ValueError(f"{base}: constants {sorted(cfg.constants)}, spec declares {declared}, "
+                         f"checker maps {sorted(kw)}")
+    if cfg.specification not in defined:
+        raise ValueError(f"{base}: SPECIFICATION {cfg.specification} is not defined in {module}.tla")
+    for inv in cfg.invariants:
+        if inv not in defined:
+            raise ValueError(f"{base}: invariant {inv} is not defined in {module}.tla")
+    res = checker(**{kw[k]: v for k, v in cfg.constants.items()}, only=list(cfg.invariants))
+    if set(res.checked) != set(cfg.invariants):
+        raise ValueError(f"{base}: the checker checked {res.checked}, the configuration lists "
+                         f"{cfg.invariants}")
+    if res.deadlock_checked != cfg.check_deadlock:
+        raise ValueError(f"{base}: CHECK_DEADLOCK {cfg.check_deadlock}, checker "
+                         f"{res.deadlock_checked}")
+    return cfg, res

@@ -94,3 +94,41 @@ def test_tla_sources_present():
               "NvlsAllReduceN.tla", "NvlsAllReduceN.cfg", "NvlsAllReduceN-broken.cfg",
               "BroadcastChainN.tla", "BroadcastChainN.cfg", "BroadcastChainN-broken.cfg"]:
         assert os.path.exists(os.path.join(REPO, "tla", f)), f
+
+
+def _cfgs():
+    d = os.path.join(REPO, "tla")
+    return sorted(f for f in os.listdir(d) if f.endswith(".cfg"))
+
+
+def test_every_spec_has_a_good_and_a_broken_cfg():
+    names = _cfgs()
+    assert len(names) == 2 * len(m.SPECS), names
+    for spec in m.SPECS:
+        assert f"{spec}.cfg" in names and f"{spec}-broken.cfg" in names, spec
+
+
+@pytest.mark.parametrize("cfg", _cfgs())
+def test_committed_cfg_checked_with_its_own_constants(cfg):
+    """Each committed configuration runs the checker with the constants it
+    states; the constants, invariants and deadlock setting must agree with
+    the spec file and the checker. Good configurations hold; broken ones
+    are refuted on one of their own invariants (or a deadlock)."""
+    c, r = m.check_cfg(os.path.join(REPO, "tla", cfg))
+    if cfg.endswith("-broken.cfg"):
+        assert not r.ok, cfg
+        assert r.violation in c.invariants or (r.violation == "Deadlock" and c.check_deadlock)
+    else:
+        assert r.ok, (cfg, r.violation, r.trace)
+
+
+def test_cfg_parser_rejects_drift(tmp_path):
+    """A configuration whose constants drift from the spec is rejected."""
+    src = open(os.path.join(REPO, "tla", "PushReduceN.cfg")).read()
+    (tmp_path / "PushReduceN.tla").write_text(open(os.path.join(REPO, "tla", "PushReduceN.tla")).read())
+    (tmp_path / "PushReduceN.cfg").write_text(src.replace("D = 2", "Depth = 2"))
+    with pytest.raises(ValueError):
+        m.check_cfg(str(tmp_path / "PushReduceN.cfg"))
+    (tmp_path / "PushReduceN.cfg").write_text(src.replace("NoStaleRead", "NoSuchInvariant"))
+    with pytest.raises(ValueError):
+        m.check_cfg(str(tmp_path / "PushReduceN.cfg"))
