@@ -176,16 +176,19 @@ class Nccl:
 
 
 def collective(nc: Nccl, kind: str, sends, recvs, comms, streams, op="sum", root=0):
-    """One grouped collective over every rank of a clique (rank i = comms[i])."""
+    """One grouped collective over every rank of a clique (rank i = comms[i]).
+    `op` is one op for every rank (a name or an ncclRedOp_t value), or a list
+    with one per rank (PreMulSum ops are created per communicator)."""
     with nc.group():
         for i, comm in enumerate(comms):
             s = streams[i]
+            o = op[i] if isinstance(op, (list, tuple)) else op
             if kind == "allreduce":
-                r = nc.all_reduce(sends[i], recvs[i], comm, s, op)
+                r = nc.all_reduce(sends[i], recvs[i], comm, s, o)
             elif kind == "allgather":
                 r = nc.all_gather(sends[i], recvs[i], comm, s)
             elif kind == "reducescatter":
-                r = nc.reduce_scatter(sends[i], recvs[i], comm, s, op)
+                r = nc.reduce_scatter(sends[i], recvs[i], comm, s, o)
             elif kind == "broadcast":
                 r = nc.broadcast(sends[i], recvs[i], root, comm, s)
             else:

@@ -34,8 +34,24 @@ overwrites every input on its caller stream right after the call, which is
 safe only if the call's side streams were joined back into the caller
 streams; --fresh-streams issues every iteration on new caller streams.
 
+Route oracle: every case also states the route an independent restatement
+of the routing rules predicts (parallel/oracle.py); the route the library
+reports running must match it, or the case FAILs with status ROUTE.
+--oracle-drop VAR hides one variable from the oracle only (the library still
+reads it), which must turn affected cases into ROUTE failures: the route
+check's own mutation test.
+
+Case sets: the standard cases (every kind, fp32/bf16/fp16, in and out of
+place, odd tails, int types, every reduction op including avg and
+PreMulSum); boundary cases (-1/0/+1 element around each kind's threshold);
+--edges: the pipeline edges of the engines (NVLS round, push-reduce piece
+round, push-chain step, host-lane piece) at -1/0/+1 vector; --big: the
+2 GiB, 4 GiB and 8 GiB logical-size edges, the last at the message cap and
+one element above it (which must fall back). Data for the large cases are
+generated and checked in chunks.
+
 Output: one TSV row per case:
-  case iters bytes mismatches status guard_bad route kind mode
+  case iters bytes mismatches status guard_bad route expect kind mode
 Parity: tests/stress_check.cu of the reference (two GPUs, fixed thresholds).
 """
 from __future__ import annotations
@@ -49,10 +65,12 @@ import torch
 
 from .._core import ALGO, policy_value
 from ..utils.data import adversarial, exact
+from . import oracle
 from .nccl import Nccl, collective
 
 GUARD = 4096
 PATTERN = 0xA5
+CHUNK = 64 << 20  # elements generated / checked at a time
 DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16,
           "int32": torch.int32, "int8": torch.int8}
 
@@ -87,7 +105,67 @@ def standard_cases(n: int, scale: int = 1) -> list[Case]:
     cases.append(Case("allgather_int8", "allgather", "int8", base // n + 1))
     cases.append(Case("broadcast_root0_int8", "broadcast", "int8", base * 4 + 5, root=0))
     cases.append(Case("allreduce_max", "allreduce", "float32", base, op="max"))
+    # Every reduction op, and PreMulSum with one host scalar per rank.
+    for op in ("prod", "min", "avg", "premulsum"):
+        cases.append(Case(f"allreduce_{op}", "allreduce", "float32", base + 5, op=op))
+        cases.append(Case(f"allreduce_{op}_bf16", "allreduce", "bfloat16", base, op=op))
+        rc = base // n - (base // n) % 8
+        cases.append(Case(f"reducescatter_{op}", "reducescatter", "float32", rc, op=op))
+    cases.append(Case("allreduce_avg_int32", "allreduce", "int32", base, op="avg"))
     return cases
+
+
+def pipeline_cases(n: int, env: dict, sms: int) -> list[Case]:
+    """-1/0/+1 vector (32 bytes of fp32) around the edges of the engines'
+    pipelines: the NVLS round (AllReduce message; per-slot part of a round
+    for ReduceScatter/AllGather), the push-reduce round of 256 KiB pieces per
+    block (per segment), the push chain's step (chunk x blocks) and the
+    host-lane piece. Each case runs on whatever route the environment picks;
+    force routes to aim them."""
+    out = []
+    R = int(policy_value(env, "nvls_round"))
+    part = (R // n) & ~31
+    step = int(policy_value(env, "ring_chunk")) * sms
+    push_round = 262144 * sms
+    piece = int(policy_value(env, "host_piece"))
+
+    def add(name, kind, nbytes):
+        for d in (-8, 0, 8):  # fp32 elements: one 32-byte vector
+            c = nbytes // 4 + d
+            if kind == "reducescatter":
+                c -= c % 4
+            if c > 0:
+                out.append(Case(f"edge_{name}_{d:+d}", kind, "float32", c))
+    add("nvls_round_ar", "allreduce", R)
+    add("nvls_round2_ar", "allreduce", 2 * R)
+    add("nvls_part_rs", "reducescatter", part)
+    add("nvls_part_ag", "allgather", part)
+    add("ring_step_bc", "broadcast", step)
+    add("ring_step2_bc", "broadcast", 2 * step)
+    add("push_round_ar", "allreduce", push_round * n)
+    add("push_round_rs", "reducescatter", push_round)
+    add("host_piece_ar", "allreduce", piece * n)
+    add("host_piece_rs", "reducescatter", piece)
+    return out
+
+
+def big_cases(n: int) -> list[Case]:
+    """The 2 GiB and 4 GiB logical-size edges (-1/0/+1 element), and the
+    8 GiB message cap: at the cap (custom) and one element above it (must
+    fall back to NCCL)."""
+    G = 1 << 30
+    out = []
+    for size, tag in ((2 * G, "2g"), (4 * G, "4g")):
+        for d in (-1, 0, 1):
+            out.append(Case(f"big_{tag}_allreduce_{d:+d}", "allreduce", "float32", size // 4 + d))
+        rc = size // 4 // n
+        out.append(Case(f"big_{tag}_reducescatter", "reducescatter", "float32", rc - rc % 4))
+        out.append(Case(f"big_{tag}_allgather_+1", "allgather", "float32", size // 4 // n + 1))
+    out.append(Case("cap_allreduce_at", "allreduce", "float32", 8 * G // 4))
+    out.append(Case("cap_allreduce_above", "allreduce", "float32", 8 * G // 4 + 1))
+    out.append(Case("cap_broadcast_at", "broadcast", "float32", 8 * G // 4, root=n - 1))
+    out.append(Case("cap_broadcast_above", "broadcast", "float32", 8 * G // 4 + 1))
+    return out
 
 
 def boundary_cases(n: int, thresholds: dict) -> list[Case]:
@@ -131,6 +209,21 @@ def custom_total(nc: Nccl) -> int:
     return sum(nc.custom_calls(a) or 0 for a in range(1, len(ALGO)))
 
 
+def route_counts(nc: Nccl) -> dict:
+    return {a: nc.custom_calls(a) or 0 for a in range(1, len(ALGO))}
+
+
+ALGO_NAME = {v: k for k, v in ALGO.items()}
+
+
+def fill_exact(t: torch.Tensor, rank: int, it: int, seed: int, n: int):
+    """exact(...) written into `t` chunk by chunk (large buffers)."""
+    total = t.numel()
+    for lo in range(0, total, CHUNK):
+        hi = min(total, lo + CHUNK)
+        t[lo:hi].copy_(exact(rank, hi - lo, it, seed, t.dtype, n, t.device, offset=lo))
+
+
 def thresholds() -> dict:
     """Per-kind routing thresholds (bytes) as the library's policy parser
     reads them from this process's environment."""
@@ -139,9 +232,71 @@ def thresholds() -> dict:
             for kind, key in (("allreduce", "ar"), ("allgather", "ag"), ("broadcast", "bc"))}
 
 
+def fold_ref(vals: list, op: str, dtype, n: int, scalar: float) -> torch.Tensor:
+    """The library's fold of `vals` (rank order), restated with torch: fp32
+    accumulation for floating types (exact data make a float64 sum equal),
+    the integer type's own width otherwise."""
+    if op == "sum":
+        if dtype.is_floating_point:
+            acc = vals[0].to(torch.float64)
+            for x in vals[1:]:
+                acc = acc + x.to(torch.float64)
+        else:
+            acc = vals[0].to(torch.int64)
+            for x in vals[1:]:
+                acc = acc + x.to(torch.int64)
+        return acc.to(dtype)
+    if not dtype.is_floating_point:
+        acc = vals[0].to(torch.int64)
+        for x in vals[1:]:
+            acc = {"max": torch.maximum, "min": torch.minimum}.get(op, torch.add)(acc, x.to(torch.int64))
+        if op == "avg":
+            acc = torch.div(acc, n, rounding_mode="trunc")
+        return acc.to(dtype)
+    acc = vals[0].float() * scalar if op == "premulsum" else vals[0].float()
+    for x in vals[1:]:
+        xf = x.float()
+        if op == "prod":
+            acc = acc * xf
+        elif op == "max":
+            acc = torch.maximum(acc, xf)
+        elif op == "min":
+            acc = torch.minimum(acc, xf)
+        elif op == "premulsum":
+            acc = acc + xf * scalar  # exact data and a power-of-two scalar: no rounding
+        else:
+            acc = acc + xf
+    if op == "avg":  # a true division, as the kernels do
+        acc = torch.div(acc, torch.full_like(acc, float(n)))
+    return acc.to(dtype)
+
+
+PREMUL_SCALAR = 0.5  # exact in every floating type
+
+
+def want_chunk(case: Case, r: int, n: int, it: int, seed: int, dtype, device, lo: int, hi: int):
+    """Expected output elements [lo, hi) of rank r, regenerated from the
+    hashed inputs (no copies of the inputs are kept)."""
+    c = case.count
+    gen = lambda q, off, m: exact(q, m, it, seed, dtype, n, device, offset=off)  # noqa: E731
+    if case.kind == "allreduce":
+        return fold_ref([gen(q, lo, hi - lo) for q in range(n)], case.op, dtype, n, PREMUL_SCALAR)
+    if case.kind == "reducescatter":
+        return fold_ref([gen(q, r * c + lo, hi - lo) for q in range(n)], case.op, dtype, n, PREMUL_SCALAR)
+    if case.kind == "broadcast":
+        return gen(case.root, lo, hi - lo)
+    parts, i = [], lo  # allgather: slot q of the output is rank q's input
+    while i < hi:
+        q, off = divmod(i, c)
+        m = min(hi - i, c - off)
+        parts.append(gen(q, off, m))
+        i += m
+    return torch.cat(parts)
+
+
 def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, seed: int,
              diff: bool, corrupt_shift: int, delay_device: int = -1, delay_ms: float = 0.0,
-             overwrite_after: bool = False, fresh_streams: bool = False) -> dict:
+             overwrite_after: bool = False, fresh_streams: bool = False, expect: str = "") -> dict:
     n = len(devs)
     dtype = DTYPES[case.dtype]
     es = torch.tensor([], dtype=dtype).element_size()
@@ -167,8 +322,11 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
             return sv, sv[r * c:(r + 1) * c]
         return b.send(), b.send()
 
+    ops = case.op
+    if case.op == "premulsum":
+        ops = [nc.premul_sum(PREMUL_SCALAR, case.dtype, comm) for comm in comms]
     mism = [torch.zeros((), dtype=torch.int64, device=f"cuda:{d}") for d in devs]
-    custom_before = custom_total(nc)
+    before = route_counts(nc)
     shadows = None
     if diff and ref is not None:
         shadows = [torch.empty(recv_elems, dtype=dtype, device=f"cuda:{d}") for d in devs]
@@ -186,24 +344,22 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
         for r, d in enumerate(devs):
             s, v = views(r)
             with torch.cuda.device(d):
-                if diff:
-                    s.copy_(adversarial(r, s.numel(), seed + it, dtype, f"cuda:{d}", nans=not reduces)
-                            if dtype.is_floating_point else exact(r, s.numel(), it, seed, dtype, n, f"cuda:{d}"))
+                if diff and dtype.is_floating_point:
+                    s.copy_(adversarial(r, s.numel(), seed + it, dtype, f"cuda:{d}", nans=not reduces))
                 else:
-                    s.copy_(exact(r, s.numel(), it, seed, dtype, n, f"cuda:{d}"))
+                    fill_exact(s, r, it, seed, n)
             sends.append(s)
             recvs.append(v)
-        inputs = [s.clone() for s in sends] if (diff or case.inplace or overwrite) else sends
         if shadows is not None:
             # Stock NCCL first, into shadow buffers, through the real library.
-            shadow_sends = [x.clone() for x in inputs]
+            shadow_sends = [x.clone() for x in sends]
             collective(ref, case.kind, shadow_sends, shadows, comms, streams, op=case.op, root=case.root)
         if 0 <= delay_device < len(devs):
             # Hold one GPU's caller stream before the call: every other rank
             # must wait for its input, not read it early.
             with torch.cuda.device(devs[delay_device]):
                 torch.cuda._sleep(int(delay_ms * 1.9e6))
-        collective(nc, case.kind, sends, recvs, comms, streams, op=case.op, root=case.root)
+        collective(nc, case.kind, sends, recvs, comms, streams, op=ops, root=case.root)
         if overwrite:
             # Stream-ordered reuse of the inputs right after the call: safe
             # only if the call's side streams joined the caller streams.
@@ -225,9 +381,11 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
                     else:
                         mism[r] += (got.view(torch.uint8) != want.view(torch.uint8)).sum()
                 else:
-                    want = expected(case, r, n, it, seed, dtype, f"cuda:{d}", [x.to(f"cuda:{d}") for x in inputs]
-                                    if case.kind in ("allgather", "broadcast") or case.op != "sum" else None)
-                    mism[r] += (got.view(torch.uint8) != want.view(torch.uint8)).sum()
+                    total = got.numel()
+                    for lo in range(0, total, CHUNK):
+                        hi = min(total, lo + CHUNK)
+                        want = want_chunk(case, r, n, it, seed, dtype, f"cuda:{d}", lo, hi)
+                        mism[r] += (got[lo:hi].view(torch.uint8) != want.view(torch.uint8)).sum()
         if fresh_streams:
             for i, d in enumerate(devs):
                 home[i].wait_stream(torch.cuda.current_stream(d))
@@ -235,37 +393,37 @@ def run_case(nc: Nccl, ref: Nccl | None, comms, devs, case: Case, iters: int, se
             streams = [h.cuda_stream for h in home]
     for d in devs:
         torch.cuda.synchronize(d)
+    if case.op == "premulsum":
+        for o, comm in zip(ops, comms):
+            nc.redop_destroy(o, comm)
     total = int(sum(m.item() for m in mism))
     guard = int(sum(b.guard_bad().item() for b in bufs))
-    custom = custom_total(nc) > custom_before
+    after = route_counts(nc)
+    ran = sorted(ALGO_NAME[a] for a in after if after[a] > before.get(a, 0))
+    route = ",".join(ran) if ran else "nccl"
+    status = "PASS" if total == 0 and guard == 0 else "FAIL"
+    if status == "PASS" and expect and not route_matches(route, expect):
+        status = "ROUTE"
     return {"case": case.name, "iters": iters, "bytes": c * es, "mismatches": total,
-            "status": "PASS" if total == 0 and guard == 0 else "FAIL", "guard_bad": guard,
-            "route": "custom" if custom else "nccl", "kind": case.kind,
-            "mode": "diff" if diff else "check"}
+            "status": status, "guard_bad": guard, "route": route, "expect": expect or "-",
+            "kind": case.kind, "mode": "diff" if diff else "check"}
 
 
-def expected(case: Case, r: int, n: int, it: int, seed: int, dtype, device, inputs):
-    c = case.count
-    if case.kind == "allreduce":
-        if case.op != "sum":
-            acc = inputs[0].float()
-            for x in inputs[1:]:
-                acc = torch.maximum(acc, x.float()) if case.op == "max" else acc + x.float()
-            return acc.to(dtype)
-        acc = None
-        for q in range(n):
-            x = exact(q, c, it, seed, dtype, n, device).to(torch.float64)
-            acc = x if acc is None else acc + x
-        return acc.to(dtype)
-    if case.kind == "reducescatter":
-        acc = None
-        for q in range(n):
-            x = exact(q, c, it, seed, dtype, n, device, offset=r * c).to(torch.float64)
-            acc = x if acc is None else acc + x
-        return acc.to(dtype)
-    if case.kind == "allgather":
-        return torch.cat(inputs)
-    return inputs[case.root]
+def route_matches(route: str, expect: str) -> bool:
+    if expect == "custom":
+        return route != "nccl"
+    return route == expect
+
+
+def oracle_route(case: Case, n: int, nvls: bool, calib: dict | None, tuned: bool,
+                 rules: oracle.Rules | None = None) -> str:
+    """The independent oracle's route for a case ("custom" when tuned routes
+    are in force but no calibration record is available to restate them)."""
+    r = oracle.expected_route(case.kind, case.dtype, case.op, case.count, n, inplace=case.inplace,
+                              nvls=nvls, rules=rules or oracle.Rules(), calib=calib)
+    if tuned and calib is None and r != "nccl":
+        return "custom"
+    return r
 
 
 def main(argv=None) -> int:
@@ -278,6 +436,12 @@ def main(argv=None) -> int:
     p.add_argument("--corrupt-shift", type=int, default=0)
     p.add_argument("--filter", default="")
     p.add_argument("--no-boundary", action="store_true")
+    p.add_argument("--no-standard", action="store_true")
+    p.add_argument("--edges", action="store_true", help="the engines' pipeline edges")
+    p.add_argument("--big", action="store_true", help="2/4 GiB edges and the 8 GiB message cap")
+    p.add_argument("--no-oracle", action="store_true", help="do not check routes against the oracle")
+    p.add_argument("--oracle-drop", default="",
+                   help="hide this variable from the oracle (mutation self-test of the route check)")
     p.add_argument("--delay-input-device", type=int, default=-1,
                    help="hold this rank's caller stream before every call")
     p.add_argument("--delay-ms", type=float, default=20.0)
@@ -290,24 +454,38 @@ def main(argv=None) -> int:
     if a.algo:
         os.environ["NCCL_B200_ALGO"] = a.algo
     devs = list(range(a.gpus))
+    n = len(devs)
     nc = Nccl("interposer")
     ref = Nccl("nccl") if a.diff else None
     comms = nc.comm_init_all(devs)
-    cases = standard_cases(len(devs), a.scale)
+    env = {k: v for k, v in os.environ.items() if k.startswith("NCCL_B200_")}
+    cases = [] if a.no_standard else standard_cases(n, a.scale)
     if not a.no_boundary:
-        cases += boundary_cases(len(devs), thresholds())
+        cases += boundary_cases(n, thresholds())
+    if a.edges:
+        cases += pipeline_cases(n, env, torch.cuda.get_device_properties(0).multi_processor_count)
+    if a.big:
+        cases += big_cases(n)
     if a.filter:
         cases = [c for c in cases if a.filter in c.name]
+    import ctypes as C
+    arr = (C.c_int * n)(*devs)
+    nvls = bool(nc.shim.nb_nvls_supported(arr, n)) and oracle.Rules().nvls != "off"
+    tuned = oracle.parse_bool(os.environ.get("NCCL_B200_TUNE")) is not False and n > 1
+    calib = oracle.load_calib(os.environ.get("NCCL_B200_CALIB_CACHE"))
+    rules = oracle.Rules({k: v for k, v in os.environ.items() if k != a.oracle_drop})
     # Warm-up: the first eligible call of the process always runs on NCCL.
     run_case(nc, None, comms, devs, Case("warmup", "allreduce", "float32", (64 << 20) // 4), 1, 0, False, 0)
-    print("case\titers\tbytes\tmismatches\tstatus\tguard_bad\troute\tkind\tmode", flush=True)
+    print("case\titers\tbytes\tmismatches\tstatus\tguard_bad\troute\texpect\tkind\tmode", flush=True)
     bad = 0
     for case in cases:
+        expect = "" if a.no_oracle or a.diff else oracle_route(case, n, nvls, calib, tuned, rules)
         res = run_case(nc, ref, comms, devs, case, a.iters, a.seed, a.diff, a.corrupt_shift,
-                       a.delay_input_device, a.delay_ms, a.overwrite_after, a.fresh_streams)
+                       a.delay_input_device, a.delay_ms, a.overwrite_after, a.fresh_streams, expect)
         bad += res["status"] != "PASS"
         print("\t".join(str(res[k]) for k in ("case", "iters", "bytes", "mismatches", "status",
-                                                "guard_bad", "route", "kind", "mode")), flush=True)
+                                                "guard_bad", "route", "expect", "kind", "mode")), flush=True)
+        torch.cuda.empty_cache()
     sys.stderr.write(nc.summary_text())
     for c in comms:
         nc.comm_destroy(c)

@@ -17,6 +17,7 @@
 #include <nvtx3/nvToolsExt.h>
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <cstddef>
 #include <cstdio>
 #include <cstdlib>
@@ -129,9 +130,19 @@ Shares shares_for(Algo a, int n, const CallDesc& c) {
   Shares s = n >= 1 && n <= kMaxRanks && r.calib[n].valid
                  ? shares_from(r.calib[n], a, n, small_message(r.calib[n], logical_bytes(c)))
                  : Shares{};
+  // The tiny band's routes move every byte on the SMs.
+  if (n >= 2 && n <= kMaxRanks && r.calib[n].valid && tiny_message(r.calib[n], logical_bytes(c))) s = Shares{};
   if (r.policy.host_share_ppm >= 0) s.host_ppm = r.policy.host_share_ppm;
   if (r.policy.ce_share_ppm >= 0) s.ce_ppm = r.policy.ce_share_ppm;
-  if (n <= 1 || a == Algo::ArNvls) s.host_ppm = s.ce_ppm = 0;
+  if (n <= 1) {
+    // One rank: the local copy's copy-engine share (policy, else tuned).
+    s = Shares{};
+    const int k = int(c.kind);
+    s.ce_ppm = r.policy.ce_share_ppm >= 0 ? r.policy.ce_share_ppm
+                                          : (r.calib[1].valid ? std::max(0, r.calib[1].ce_ppm[k]) : 0);
+    return s;
+  }
+  if (a == Algo::ArNvls) s.host_ppm = s.ce_ppm = 0;
   // Device-resident PreMulSum scalars cannot be applied by the host fold.
   if (c.op == RedOp::PreMulSum && c.scalar_residence == 0) s.host_ppm = 0;
   if (a == Algo::RsPull || a == Algo::RsStaged || a == Algo::ArStaged) s.ce_ppm = 0;
@@ -146,6 +157,18 @@ void prewarm(const int* devices, int n) {
     cudaGetLastError();
     if (r.summary.enabled()) r.summary.note("prewarm_failed " + why);
     return;
+  }
+  if (n == 1 && r.policy.tune && !r.calib_tried[1]) {
+    r.calib_tried[1] = true;
+    CalibResult c;
+    tune_single(devices[0], r.policy.tune_bytes, &c);
+    r.calib[1] = c;
+    if (c.valid) {
+      char line[160];
+      std::snprintf(line, sizeof line, "routes n=1 local copy: sm stream copy%s (ce_ppm=%d, %.1f GB/s)",
+                    c.ce_ppm[0] > 0 ? " + copy engine" : " alone", c.ce_ppm[0], c.route_gbs[0]);
+      r.summary.note(line);
+    }
   }
   if (r.policy.calibrate && n > 1 && !r.calib_tried[n]) {
     r.calib_tried[n] = true;
@@ -171,6 +194,13 @@ void prewarm(const int* devices, int n) {
                       "reducescatter=%s broadcast=%s", n, c.small_below_mib,
                       algo_name(Algo(c.small_pref[0])), algo_name(Algo(c.small_pref[1])),
                       algo_name(Algo(c.small_pref[2])), algo_name(Algo(c.small_pref[3])));
+        r.summary.note(line);
+      }
+      if (c.tiny_below_kib > 0) {
+        std::snprintf(line, sizeof line, "routes n=%d below %d KiB: allreduce=%s allgather=%s "
+                      "reducescatter=%s broadcast=%s", n, c.tiny_below_kib,
+                      algo_name(Algo(c.tiny_pref[0])), algo_name(Algo(c.tiny_pref[1])),
+                      algo_name(Algo(c.tiny_pref[2])), algo_name(Algo(c.tiny_pref[3])));
         r.summary.note(line);
       }
     }
@@ -358,7 +388,7 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
     return Outcome::Error;
   }
   if (status == ExecStatus::Ok) {
-    r.summary.count_custom(d.algo, logical_bytes(descs[0]), n, plan.sm_bytes, plan.ce_bytes,
+    r.summary.count_custom(plan.algo, logical_bytes(descs[0]), n, plan.sm_bytes, plan.ce_bytes,
                            plan.host_bytes);
     return Outcome::Handled;
   }

@@ -57,6 +57,10 @@ struct Runtime {
 // Time every candidate route on the clique's GPUs at `bytes` and record the
 // fastest per collective kind (abi/tune.cc).
 void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out);
+// One-rank cliques: time the local copy (the SM stream copy kernel alone and
+// beside copy-engine shares) at `bytes` and keep the fastest copy-engine
+// share for every kind (abi/tune.cc).
+void tune_single(int device, size_t bytes, CalibResult* out);
 
 Runtime& rt();
 // Resolve the real libnccl once (dlsym RTLD_NEXT, then the loaded

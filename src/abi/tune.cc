@@ -26,10 +26,52 @@ struct Candidate {
   int host_ppm;
   int piece_mib;  // staged routes
   int depth;
+  int split_ppm = 0;     // hybrid routes: the switch's share (per 10000)
+  int split_blocks = 0;  // and its blocks per GPU
 };
+
+// Hybrid splits tried per kind. AllReduce: the NVLS AllReduce is limited by
+// the switch below the link rate, so a P2P two-shot share on the remaining
+// SMs can use the links' spare capacity. ReduceScatter: NVLS reads every
+// byte of a GPU once more than the P2P pulls do, so its share is smaller.
+constexpr int kArSplits[][2] = {{6000, 74}, {7000, 96}, {7800, 110}, {8500, 120}};
+constexpr int kRsSplits[][2] = {{2500, 48}, {4000, 74}, {5500, 96}};
 
 // Every candidate route of a kind; a host-lane variant is added wherever the
 // rate model (measured PCIe, NVLink and fold rates) predicts a host share.
+std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& rates);
+
+// Small messages: the routes whose every byte moves on the SMs, with no
+// pipeline to start (one-shot and two-shot folds, pulls, pushes, NVLS).
+std::vector<Candidate> tiny_candidates(Kind k, int n, bool nvls) {
+  std::vector<Candidate> v;
+  auto add = [&](Algo a) { v.push_back({a, 0, 0, 0, 0}); };
+  switch (k) {
+    case Kind::AllReduce:
+      add(Algo::ArOneShot);
+      add(Algo::ArTwoShot);
+      if (nvls) add(Algo::ArNvls);
+      break;
+    case Kind::ReduceScatter:
+      add(Algo::RsPull);
+      if (nvls) add(Algo::RsNvls);
+      break;
+    case Kind::AllGather:
+      add(Algo::AgPull);
+      add(Algo::AgPush);
+      if (nvls) add(Algo::AgNvls);
+      break;
+    case Kind::Broadcast:
+      add(n >= 3 ? Algo::BcScatter : Algo::BcPull);
+      add(Algo::BcRing);
+      if (nvls) add(Algo::BcNvls);
+      break;
+    default:
+      break;
+  }
+  return v;
+}
+
 std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& rates) {
   std::vector<Candidate> v;
   auto add = [&](Algo a, int ce, int piece = 0, int depth = 0) {
@@ -50,10 +92,14 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
         add(Algo::ArStaged, 0, 256, 2);
       }
       if (nvls && n >= 2) v.push_back({Algo::ArNvls, 0, 0, 0, 0});
+      if (nvls && n >= 4)
+        for (const auto& sp : kArSplits) v.push_back({Algo::ArHybrid, 0, 0, 0, 0, sp[0], sp[1]});
       v.push_back({Algo::ArPush, 0, 0, 0, 0});
       break;
     case Kind::ReduceScatter:
       if (nvls && n >= 2) v.push_back({Algo::RsNvls, 0, 0, 0, 0});
+      if (nvls && n >= 4)
+        for (const auto& sp : kRsSplits) v.push_back({Algo::RsHybrid, 0, 0, 0, 0, sp[0], sp[1]});
       add(Algo::RsPull, 0);
       v.push_back({Algo::RsPush, 0, 0, 0, 0});
       if (small) {
@@ -115,11 +161,13 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
   const bool nvls = r.policy.nvls != NvlsMode::Off && nvls_supported(devices, n);
   // Two tuning sizes: the large one (the policy's) and a small one; the
   // small choice serves messages below their geometric mean.
+  // A third, tiny size picks among the SM routes for small messages.
   const size_t unit = size_t(n) * 256;
   const size_t small_bytes = std::max(unit, (size_t(64) << 20) / unit * unit);
+  const size_t tiny_bytes = std::max(unit, (size_t(4) << 20) / unit * unit);
   const bool two_sizes = bytes >= 4 * small_bytes;
-  for (int pass = 0; pass < (two_sizes ? 2 : 1); ++pass) {
-    const size_t size = pass == 0 ? bytes : small_bytes;
+  for (int pass = 0; pass < (two_sizes ? 3 : 1); ++pass) {
+    const size_t size = pass == 0 ? bytes : pass == 1 ? small_bytes : tiny_bytes;
     for (int kk = 0; ok && kk < int(Kind::Count); ++kk) {
       const Kind kind = Kind(kk);
       CliqueDesc d;
@@ -143,12 +191,14 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
       }
       double best_ms = 1e30, best_real_ms = 1e30;
       Candidate best{Algo::Fallback, -1, -1, 0, 0};
-      for (const Candidate& c : candidates(kind, n, nvls, *out)) {
+      for (const Candidate& c : pass == 2 ? tiny_candidates(kind, n, nvls) : candidates(kind, n, nvls, *out)) {
         Shares s;
         s.ce_ppm = c.ce_ppm;
         s.host_ppm = c.host_ppm;
         s.stage_piece = size_t(c.piece_mib) << 20;
         s.stage_depth = c.depth;
+        s.split_ppm = c.split_ppm;
+        s.split_blocks = c.split_blocks;
         Plan plan;
         build_plan(c.algo, d, r.policy, s, plan);
         std::string why;
@@ -187,12 +237,13 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
           r.exec.drain(devices, n);
           continue;
         }
-        char line[160];
+        char line[240];
         const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? size : d.bytes;
         std::snprintf(line, sizeof line,
-                      "tune %s n=%d bytes=%zu %s ce_ppm=%d host_ppm=%d piece_mib=%d depth=%d busbw_gbs=%.1f",
+                      "tune %s n=%d bytes=%zu %s ce_ppm=%d host_ppm=%d piece_mib=%d depth=%d split=%d/%d "
+                      "busbw_gbs=%.1f",
                       kind_name(kind), n, logical, algo_name(c.algo), c.ce_ppm, c.host_ppm, c.piece_mib,
-                      c.depth, logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
+                      c.depth, c.split_ppm, c.split_blocks, logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
         r.summary.note(line);
         // An event-ordered chain pays a cross-GPU event wait per piece and hop,
         // so its rate drops as messages outgrow the tuning size (measured at 4
@@ -205,18 +256,24 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
           best = c;
         }
       }
-      if (best.algo != Algo::Fallback && pass == 1) {
+      if (best.algo != Algo::Fallback && pass == 2) {
+        out->tiny_pref[kk] = int(best.algo);
+      } else if (best.algo != Algo::Fallback && pass == 1) {
         out->small_pref[kk] = int(best.algo);
         out->small_ce_ppm[kk] = best.ce_ppm;
         out->small_host_ppm[kk] = best.host_ppm;
         out->small_piece_mib[kk] = best.piece_mib;
         out->small_depth[kk] = best.depth;
+        out->small_split_ppm[kk] = best.split_ppm;
+        out->small_split_blocks[kk] = best.split_blocks;
       } else if (best.algo != Algo::Fallback) {
         out->preferred[kk] = int(best.algo);
         out->ce_ppm[kk] = best.ce_ppm;
         out->host_ppm[kk] = best.host_ppm;
         out->stage_piece_mib[kk] = best.piece_mib;
         out->stage_depth[kk] = best.depth;
+        out->split_ppm[kk] = best.split_ppm;
+        out->split_blocks[kk] = best.split_blocks;
         const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? size : d.bytes;
         out->route_gbs[kk] = logical / (best_real_ms * 1e-3) / 1e9 * busbw_factor(kind, n);
       }
@@ -225,6 +282,7 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
   if (two_sizes) {
     const double mean = std::sqrt(double(small_bytes) * double(bytes));
     out->small_below_mib = int(mean / double(1 << 20));
+    out->tiny_below_kib = int(std::sqrt(double(tiny_bytes) * double(small_bytes)) / 1024.0);
   }
   for (int i = 0; i < n; ++i) {
     cudaSetDevice(devices[i]);
@@ -235,6 +293,94 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
     if (e0[size_t(i)]) cudaEventDestroy(e0[size_t(i)]);
     if (e1[size_t(i)]) cudaEventDestroy(e1[size_t(i)]);
   }
+  cudaGetLastError();
+}
+
+void tune_single(int device, size_t bytes, CalibResult* out) {
+  Runtime& r = rt();
+  bytes = bytes / 256 * 256;
+  if (!bytes) return;
+  void* send = nullptr;
+  void* recv = nullptr;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  bool ok = cudaSetDevice(device) == cudaSuccess && cudaMalloc(&send, bytes) == cudaSuccess &&
+            cudaMalloc(&recv, bytes) == cudaSuccess && cudaMemset(send, 0, bytes) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
+  const int devices[1] = {device};
+  CliqueDesc d;
+  d.kind = Kind::AllReduce;
+  d.dtype = DType::F32;
+  d.op = RedOp::Sum;
+  d.nranks = 1;
+  d.bytes = bytes;
+  d.count = bytes / 4;
+  Binding b;
+  b.nranks = 1;
+  b.device[0] = device;
+  b.stream[0] = stream;
+  b.send[0] = send;
+  b.recv[0] = recv;
+  b.fold.dtype = DType::F32;
+  b.fold.nranks = 1;
+  double best_ms = 1e30;
+  int best_ce = -1;
+  // The kernel alone, and beside copy-engine shares of the leading bytes.
+  for (int ce : {0, 1500, 2500, 3500}) {
+    if (!ok) break;
+    Shares s;
+    s.ce_ppm = ce;
+    Plan plan;
+    build_plan(Algo::ArTwoShot, d, r.policy, s, plan);
+    std::string why;
+    if (!r.exec.ensure(plan.needs, devices, 1, &why)) {
+      cudaGetLastError();
+      continue;
+    }
+    bool good = true;
+    float ms = 0;
+    for (int rep = 0; rep < 2 && good; ++rep) {  // rep 0 warms up
+      const int runs = rep ? 5 : 2;
+      good = cudaEventRecord(e0, stream) == cudaSuccess;
+      for (int k = 0; k < runs && good; ++k) {
+        cudaError_t err = cudaSuccess;
+        good = r.exec.execute(plan, b, &err, nullptr) == ExecStatus::Ok;
+      }
+      good = good && cudaEventRecord(e1, stream) == cudaSuccess && cudaEventSynchronize(e1) == cudaSuccess &&
+             cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess;
+      ms /= float(runs);
+    }
+    if (!good) {
+      cudaGetLastError();
+      r.exec.drain(devices, 1);
+      continue;
+    }
+    char line[128];
+    std::snprintf(line, sizeof line, "tune local-copy n=1 bytes=%zu ce_ppm=%d algbw_gbs=%.1f", bytes, ce,
+                  bytes / (ms * 1e-3) / 1e9);
+    r.summary.note(line);
+    if (ms < best_ms) {
+      best_ms = ms;
+      best_ce = ce;
+    }
+  }
+  if (best_ce >= 0) {
+    out->valid = true;
+    for (int k = 0; k < 4; ++k) {
+      out->preferred[k] = int(Algo::ArTwoShot);  // unused at one rank (every kind is the copy)
+      out->ce_ppm[k] = best_ce;
+      out->host_ppm[k] = 0;
+      out->route_gbs[k] = bytes / (best_ms * 1e-3) / 1e9;
+    }
+  }
+  cudaSetDevice(device);
+  cudaDeviceSynchronize();
+  if (send) cudaFree(send);
+  if (recv) cudaFree(recv);
+  if (stream) cudaStreamDestroy(stream);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
   cudaGetLastError();
 }
 

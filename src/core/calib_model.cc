@@ -11,8 +11,13 @@ bool small_message(const CalibResult& c, size_t logical) {
   return c.small_below_mib > 0 && logical < (size_t(c.small_below_mib) << 20);
 }
 
+bool tiny_message(const CalibResult& c, size_t logical) {
+  return c.tiny_below_kib > 0 && logical < (size_t(c.tiny_below_kib) << 10);
+}
+
 Algo tuned_route(const CalibResult& c, int kind, size_t logical) {
   if (kind < 0 || kind >= 4) return Algo::Fallback;
+  if (tiny_message(c, logical) && c.tiny_pref[kind] != 0) return Algo(c.tiny_pref[kind]);
   if (small_message(c, logical) && c.small_pref[kind] != 0) return Algo(c.small_pref[kind]);
   return Algo(c.preferred[kind]);
 }
@@ -62,6 +67,8 @@ Shares shares_from(const CalibResult& c, Algo a, int n, bool small) {
       if (c.small_host_ppm[k] >= 0) s.host_ppm = c.small_host_ppm[k];
       if (c.small_piece_mib[k] > 0) s.stage_piece = size_t(c.small_piece_mib[k]) << 20;
       if (c.small_depth[k] > 0) s.stage_depth = c.small_depth[k];
+      if (c.small_split_ppm[k] > 0) s.split_ppm = c.small_split_ppm[k];
+      if (c.small_split_blocks[k] > 0) s.split_blocks = c.small_split_blocks[k];
       continue;
     }
     if (c.preferred[k] != int(a)) continue;
@@ -69,6 +76,8 @@ Shares shares_from(const CalibResult& c, Algo a, int n, bool small) {
     if (c.host_ppm[k] >= 0) s.host_ppm = c.host_ppm[k];
     if (c.stage_piece_mib[k] > 0) s.stage_piece = size_t(c.stage_piece_mib[k]) << 20;
     if (c.stage_depth[k] > 0) s.stage_depth = c.stage_depth[k];
+    if (c.split_ppm[k] > 0) s.split_ppm = c.split_ppm[k];
+    if (c.split_blocks[k] > 0) s.split_blocks = c.split_blocks[k];
   }
   return s;
 }
@@ -94,8 +103,17 @@ std::string calib_to_json(const CalibResult& c, const std::string& key) {
                   c.small_piece_mib[k], k, c.small_depth[k]);
     s += buf;
   }
-  std::snprintf(buf, sizeof buf, ", \"small_below_mib\": %d", c.small_below_mib);
+  std::snprintf(buf, sizeof buf, ", \"small_below_mib\": %d, \"tiny_below_kib\": %d", c.small_below_mib,
+                c.tiny_below_kib);
   s += buf;
+  for (int k = 0; k < 4; ++k) {
+    std::snprintf(buf, sizeof buf,
+                  ", \"tpref%d\": %d, \"split%d\": %d, \"sblocks%d\": %d, \"ssplit%d\": %d, "
+                  "\"ssblocks%d\": %d",
+                  k, c.tiny_pref[k], k, c.split_ppm[k], k, c.split_blocks[k], k, c.small_split_ppm[k], k,
+                  c.small_split_blocks[k]);
+    s += buf;
+  }
   return s + "}\n";
 }
 
@@ -140,6 +158,15 @@ bool calib_from_json(const std::string& text, const std::string& key, CalibResul
   {
     double v = 0;
     if (json_number(text, "small_below_mib", &v)) c.small_below_mib = int(v);
+    if (json_number(text, "tiny_below_kib", &v)) c.tiny_below_kib = int(v);
+    for (int k = 0; k < 4; ++k) {
+      const std::string K = std::to_string(k);
+      if (json_number(text, ("tpref" + K).c_str(), &v)) c.tiny_pref[k] = int(v);
+      if (json_number(text, ("split" + K).c_str(), &v)) c.split_ppm[k] = int(v);
+      if (json_number(text, ("sblocks" + K).c_str(), &v)) c.split_blocks[k] = int(v);
+      if (json_number(text, ("ssplit" + K).c_str(), &v)) c.small_split_ppm[k] = int(v);
+      if (json_number(text, ("ssblocks" + K).c_str(), &v)) c.small_split_blocks[k] = int(v);
+    }
   }
   c.valid = true;
   *out = c;

@@ -36,6 +36,8 @@ struct CalibResult {
   int stage_piece_mib[4] = {0, 0, 0, 0};
   int stage_depth[4] = {0, 0, 0, 0};
   double route_gbs[4] = {0, 0, 0, 0};  // busbw of the chosen route at the tuning size
+  int split_ppm[4] = {0, 0, 0, 0};     // hybrid routes: the switch's share and blocks
+  int split_blocks[4] = {0, 0, 0, 0};
   // The same, tuned at a small size: used for messages below small_below_mib
   // (0 = no small-size choice). Pipelined routes pay a start-up that only
   // large messages amortize, so the best route differs with size.
@@ -44,11 +46,19 @@ struct CalibResult {
   int small_host_ppm[4] = {-1, -1, -1, -1};
   int small_piece_mib[4] = {0, 0, 0, 0};
   int small_depth[4] = {0, 0, 0, 0};
+  int small_split_ppm[4] = {0, 0, 0, 0};
+  int small_split_blocks[4] = {0, 0, 0, 0};
   int small_below_mib = 0;
+  // A third band for small messages, tuned among the SM routes only (no
+  // pipelines, no copy-engine or host shares): used below tiny_below_kib.
+  int tiny_pref[4] = {0, 0, 0, 0};
+  int tiny_below_kib = 0;
 };
 
 // Whether a message of `logical` bytes takes the small-size choice.
 bool small_message(const CalibResult& c, size_t logical);
+// Whether it takes the tiny-size choice (a route of the small band's own).
+bool tiny_message(const CalibResult& c, size_t logical);
 // The tuned route of `kind` for a message of `logical` bytes (Fallback when
 // untuned).
 Algo tuned_route(const CalibResult& c, int kind, size_t logical);

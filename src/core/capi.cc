@@ -9,6 +9,7 @@
 #include <string>
 #include <vector>
 
+#include "core/bufclass.h"
 #include "core/calib_model.h"
 #include "core/clique.h"
 #include "core/exec_loop.h"
@@ -337,6 +338,7 @@ double nb_policy_value(const char* env, const char* field) {
   const Policy p = EnvMap(env).policy();
   const std::string f(field);
   if (f == "enabled") return p.enabled;
+  if (f == "local_copy_tma") return p.local_copy_tma ? 1 : 0;
   if (f == "ar_min") return double(p.min_bytes[0]);
   if (f == "ag_min") return double(p.min_bytes[1]);
   if (f == "rs_min") return double(p.min_bytes[2]);
@@ -355,6 +357,8 @@ double nb_policy_value(const char* env, const char* field) {
   if (f == "force_ag") return double(int(p.force_algo[1]));
   if (f == "force_rs") return double(int(p.force_algo[2]));
   if (f == "ring_chunk") return double(p.ring_chunk);
+  if (f == "nvls_round") return double(p.nvls_round_bytes);
+  if (f == "min_host_bytes") return double(p.min_host_bytes);
   if (f == "hybrid_nvls_ppm") return p.hybrid_nvls_ppm;
   if (f == "hybrid_blocks") return p.hybrid_blocks;
   if (f == "nvls_tma") return p.nvls_tma;
@@ -589,6 +593,40 @@ int nb_summary_sample(char* out, size_t cap) {
   for (const std::string& l : s.render("test")) all += l + "\n";
   copy_out(all, out, cap);
   return int(all.size());
+}
+
+
+
+// ---- Buffer classification (pointer facts -> class) ------------------------
+
+struct nb_facts_t {
+  int known, device_memory, device, from_pool, legacy_ipc, ndev;
+  uint64_t range_start, range_size, mapping_start, mapping_size;
+  int access[kMaxRanks];  // Access enum values
+};
+
+static PointerFacts to_facts(const nb_facts_t& c) {
+  PointerFacts f;
+  f.known = c.known != 0;
+  f.device_memory = c.device_memory != 0;
+  f.device = c.device;
+  f.from_pool = c.from_pool != 0;
+  f.legacy_ipc = c.legacy_ipc;
+  f.ndev = c.ndev;
+  f.range_start = c.range_start;
+  f.range_size = c.range_size;
+  f.mapping_start = c.mapping_start;
+  f.mapping_size = c.mapping_size;
+  for (int i = 0; i < kMaxRanks; ++i) f.access[i] = Access(c.access[i]);
+  return f;
+}
+
+// 0 refused, 1 ordinary, 2 mapped; the deciding rule's name into `rule`.
+int nb_classify_buffer(const nb_facts_t* first, const nb_facts_t* last, uint64_t addr, uint64_t bytes,
+                       int device, char* rule, size_t cap) {
+  const BufferVerdict v = classify_buffer(to_facts(*first), to_facts(*last), addr, bytes, device);
+  copy_out(v.rule, rule, cap);
+  return int(v.cls);
 }
 
 }  // extern "C"

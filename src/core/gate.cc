@@ -63,6 +63,8 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
       return k == Kind::AllReduce && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
              (op == RedOp::Sum || op == RedOp::Avg || op == RedOp::PreMulSum);
+    case Algo::ArOneShot:
+      return k == Kind::AllReduce && nranks >= 2 && (t == DType::F32 || t == DType::F16 || t == DType::BF16);
     case Algo::RsPull: return k == Kind::ReduceScatter;
     case Algo::AgPull: return k == Kind::AllGather;
     case Algo::BcPull: return k == Kind::Broadcast;
@@ -79,6 +81,7 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
       return k == (a == Algo::RsPush ? Kind::ReduceScatter : Kind::AllReduce) && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16);
     case Algo::RsNvls:
+    case Algo::RsHybrid:
       return k == Kind::ReduceScatter && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
              (op == RedOp::Sum || op == RedOp::Avg || op == RedOp::PreMulSum);
@@ -144,7 +147,7 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
   // every slot must be 16-byte aligned. They scale the switch's sum once, so
   // a PreMulSum takes them only when every rank passed the same host scalar.
   const bool nvls = algo == Algo::ArNvls || algo == Algo::BcNvls || algo == Algo::AgNvls ||
-                    algo == Algo::RsNvls || algo == Algo::ArHybrid;
+                    algo == Algo::RsNvls || algo == Algo::ArHybrid || algo == Algo::RsHybrid;
   bool aligned = call_bytes(a) % 16 == 0;
   for (const CallDesc& c : calls)
     aligned = aligned && c.recv % 16 == 0 && (c.send % 16 == 0 || (c.kind == Kind::Broadcast && c.rank != c.root));

@@ -1,9 +1,10 @@
-// NCCL group buffering state machine, generalized to cliques of N ranks.
+// NCCL group buffering state machine, generalized to cliques of N ranks,
+// written as the transition system of tla/GroupFallbackN.tla (Receive, End).
 //
 // Inside an outer ncclGroupStart/End, up to N eligible calls of one kind are
 // buffered (NCCL itself defers grouped calls, so returning success without
 // touching the GPU is legal). At the outer GroupEnd an exact clique set (N
-// calls) is handed to the clique runner; anything else is replayed, in
+// calls) is handed to the clique runner; anything else is forwarded, in
 // arrival order, into the real group that GroupStart already opened. The
 // first call that cannot be buffered (wrong kind, failed gate, one call too
 // many, an unsupported operation, a nested group) flushes the buffered prefix
@@ -88,7 +89,11 @@ class GroupMachine {
   int force_passthrough(GroupState& g, bool initialization = false);
 
  private:
-  int replay(GroupState& g, Reason reason);
+  Reason decide_receive(const GroupState& g, Call& c);
+  bool decide_end(const GroupState& g) const;
+  int apply_flush(GroupState& g, Reason why, const Call* arriving);
+  int forward_pending(GroupState& g, Reason why);
+  int ungrouped(Call& c);
   GroupBackend& b_;
 };
 

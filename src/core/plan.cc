@@ -19,6 +19,7 @@ void Needs::merge(const Needs& o) {
   temp_bytes = std::max(temp_bytes, o.temp_bytes);
   ring = ring || o.ring;
   pushred = pushred || o.pushred;
+  oneshot = oneshot || o.oneshot;
 }
 
 void slice_of(size_t bytes, int parts, int i, size_t* off, size_t* len) {
@@ -167,6 +168,14 @@ class Builder {
   void prologue() {
     for (int r = 0; r < n_; ++r) record(input_ready(r), caller(r));
   }
+  // Gang engines launched on caller streams share state across calls (see
+  // Ev::GangDone): every rank's caller stream first waits for the previous
+  // gang call to have finished on every GPU of the clique.
+  void gang_fence() {
+    for (int r = 0; r < n_; ++r)
+      for (int q = 0; q < n_; ++q) wait(caller(r), {Ev::GangDone, uint8_t(q), 0, 0});
+  }
+  void gang_done(int r) { record({Ev::GangDone, uint8_t(r), 0, 0}, caller(r)); }
   // Every rank's caller stream waits for its own internal streams, then for
   // every peer's join, so no rank returns while a peer still reads its send
   // buffer or writes its receive buffer.
@@ -723,11 +732,13 @@ void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p) {
 // pieces to its successor as they arrive (in-kernel progress words).
 void plan_bc_ring(Builder& b, const CliqueDesc& d) {
   const int n = b.n();
+  b.gang_fence();
   b.prologue();
   for (int r = 0; r < n; ++r) {
     const StreamId cs{Strm::Caller, uint8_t(r), 0};
     for (int q = 0; q < n; ++q) b.touch(cs, q);
     b.nvls(cs, r, d.bytes);
+    b.gang_done(r);
   }
   b.plan().needs.ring = true;
   b.plan().sm_bytes += d.bytes * size_t(n - 1);
@@ -738,14 +749,19 @@ void plan_bc_ring(Builder& b, const CliqueDesc& d) {
 // NVLS gang on `hybrid_blocks` SMs per GPU, launched first), the rest by the
 // two-shot P2P kernel, which the remaining SMs run at the same time; both
 // shares cross NVLink concurrently. The split point is 4 KiB aligned.
+int split_ppm(const Policy& p, const Shares& s) { return s.split_ppm > 0 ? s.split_ppm : p.hybrid_nvls_ppm; }
+uint16_t split_blocks(const Policy& p, const Shares& s) {
+  return uint16_t(s.split_blocks > 0 ? s.split_blocks : p.hybrid_blocks);
+}
+
 void plan_ar_hybrid(Builder& b, const CliqueDesc& d, const Policy& p, const Shares& s) {
   const int n = b.n();
   b.prologue();
-  const size_t nv = d.bytes / 10000 * size_t(p.hybrid_nvls_ppm) / 4096 * 4096;
+  const size_t nv = d.bytes / 10000 * size_t(split_ppm(p, s)) / 4096 * 4096;
   for (int r = 0; r < n; ++r) {
     const StreamId as{Strm::Aux, uint8_t(r), 0};
     for (int q = 0; q < n; ++q) b.touch(as, q);
-    if (nv) b.nvls(as, r, nv, 0, uint16_t(p.hybrid_blocks));
+    if (nv) b.nvls(as, r, nv, 0, split_blocks(p, s));
   }
   if (nv) {
     b.plan().needs.nvls_bytes = p.nvls_round_bytes;
@@ -757,15 +773,50 @@ void plan_ar_hybrid(Builder& b, const CliqueDesc& d, const Policy& p, const Shar
   b.join();
 }
 
+// Hybrid ReduceScatter: the leading share of every slot through the switch
+// (the NVLS ReduceScatter gang on part of the SMs, launched first on the aux
+// streams), the rest of each slot by the P2P pull fold on the caller
+// streams, at the same time. NVLS reads every slot of every GPU once through
+// the switch while the pulls use the links' remaining capacity.
+void plan_rs_hybrid(Builder& b, const CliqueDesc& d, const Policy& p, const Shares& s) {
+  const int n = b.n();
+  b.prologue();
+  const size_t slot = d.bytes;
+  const size_t nv = slot / 10000 * size_t(split_ppm(p, s)) / 4096 * 4096;
+  for (int r = 0; r < n; ++r) {
+    const StreamId as{Strm::Aux, uint8_t(r), 0};
+    for (int q = 0; q < n; ++q) b.touch(as, q);
+    if (nv) b.nvls(as, r, nv, 0, split_blocks(p, s));
+  }
+  if (nv) {
+    b.plan().needs.nvls_bytes = p.nvls_round_bytes;
+    b.plan().sm_bytes += nv * size_t(n) * size_t(n);
+  }
+  for (int r = 0; r < n && nv < slot; ++r) {
+    const StreamId cs{Strm::Caller, uint8_t(r), 0};
+    Loc src[kMaxRanks];
+    for (int q = 0; q < n; ++q) {
+      b.touch(cs, q);
+      src[q] = send_at(q, size_t(r) * slot + nv);
+    }
+    const Loc dst = recv_at(r, nv);
+    b.sm_reduce(cs, src, n, &dst, 1, slot - nv);
+    b.plan().sm_bytes += (slot - nv) * size_t(n - 1);
+  }
+  b.join();
+}
+
 // Push-reduce ReduceScatter / AllReduce (exec/pushred.cu): one gang op per
 // rank on its caller stream after every rank's input is ready.
 void plan_pushred(Builder& b, const CliqueDesc& d) {
   const int n = b.n();
+  b.gang_fence();
   b.prologue();
   for (int r = 0; r < n; ++r) {
     const StreamId cs{Strm::Caller, uint8_t(r), 0};
     for (int q = 0; q < n; ++q) b.touch(cs, q);
     b.nvls(cs, r, d.bytes);
+    b.gang_done(r);
   }
   b.plan().needs.pushred = true;
   const size_t moved = d.kind == Kind::AllReduce ? d.bytes * size_t(2 * (n - 1)) : d.bytes * size_t(n - 1) * size_t(n);
@@ -773,16 +824,40 @@ void plan_pushred(Builder& b, const CliqueDesc& d) {
   b.join();
 }
 
+// AllReduce one-shot (exec/oneshot.cu): one gang op per rank on its caller
+// stream and nothing else -- no event records or waits. Inside, every
+// rank's blocks meet their counterparts on every GPU (arrive), fold the
+// whole message from all N inputs in rank order into their own output only,
+// and meet again (depart) before the stream may go on. Each GPU reads
+// (N-1) x S over NVLink, so the route pays for small and medium messages,
+// where the cross-device event fans of an event-ordered plan would cost
+// more than the bytes. In place, a rank would overwrite its input while
+// peers still read it, so an in-place call takes the two-shot plan instead.
+void plan_ar_oneshot(Builder& b, const CliqueDesc& d) {
+  const int n = b.n();
+  for (int r = 0; r < n; ++r) b.nvls({Strm::Caller, uint8_t(r), 0}, r, d.bytes);
+  b.plan().needs.oneshot = true;
+  b.plan().sm_bytes += d.bytes * size_t(n - 1) * size_t(n);
+}
+
 // One rank: every collective except a scaled one (PreMulSum) is a copy of
-// the input into the output on the caller stream: the SM copy kernel, which
-// takes the TMA bulk path for a large copy within one GPU.
-void plan_single(Builder& b, const CliqueDesc& d) {
+// the input into the output: the SM stream copy kernel on the caller stream,
+// beside an optional copy-engine share (the leading ce_ppm of the bytes, on
+// the copy stream) that the init-time tuning keeps when the two engines
+// together move more than the kernel alone.
+void plan_single(Builder& b, const CliqueDesc& d, const Shares& s) {
   b.prologue();
   const StreamId cl{Strm::Caller, 0, 0};
   b.touch(cl, 0);
   if (!d.in_place[0]) {
-    const Loc dst = recv_at(0, 0), src = send_at(0, 0);
-    const size_t len = d.bytes;
+    const size_t ce = ce_share(d.bytes, s.ce_ppm) & ~size_t(31);  // keeps the SM part 32-byte aligned
+    if (ce) {
+      const StreamId cp{Strm::Copy, 0, 0};
+      b.touch(cp, 0);
+      b.ce_copy(cp, recv_at(0, 0), send_at(0, 0), ce);
+    }
+    const Loc dst = recv_at(0, ce), src = send_at(0, ce);
+    const size_t len = d.bytes - ce;
     b.sm_copy(cl, &dst, &src, &len, 1);
   }
   b.join();
@@ -793,10 +868,15 @@ void plan_single(Builder& b, const CliqueDesc& d) {
 void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s, Plan& out) {
   Builder b(out, algo, d, p);
   if (d.nranks == 1 && algo != Algo::Fallback && !(reduces(d.kind) && d.op == RedOp::PreMulSum)) {
-    plan_single(b, d);
+    plan_single(b, d, s);
     return;
   }
+  bool in_place = false;
+  for (int r = 0; r < d.nranks; ++r) in_place = in_place || d.in_place[r];
+  if (algo == Algo::ArOneShot && in_place) algo = Algo::ArTwoShot;
+  b.plan().algo = algo;
   switch (algo) {
+    case Algo::ArOneShot: plan_ar_oneshot(b, d); break;
     case Algo::ArTwoShot: plan_ar_twoshot(b, d, s); break;
     case Algo::ArNvls: plan_ar_nvls(b, d, p); break;
     case Algo::RsPull: plan_rs_pull(b, d, s); break;
@@ -805,6 +885,7 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
     case Algo::BcRing: plan_bc_ring(b, d); break;
     case Algo::RsPush: case Algo::ArPush: plan_pushred(b, d); break;
     case Algo::ArHybrid: plan_ar_hybrid(b, d, p, s); break;
+    case Algo::RsHybrid: plan_rs_hybrid(b, d, p, s); break;
     case Algo::BcPull: plan_bc_pull(b, d, s); break;
     case Algo::BcScatter: plan_bc_scatter(b, d, s); break;
     case Algo::ArStaged: plan_staged(b, d, s, true); break;

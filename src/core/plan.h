@@ -44,7 +44,13 @@ inline bool operator!=(StreamId a, StreamId b) { return !(a == b); }
 // an internal stream's work in this plan (index = stream kind).
 // TempFree(dev) marks the end of a staged call's last read of its scratch:
 // the next staged call's first copy into that scratch waits for it.
-enum class Ev : uint8_t { InputReady, Join, Phase, Done, D2HDone, H2DDone, HostDone, LaneFree, TempFree, Count };
+// GangDone(dev) marks the end of the last gang op a caller stream ran on that
+// GPU (push chain, push-reduce): those engines keep per-device-set scratch,
+// progress words and an epoch, so the next such call waits for GangDone on
+// every GPU of its clique before it starts (two calls on unordered streams,
+// or from two cliques over the same GPUs, never overlap).
+enum class Ev : uint8_t { InputReady, Join, Phase, Done, D2HDone, H2DDone, HostDone, LaneFree, TempFree,
+                          GangDone, Count };
 struct EventId {
   Ev kind = Ev::InputReady;
   uint8_t dev = 0;
@@ -80,7 +86,8 @@ inline Loc temp_at(int r, size_t off) { return {Buf::Temp, uint8_t(r), 0, off}; 
 // NvlsReduce: one rank's share of a gang collective (NVLS, push chain,
 // push-reduce); the N NvlsReduce ops of a plan form a gang that synchronizes
 // inside the kernel. For AllReduce it covers [src[0].off, +bytes) of every
-// rank's buffers; for the other kinds the whole message.
+// rank's buffers; for ReduceScatter that range of every slot; for the other
+// kinds the whole message.
 enum class OpKind : uint8_t { Record, Wait, CeCopy, SmCopy, SmReduce, HostReduce, NvlsReduce };
 struct PlanOp {
   OpKind kind = OpKind::Record;
@@ -103,6 +110,7 @@ struct Needs {
   size_t temp_bytes = 0;       // device scratch per GPU (staged routes)
   bool ring = false;           // progress words for the in-kernel chain
   bool pushred = false;        // scratch and progress words of the push-reduce engine
+  bool oneshot = false;        // arrive/depart tables of the one-shot engine
   void merge(const Needs& o);
 };
 
@@ -113,6 +121,10 @@ struct Shares {
   int ce_ppm = 0;
   size_t stage_piece = 0;
   int stage_depth = 0;
+  // Hybrid routes: the switch's share of the message (per 10000) and the
+  // blocks per GPU its kernel gets (0 = the policy's).
+  int split_ppm = 0;
+  int split_blocks = 0;
 };
 
 struct Plan {

@@ -193,12 +193,23 @@ void accesses_of(const PlanOp& op, const SimLayout& lay, const CliqueDesc& d,
       for (int i = 0; i < op.ndst; ++i) add(op.dst[i], op.bytes, true);
       break;
     case OpKind::NvlsReduce:
-      // The gang reads every rank's input and writes every rank's output
-      // (for AllReduce, over the op's range).
+      // The gang reads every rank's input and writes every rank's output:
+      // AllReduce over the op's range, ReduceScatter over the op's range of
+      // every slot, the other kinds over the whole message.
       for (int q = 0; q < n; ++q) {
-        const bool ranged = d.kind == Kind::AllReduce;
-        add(send_at(q, ranged ? op.src[0].off : 0), ranged ? op.bytes : d.bytes, false);
-        add(recv_at(q, ranged ? op.dst[0].off : 0), ranged ? op.bytes : d.bytes, true);
+        if (d.kind == Kind::AllReduce) {
+          add(send_at(q, op.src[0].off), op.bytes, false);
+          add(recv_at(q, op.dst[0].off), op.bytes, true);
+        } else if (d.kind == Kind::ReduceScatter) {
+          for (int r = 0; r < n; ++r) add(send_at(q, size_t(r) * d.bytes + op.src[0].off), op.bytes, false);
+          add(recv_at(q, op.dst[0].off), op.bytes, true);
+        } else if (d.kind == Kind::AllGather) {
+          add(send_at(q, 0), d.bytes, false);
+          add(recv_at(q, 0), d.bytes * size_t(n), true);
+        } else {
+          add(send_at(q, 0), d.bytes, false);
+          add(recv_at(q, 0), d.bytes, true);
+        }
       }
       break;
     default:
@@ -345,7 +356,8 @@ std::string simulate_plan(const Plan& plan, const SimLayout& lay, const FoldPara
       // The whole gang collective for every rank at once (an AllReduce gang
       // over its ops' range).
       size_t bytes = plan.desc.bytes, goff = 0;
-      if (plan.desc.kind == Kind::AllReduce)
+      const size_t slot = plan.desc.bytes;  // ReduceScatter: the stride between slots
+      if (plan.desc.kind == Kind::AllReduce || plan.desc.kind == Kind::ReduceScatter)
         for (const PlanOp& op : plan.ops)
           if (op.kind == OpKind::NvlsReduce) {
             bytes = op.bytes;
@@ -376,7 +388,7 @@ std::string simulate_plan(const Plan& plan, const SimLayout& lay, const FoldPara
           std::vector<uint8_t> all(bytes * size_t(n));
           for (int r = 0; r < n; ++r) {
             const void* srcs[kMaxRanks];
-            for (int q = 0; q < n; ++q) srcs[q] = send(q) + size_t(r) * bytes;
+            for (int q = 0; q < n; ++q) srcs[q] = send(q) + size_t(r) * slot;
             host_fold(fp, srcs, n, all.data() + size_t(r) * bytes, bytes);
           }
           for (int r = 0; r < n; ++r) std::memcpy(recv(r), all.data() + size_t(r) * bytes, bytes);

@@ -53,6 +53,7 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else return false;
   if (a == "nccl" || a == "fallback") *algo = Algo::Fallback;
   else if (a == "twoshot" && *kind == Kind::AllReduce) *algo = Algo::ArTwoShot;
+  else if (a == "oneshot" && *kind == Kind::AllReduce) *algo = Algo::ArOneShot;
   else if (a == "nvls" && *kind == Kind::AllReduce) *algo = Algo::ArNvls;
   else if (a == "pull" && *kind == Kind::ReduceScatter) *algo = Algo::RsPull;
   else if (a == "pull" && *kind == Kind::AllGather) *algo = Algo::AgPull;
@@ -69,6 +70,7 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else if (a == "push" && *kind == Kind::ReduceScatter) *algo = Algo::RsPush;
   else if (a == "push" && *kind == Kind::AllReduce) *algo = Algo::ArPush;
   else if (a == "hybrid" && *kind == Kind::AllReduce) *algo = Algo::ArHybrid;
+  else if (a == "hybrid" && *kind == Kind::ReduceScatter) *algo = Algo::RsHybrid;
   else return false;
   return true;
 }
@@ -101,6 +103,10 @@ Policy policy_from_env(const EnvLookup& env) {
   if (parse_int(env("NCCL_B200_NVLS_UNROLL"), &i) && (i == 4 || i == 8)) p.nvls_unroll = int(i);
   if (parse_bool(env("NCCL_B200_NVLS_TRACE"), &b)) p.nvls_trace = b;
   if (parse_bool(env("NCCL_B200_NVLS_TMA"), &b)) p.nvls_tma = b;
+  if (const char* v = env("NCCL_B200_LOCAL_COPY")) {
+    if (std::strcmp(v, "tma") == 0) p.local_copy_tma = true;
+    else if (std::strcmp(v, "sm") == 0) p.local_copy_tma = false;
+  }
   if (parse_size(env("NCCL_B200_RING_CHUNK"), &z) && z >= 4096 && z <= (64u << 20) && z % 32 == 0)
     p.ring_chunk = z;
   if (parse_int(env("NCCL_B200_HYBRID_NVLS_PPM"), &i) && i >= 1000 && i <= 9000) p.hybrid_nvls_ppm = int(i);

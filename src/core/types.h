@@ -54,6 +54,8 @@ enum class Algo : uint8_t {
   RsPush,      // senders store into owners' scratch; owners fold (stores only)
   ArPush,      // RsPush, then owners store the result into every output
   ArHybrid,    // NVLS on part of the SMs for one share, two-shot P2P for the rest
+  ArOneShot,   // every rank folds the whole message from all inputs into its own output
+  RsHybrid,    // NVLS ReduceScatter on part of the SMs for one share, P2P pulls for the rest
   Count
 };
 

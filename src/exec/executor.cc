@@ -5,6 +5,7 @@
 #include <cstring>
 
 #include "exec/nvls.h"
+#include "exec/oneshot.h"
 #include "exec/pushred.h"
 #include "exec/ring.h"
 #include "kernels/kernels.h"
@@ -80,7 +81,8 @@ bool Executor::ensure_device(int dev, std::string* why) {
   }
   r.sm_count = sms;
   bool ok = make_stream(r.aux) && make_stream(r.copy) && make_stream(r.push) &&
-            make_event(r.input_ready) && make_event(r.join) && make_event(r.temp_free);
+            make_event(r.input_ready) && make_event(r.join) && make_event(r.temp_free) &&
+            make_event(r.gang_done);
   for (int l = 0; ok && l < kMaxLanes; ++l)
     ok = make_stream(r.d2h[l]) && make_stream(r.h2d[l]) && make_event(r.d2h_done[l]) &&
          make_event(r.h2d_done[l]);
@@ -240,6 +242,7 @@ bool Executor::ensure(const Needs& needs, const int* devices, int n, std::string
   if (needs.nvls_bytes > 0 && !nvls_ensure(devices, n, needs.nvls_bytes, why)) return false;
   if (needs.ring && !ring_ensure(devices, n, why)) return false;
   if (needs.pushred && !pushred_ensure(devices, n, why)) return false;
+  if (needs.oneshot && !oneshot_ensure(devices, n, why)) return false;
   return true;
 }
 
@@ -272,6 +275,7 @@ cudaEvent_t Executor::bind_event(EventId e, const Binding& b) {
     case Ev::InputReady: return r.input_ready;
     case Ev::Join: return r.join;
     case Ev::TempFree: return r.temp_free;
+    case Ev::GangDone: return r.gang_done;
     case Ev::Phase: return e.index < r.phase.size() ? r.phase[e.index] : nullptr;
     case Ev::Done: return r.done[e.index][e.lane];
     case Ev::D2HDone: return r.d2h_done[e.lane];
@@ -310,6 +314,7 @@ cudaError_t Executor::submit(const PlanOp& op, const Plan& plan, const Binding& 
       CopyLaunch c;
       c.nseg = op.nsrc;
       c.local = true;
+      c.prefer_tma = policy_.local_copy_tma;
       const auto on_device = [&](const Loc& l) {
         return (l.buf == Buf::Send || l.buf == Buf::Recv || l.buf == Buf::Temp) &&
                b.device[l.dev] == b.device[op.stream.dev];
@@ -357,6 +362,7 @@ cudaError_t Executor::submit(const PlanOp& op, const Plan& plan, const Binding& 
       launches_.fetch_add(1, std::memory_order_relaxed);
       if (plan.algo == Algo::BcRing) return ring_launch(op, plan, b, policy_, s);
       if (plan.algo == Algo::RsPush || plan.algo == Algo::ArPush) return pushred_launch(op, plan, b, policy_, s);
+      if (plan.algo == Algo::ArOneShot) return oneshot_launch(op, plan, b, policy_, s);
       return nvls_launch(op, plan, b, policy_, s, dev);
     default:
       return cudaErrorNotSupported;

@@ -49,7 +49,7 @@ struct DeviceResources {
   int sm_count = 0;
   cudaStream_t aux = nullptr, copy = nullptr, push = nullptr;
   cudaStream_t d2h[kMaxLanes] = {}, h2d[kMaxLanes] = {};
-  cudaEvent_t input_ready = nullptr, join = nullptr, temp_free = nullptr;
+  cudaEvent_t input_ready = nullptr, join = nullptr, temp_free = nullptr, gang_done = nullptr;
   void* temp = nullptr;  // device scratch of the staged routes
   size_t temp_bytes = 0;
   cudaEvent_t done[size_t(Strm::Count)][kMaxLanes] = {};

@@ -1,97 +1,155 @@
 // NUMA-local pinned host staging buffers for the PCIe host lane.
 //
-// The GPU's NUMA node comes from cudaDevAttrNumaId when the runtime has it,
-// else from /sys/bus/pci/devices/<bdf>/numa_node. The buffer is an anonymous
-// mapping bound to that node (mbind MPOL_BIND, STRICT|MOVE), first-touched,
-// verified with move_pages on up to 16 sampled pages, then registered with
-// cudaHostRegister(Portable). Any failure falls back to cudaHostAlloc.
+// Node: cudaDevAttrHostNumaId, the host node nearest the GPU as the driver
+// reports it; where the driver has none, the numa_node file of the GPU's PCI
+// function in sysfs.
 //
-// Parity: staging_numa_node / staging_placement / allocate_bounce /
-// free_bounce of the reference (shim/nccl_collectives_shim.cu:956-1078).
+// Placement: for the duration of one allocation the calling thread's memory
+// policy binds to that node (set_mempolicy; the previous policy is restored
+// afterwards). An anonymous mapping is created with MAP_POPULATE, so every
+// page is faulted in now, by this thread, under that policy; the pages are
+// then pinned for the GPU with cudaHostRegister (portable). The placement is
+// checked page by page on an even sample of the buffer (get_mempolicy with
+// MPOL_F_NODE | MPOL_F_ADDR answers the node a page lives on). Any failure
+// frees what was made and falls back to cudaHostAlloc; the summary reports
+// the target node, the node found and which method served.
+//
+// Parity: the reference's host bounce buffers (shim/nccl_collectives_shim.cu:
+// 956-1078) are NUMA-local pinned memory placed with mbind and checked with
+// move_pages.
 #include <linux/mempolicy.h>
 #include <sys/mman.h>
 #include <sys/syscall.h>
 #include <unistd.h>
 
+#include <algorithm>
+#include <array>
 #include <cctype>
-#include <cstdio>
+#include <fstream>
+#include <string>
 #include <vector>
 
 #include "exec/executor.h"
 
 namespace nb {
 
-int gpu_numa_node(int dev) {
+namespace {
+
+// Bits in the node masks passed to the kernel (covers every node id a
+// machine of this class can have; get_mempolicy refuses masks smaller than
+// the kernel's node count).
+constexpr unsigned long kMaskBits = 4096;
+using NodeMask = std::array<unsigned long, kMaskBits / (8 * sizeof(unsigned long))>;
+
+long sys_set_policy(int mode, const unsigned long* mask, unsigned long bits) {
+  return syscall(SYS_set_mempolicy, mode, mask, bits);
+}
+
+// The node a page lives on, or -1.
+int node_of_page(void* addr) {
   int node = -1;
-  if (cudaDeviceGetAttribute(&node, cudaDevAttrNumaId, dev) == cudaSuccess && node >= 0) return node;
-  cudaGetLastError();
-  char pci[32] = {};
-  if (cudaDeviceGetPCIBusId(pci, sizeof(pci), dev) != cudaSuccess) {
+  if (syscall(SYS_get_mempolicy, &node, nullptr, 0ul, addr, MPOL_F_NODE | MPOL_F_ADDR) != 0) return -1;
+  return node;
+}
+
+// Binds this thread's allocations to one node while alive; restores the
+// thread's previous policy on destruction.
+class ThreadNodeBinding {
+ public:
+  explicit ThreadNodeBinding(int node) {
+    NodeMask old{};
+    if (syscall(SYS_get_mempolicy, &old_mode_, old.data(), kMaskBits, nullptr, 0ul) != 0) return;
+    old_mask_ = old;
+    saved_ = true;
+    NodeMask want{};
+    want[size_t(node) / (8 * sizeof(unsigned long))] |= 1ul << (size_t(node) % (8 * sizeof(unsigned long)));
+    bound_ = sys_set_policy(MPOL_BIND, want.data(), kMaskBits) == 0;
+  }
+  ~ThreadNodeBinding() {
+    if (!bound_) return;
+    if (old_mode_ == MPOL_DEFAULT) sys_set_policy(MPOL_DEFAULT, nullptr, 0);
+    else sys_set_policy(old_mode_, old_mask_.data(), kMaskBits);
+  }
+  bool bound() const { return saved_ && bound_; }
+  ThreadNodeBinding(const ThreadNodeBinding&) = delete;
+  ThreadNodeBinding& operator=(const ThreadNodeBinding&) = delete;
+
+ private:
+  int old_mode_ = MPOL_DEFAULT;
+  NodeMask old_mask_{};
+  bool saved_ = false, bound_ = false;
+};
+
+// The node every sampled page of [p, p + len) lives on, or -1 when they
+// differ or cannot be read: pages at each eighth of the buffer and its last.
+int placement_of(void* p, size_t len, size_t page) {
+  if (!p || !len || !page) return -1;
+  std::vector<size_t> offsets;
+  for (int k = 0; k < 8; ++k) offsets.push_back(len / 8 * size_t(k) / page * page);
+  offsets.push_back((len - 1) / page * page);
+  int node = -2;
+  for (size_t off : offsets) {
+    const int here = node_of_page(static_cast<char*>(p) + off);
+    if (here < 0 || (node != -2 && here != node)) return -1;
+    node = here;
+  }
+  return node;
+}
+
+int sysfs_numa_node(int dev) {
+  char bus[64] = {};
+  if (cudaDeviceGetPCIBusId(bus, sizeof bus, dev) != cudaSuccess) {
     cudaGetLastError();
     return -1;
   }
-  for (char* c = pci; *c; ++c) {
-    const unsigned char v = static_cast<unsigned char>(*c);
-    if (!std::isxdigit(v) && *c != ':' && *c != '.') return -1;
-    *c = static_cast<char>(std::tolower(v));
-  }
-  char path[96];
-  std::snprintf(path, sizeof(path), "/sys/bus/pci/devices/%s/numa_node", pci);
-  FILE* f = std::fopen(path, "r");
-  if (!f) return -1;
-  int placed = -1;
-  const bool parsed = std::fscanf(f, "%d", &placed) == 1;
-  std::fclose(f);
-  return parsed ? placed : -1;
+  std::string id(bus);
+  std::transform(id.begin(), id.end(), id.begin(), [](unsigned char c) { return char(std::tolower(c)); });
+  const bool plain = !id.empty() && std::all_of(id.begin(), id.end(), [](unsigned char c) {
+    return std::isxdigit(c) || c == ':' || c == '.';
+  });
+  if (!plain) return -1;
+  std::ifstream in("/sys/bus/pci/devices/" + id + "/numa_node");
+  int node = -1;
+  return (in >> node) ? node : -1;
 }
 
-static int sampled_placement(void* p, size_t n, size_t page) {
-  if (!n || !page) return -1;
-  const size_t pages = 1 + (n - 1) / page;
-  const size_t count = pages < 16 ? pages : 16;
-  void* addresses[16];
-  int status[16];
-  for (size_t i = 0; i < count; ++i) {
-    const size_t index = count == 1 ? 0 : (pages - 1) * i / (count - 1);
-    addresses[i] = static_cast<char*>(p) + index * page;
-    status[i] = -1;
-  }
-  if (syscall(SYS_move_pages, 0, count, addresses, nullptr, status, 0) != 0) return -1;
-  for (size_t i = 0; i < count; ++i)
-    if (status[i] < 0 || status[i] != status[0]) return -1;
-  return status[0];
+}  // namespace
+
+int gpu_numa_node(int dev) {
+  int node = -1;
+  if (cudaDeviceGetAttribute(&node, cudaDevAttrHostNumaId, dev) == cudaSuccess && node >= 0) return node;
+  cudaGetLastError();
+  return sysfs_numa_node(dev);
 }
 
 void* alloc_pinned_near(int dev, size_t bytes, size_t* mapped, int* target_out, int* placed_out,
                         const char** method) {
   *mapped = 0;
+  *placed_out = -1;
   const int target = gpu_numa_node(dev);
   *target_out = target;
-  *placed_out = -1;
-  const long page_size = sysconf(_SC_PAGESIZE);
-  const size_t page = page_size > 0 ? size_t(page_size) : 0;
-  if (target >= 0 && target < 4096 && page && bytes <= SIZE_MAX - (page - 1)) {
-    const size_t rounded = ((bytes + page - 1) / page) * page;
-    void* p = mmap(nullptr, rounded, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+  const long sz = sysconf(_SC_PAGESIZE);
+  const size_t page = sz > 0 ? size_t(sz) : 0;
+  const bool placeable = target >= 0 && size_t(target) < kMaskBits && page && bytes > 0 &&
+                         bytes <= ~size_t(0) - page;
+  if (placeable) {
+    const size_t len = (bytes + page - 1) / page * page;
+    void* p = MAP_FAILED;
+    {
+      ThreadNodeBinding bind(target);
+      if (bind.bound())
+        p = mmap(nullptr, len, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS | MAP_POPULATE, -1, 0);
+    }
     if (p != MAP_FAILED) {
-      constexpr size_t bits = sizeof(unsigned long) * 8;
-      std::vector<unsigned long> mask(size_t(target) / bits + 2, 0);
-      mask[size_t(target) / bits] |= 1UL << (size_t(target) % bits);
-      bool ok = syscall(SYS_mbind, p, rounded, MPOL_BIND, mask.data(),
-                        static_cast<unsigned long>(mask.size() * bits), MPOL_MF_STRICT | MPOL_MF_MOVE) == 0;
-      if (ok) {
-        for (size_t off = 0; off < rounded; off += page) static_cast<volatile unsigned char*>(p)[off] = 0;
-        const int placed = sampled_placement(p, rounded, page);
-        *placed_out = placed;
-        ok = placed == target;
-      }
-      if (ok && cudaHostRegister(p, rounded, cudaHostRegisterPortable) == cudaSuccess) {
-        *mapped = rounded;
-        *method = "mbind";
+      const int placed = placement_of(p, len, page);
+      *placed_out = placed;
+      if (placed == target && cudaHostRegister(p, len, cudaHostRegisterPortable) == cudaSuccess) {
+        *mapped = len;
+        *method = "bound";
         return p;
       }
       cudaGetLastError();
-      munmap(p, rounded);
+      munmap(p, len);
     }
   }
   void* p = nullptr;
@@ -99,26 +157,23 @@ void* alloc_pinned_near(int dev, size_t bytes, size_t* mapped, int* target_out, 
     cudaGetLastError();
     return nullptr;
   }
-  *placed_out = page ? sampled_placement(p, bytes, page) : -1;
+  *placed_out = page ? placement_of(p, bytes, page) : -1;
   *method = "fallback";
   return p;
 }
 
 bool free_pinned(void* p, size_t bytes, size_t mapped) {
   if (!p) return true;
+  bool ok = true;
   if (mapped) {
-    if (cudaHostUnregister(p) != cudaSuccess) {
-      cudaGetLastError();
-      return false;
-    }
-    return munmap(p, mapped) == 0;
+    ok = cudaHostUnregister(p) == cudaSuccess;
+    if (!ok) cudaGetLastError();
+    return ok && munmap(p, mapped) == 0;
   }
   (void)bytes;
-  if (cudaFreeHost(p) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  return true;
+  ok = cudaFreeHost(p) == cudaSuccess;
+  if (!ok) cudaGetLastError();
+  return ok;
 }
 
 }  // namespace nb

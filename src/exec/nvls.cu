@@ -15,8 +15,11 @@
 // each waiting for exactly the steps it consumes, so neither waits on the
 // other group's unrelated work. Every wait is bounded by %globaltimer: on
 // expiry the kernel writes a status word in mapped host memory and returns;
-// the host turns it into ncclUnhandledCudaError and disables the route. No
-// TMA, and no multicast TMA, is used.
+// the host turns it into ncclUnhandledCudaError and disables the route.
+// The copier group can run as one warp of TMA bulk copies (cp.async.bulk
+// global -> shared on an mbarrier, shared -> global in bulk groups); those
+// copies read and write only this GPU's own memory (the user's buffers and
+// the unicast view of its scratch). No load with cluster multicast is used.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -56,7 +59,8 @@ struct NvlsArgs {
   int movers;                // threads of a block that work through the switch
   int mode;                  // collective kind (xfer kernel)
   int root;                  // Broadcast
-  unsigned long long slot;   // AllGather / ReduceScatter per-rank slot bytes
+  unsigned long long slot;   // AllGather / ReduceScatter bytes per slot to move
+  unsigned long long slot_stride;  // distance between consecutive slots
   unsigned long long* trace; // per-block phase timing record, or null
 };
 
@@ -605,7 +609,8 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_xfer_kernel(const __g
         if (s >= 3 && !group_wait(a, g, kMover, a.base + s - 2, -1)) break;
         cp.acquired();
         char* buf = a.uc + (s % 3) * a.buf_stride;
-        for (int q = 0; q < n; ++q) cp.copy(buf + q * part + lo, a.send + q * a.slot + s * part + lo, hi - lo);
+        for (int q = 0; q < n; ++q)
+          cp.copy(buf + q * part + lo, a.send + q * a.slot_stride + s * part + lo, hi - lo);
         cp.flush();
       }
     } else if (g.mover) {
@@ -624,7 +629,8 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_xfer_kernel(const __g
       if (bc) {
         cp.copy(a.recv + s * part + lo, buf + lo, hi - lo);
       } else {
-        for (int q = 0; q < n; ++q) cp.copy(a.recv + q * a.slot + s * part + lo, buf + q * part + lo, hi - lo);
+        for (int q = 0; q < n; ++q)
+          cp.copy(a.recv + q * a.slot_stride + s * part + lo, buf + q * part + lo, hi - lo);
       }
       cp.flush();
     }
@@ -886,10 +892,12 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   }
   if (plan.desc.bytes % 16 != 0) return cudaErrorInvalidValue;
   const bool ar = plan.desc.kind == Kind::AllReduce;
-  // An AllReduce gang covers the op's range of the buffers (the hybrid
-  // route gives the switch a leading share); the other kinds the message.
-  const size_t off = ar ? op.src[0].off : 0;
-  const size_t range = ar ? op.bytes : plan.desc.bytes;
+  const bool rs = plan.desc.kind == Kind::ReduceScatter;
+  // An AllReduce gang covers the op's range of the buffers, a ReduceScatter
+  // gang that range of every slot (the hybrid routes give the switch a
+  // leading share); the other kinds the message.
+  const size_t off = ar || rs ? op.src[0].off : 0;
+  const size_t range = ar || rs ? op.bytes : plan.desc.bytes;
   if (off % 16 != 0 || range % 16 != 0) return cudaErrorInvalidValue;
   const unsigned grid = op.grid ? std::min<unsigned>(op.grid, unsigned(c->blocks)) : unsigned(c->blocks);
   NvlsArgs a{};
@@ -899,7 +907,7 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.mc = c->mc[size_t(r)];
   a.uc_flags = reinterpret_cast<unsigned*>(a.uc + 3 * c->stride);
   a.mc_flags = reinterpret_cast<unsigned*>(a.mc + 3 * c->stride);
-  a.bytes = range;
+  a.bytes = ar ? range : plan.desc.bytes;
   a.round = c->round;
   a.buf_stride = c->stride;
   a.timeout_ns = p.device_timeout_ns;
@@ -913,7 +921,8 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.mul = plan.desc.op == RedOp::Avg ? 1.0f / float(b.nranks) : float(plan.desc.scalar);
   a.mode = int(plan.desc.kind);
   a.root = plan.desc.root;
-  a.slot = plan.desc.bytes;  // AG send slot / RS receive slot
+  a.slot = rs ? range : plan.desc.bytes;  // AG send slot / RS part of each receive slot
+  a.slot_stride = plan.desc.bytes;
   a.trace = p.nvls_trace ? c->trace[size_t(r)] : nullptr;
   // The largest progress value this call publishes (every rank the same):
   // the next call's epoch.
@@ -924,7 +933,7 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
     const bool bc = plan.desc.kind == Kind::Broadcast;
     const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)b.nranks) & ~31ull);
     if (part == 0) return cudaErrorInvalidValue;
-    steps = (plan.desc.bytes + part - 1) / part;
+    steps = ((bc ? plan.desc.bytes : a.slot) + part - 1) / part;
   }
   // TMA copier: the movers plus one copier warp, with the staging buffers
   // in dynamic shared memory; SM copier: the configured split.
@@ -954,12 +963,18 @@ int nvls_trace_read(const int* devices, int n, int rank, double out[6], bool res
   if (e == cudaSuccess && reset) e = cudaMemset(c->trace[size_t(rank)], 0, bytes);
   cudaSetDevice(prev);
   if (e != cudaSuccess) return -1;
-  for (int k = 0; k < 6; ++k) {
-    double sum = 0;
-    for (int b = 0; b < c->blocks; ++b) sum += double(rec[size_t(b) * 8 + size_t(k)]);
-    out[k] = sum / double(c->blocks);  // mean over blocks, ns
+  // Mean over the blocks that ran: a launch with a smaller grid (the hybrid
+  // route gives the switch part of the SMs) leaves the other records zero.
+  int ran = 0;
+  double sum[6] = {};
+  for (int b = 0; b < c->blocks; ++b) {
+    const unsigned long long* r = &rec[size_t(b) * 8];
+    if (!(r[0] | r[1] | r[2] | r[3] | r[4] | r[5])) continue;
+    ++ran;
+    for (int k = 0; k < 6; ++k) sum[k] += double(r[k]);
   }
-  return c->blocks;
+  for (int k = 0; k < 6; ++k) out[k] = ran ? sum[k] / double(ran) : 0.0;  // ns
+  return ran;
 }
 
 unsigned nvls_status(const int* devices, int n) {

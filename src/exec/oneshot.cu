@@ -1,0 +1,386 @@
+// Low-latency one-shot AllReduce over peer memory, synchronized inside the
+// kernel instead of by cross-device events.
+//
+// One kernel per rank, launched on the caller's own stream with nothing
+// around it. Block b of every rank's kernel:
+//   1. arrives: stores the call's epoch into word (b, r) of every peer's
+//      arrive table (P2P st.release.sys) -- this rank's stream has reached
+//      the call, so its whole input is ready;
+//   2. waits until every peer's block b arrived here (ld.acquire.sys polls
+//      of this GPU's own table);
+//   3. folds its share of the message (grid-stride 16/32-byte vectors) from
+//      all N inputs in rank order -- its own from HBM, the peers' over
+//      NVLink -- with fp32 accumulation, and stores only this rank's output;
+//   4. departs: stores the epoch into the peers' depart tables, and waits
+//      until every peer's block b departed, i.e. finished reading this
+//      rank's input; only then may this rank's stream go on (the caller may
+//      overwrite the input).
+// A call thus costs N kernel launches and no event traffic: the two
+// cross-device event fans of an event-ordered plan (every stream waiting on
+// every peer before and after) are what bound small messages otherwise.
+//
+// Calls on the same streams need no further ordering: a rank's next kernel
+// starts after its previous one, which ended only after every peer had
+// departed from it; arrive and depart use separate tables, so a peer still
+// waiting in its depart phase sees no stray arrival. When a call comes on
+// streams other than the previous call's (another stream of the same
+// clique, or a clique over the same GPUs), each rank's stream first waits
+// for the previous call's kernels on every GPU (one event per GPU,
+// recorded after every launch).
+//
+// Every wait is bounded by %globaltimer: on expiry the kernel writes the
+// status word (mapped host memory) and returns; the host then reports
+// ncclUnhandledCudaError and disables the route.
+//
+// Counterpart: the reference's direct peer-read route ArPeerRead
+// (shim/nccl_collectives_shim.cu:547-565), which is planned but never
+// selected, reads the peer's half with a kernel between event waits.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "exec/oneshot.h"
+#include "kernels/fold.cuh"
+
+namespace nb {
+
+namespace {
+
+using namespace kfold;
+
+struct OsArgs {
+  const void* src[kMaxRanks];         // every rank's input (peer pointers)
+  void* dst;                          // this rank's output
+  const void* dev_scalar[kMaxRanks];  // PreMulSum scalars in device memory, per rank
+  double scale[kMaxRanks];            // host PreMulSum scalars, per rank
+  unsigned* arrive_mine;              // this GPU's tables: [block][rank]
+  unsigned* depart_mine;
+  unsigned* arrive_peer[kMaxRanks];   // every rank's tables (peer pointers)
+  unsigned* depart_peer[kMaxRanks];
+  unsigned long long nvec;            // whole vectors
+  unsigned long long tail_elems;      // trailing elements
+  unsigned long long timeout_ns;
+  unsigned* status;                   // mapped host word: nonzero = a wait expired
+  unsigned epoch;
+  unsigned skew;                      // added to wait targets (bounded-wait test only)
+  int op, nranks, rank;
+};
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_rel(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Thread 0 publishes this block's step to every rank, then waits (bounded)
+// for every rank's block with the same index; the block then proceeds. False
+// when a wait expired.
+__device__ bool block_barrier(const OsArgs& a, unsigned* const* peer_tables, const unsigned* mine,
+                              volatile int* abort_flag) {
+  if (threadIdx.x == 0) {
+    // Everything this block did before (its loads of peer inputs) is ordered
+    // before the release stores.
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int q = 0; q < a.nranks; ++q)
+      st_rel(peer_tables[q] + blockIdx.x * unsigned(kMaxRanks) + unsigned(a.rank), a.epoch);
+    const unsigned target = a.epoch + a.skew;
+    const unsigned long long t0 = gtimer();
+    for (int q = 0; q < a.nranks && !*abort_flag; ++q) {
+      const unsigned* w = mine + blockIdx.x * unsigned(kMaxRanks) + unsigned(q);
+      while (int(ld_acq(w) - target) < 0) {
+        if (gtimer() - t0 > a.timeout_ns) {
+          *reinterpret_cast<volatile unsigned*>(a.status) = 1u;
+          __threadfence_system();
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return *abort_flag == 0;
+}
+
+template <int VB>
+struct Vec {
+  uint4 h[VB / 16];
+};
+
+template <int VB>
+__device__ __forceinline__ Vec<VB> ld_vec(const void* p) {
+  Vec<VB> v;
+  if constexpr (VB == 32) {
+    asm volatile("ld.global.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v.h[0].x), "=r"(v.h[0].y), "=r"(v.h[0].z), "=r"(v.h[0].w), "=r"(v.h[1].x),
+                   "=r"(v.h[1].y), "=r"(v.h[1].z), "=r"(v.h[1].w)
+                 : "l"(p)
+                 : "memory");
+  } else {
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.h[0].x), "=r"(v.h[0].y), "=r"(v.h[0].z), "=r"(v.h[0].w)
+                 : "l"(p)
+                 : "memory");
+  }
+  return v;
+}
+
+template <int VB>
+__device__ __forceinline__ void st_vec(void* p, const Vec<VB>& v) {
+  if constexpr (VB == 32) {
+    asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.h[0].x),
+                 "r"(v.h[0].y), "r"(v.h[0].z), "r"(v.h[0].w), "r"(v.h[1].x), "r"(v.h[1].y),
+                 "r"(v.h[1].z), "r"(v.h[1].w)
+                 : "memory");
+  } else {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.h[0].x), "r"(v.h[0].y),
+                 "r"(v.h[0].z), "r"(v.h[0].w)
+                 : "memory");
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ typename Acc<T>::type scalar_of(const OsArgs& a, int q) {
+  using A = typename Acc<T>::type;
+  if (a.dev_scalar[q]) return to_acc<T>(*static_cast<const T*>(a.dev_scalar[q]));
+  return A(a.scale[q]);
+}
+
+template <typename T, int NSRC, int VB>
+__global__ void __launch_bounds__(512) oneshot_kernel(const __grid_constant__ OsArgs a) {
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = 0;
+  __syncthreads();
+  if (!block_barrier(a, a.arrive_peer, a.arrive_mine, &abort_flag)) return;
+  using A = typename Acc<T>::type;
+  using V = Vec<VB>;
+  constexpr int U = (8 * 16 / VB / NSRC) > 0 ? (8 * 16 / VB / NSRC) : 1;  // ~8 16-byte loads in flight
+  A s[NSRC];
+#pragma unroll
+  for (int k = 0; k < NSRC; ++k) s[k] = scalar_of<T>(a, k);
+  const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+  for (unsigned long long base = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; base < a.nvec;
+       base += stride * U) {
+    V v[U][NSRC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const unsigned long long i = base + u * stride;
+      if (i < a.nvec) {
+#pragma unroll
+        for (int k = 0; k < NSRC; ++k) v[u][k] = ld_vec<VB>(static_cast<const char*>(a.src[k]) + i * VB);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const unsigned long long i = base + u * stride;
+      if (i < a.nvec) {
+        V out;
+#pragma unroll
+        for (int j = 0; j < VB / 16; ++j) {
+          uint4 part[NSRC];
+#pragma unroll
+          for (int k = 0; k < NSRC; ++k) part[k] = v[u][k].h[j];
+          out.h[j] = fold_vec<T, NSRC>(part, a.op, a.nranks, s);
+        }
+        st_vec<VB>(static_cast<char*>(a.dst) + i * VB, out);
+      }
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < a.tail_elems) {
+    const unsigned long long e = a.nvec * (VB / sizeof(T)) + threadIdx.x;
+    A acc = first<T>(static_cast<const T*>(a.src[0])[e], a.op, s[0]);
+#pragma unroll
+    for (int k = 1; k < NSRC; ++k) acc = combine<T>(acc, static_cast<const T*>(a.src[k])[e], a.op, s[k]);
+    static_cast<T*>(a.dst)[e] = finish<T>(acc, a.op, a.nranks);
+  }
+  __syncthreads();
+  block_barrier(a, a.depart_peer, a.depart_mine, &abort_flag);
+}
+
+using OsFn = void (*)(OsArgs);
+
+template <typename T, int VB>
+OsFn by_ranks(int n) {
+  switch (n) {
+    case 2: return oneshot_kernel<T, 2, VB>;
+    case 3: return oneshot_kernel<T, 3, VB>;
+    case 4: return oneshot_kernel<T, 4, VB>;
+    case 5: return oneshot_kernel<T, 5, VB>;
+    case 6: return oneshot_kernel<T, 6, VB>;
+    case 7: return oneshot_kernel<T, 7, VB>;
+    case 8: return oneshot_kernel<T, 8, VB>;
+    default: return nullptr;
+  }
+}
+
+OsFn pick(DType t, int n, bool wide) {
+  switch (t) {
+    case DType::F32: return wide ? by_ranks<float, 32>(n) : by_ranks<float, 16>(n);
+    case DType::F16: return wide ? by_ranks<__half, 32>(n) : by_ranks<__half, 16>(n);
+    case DType::BF16: return wide ? by_ranks<__nv_bfloat16, 32>(n) : by_ranks<__nv_bfloat16, 16>(n);
+    default: return nullptr;
+  }
+}
+
+constexpr int kThreads = 512;
+
+struct OsContext {
+  std::vector<int> devices;
+  std::vector<unsigned*> arrive, depart;  // per device: blocks x kMaxRanks words
+  std::vector<cudaEvent_t> done;          // per device: recorded after each launch there
+  std::vector<cudaStream_t> last;         // per device: the stream of the previous call
+  unsigned* status = nullptr;
+  unsigned* status_dev = nullptr;
+  unsigned epoch = 0;
+  int launched = 0;
+  bool fence = false;  // this call's streams differ from the previous call's
+  int blocks = 0;
+  bool broken = false;
+};
+
+std::mutex g_os_mu;
+std::vector<OsContext*> g_os;
+
+OsContext* find_os(const int* devices, int n) {
+  for (OsContext* c : g_os) {
+    if (int(c->devices.size()) != n) continue;
+    bool same = true;
+    for (int i = 0; i < n; ++i) same &= c->devices[size_t(i)] == devices[i];
+    if (same) return c;
+  }
+  return nullptr;
+}
+
+}  // namespace
+
+bool oneshot_supported(DType t, int n) { return pick(t, n, false) != nullptr; }
+
+bool oneshot_ensure(const int* devices, int n, std::string* why) {
+  std::lock_guard<std::mutex> lk(g_os_mu);
+  if (OsContext* c = find_os(devices, n)) {
+    if (c->broken && why) *why = "one-shot route disabled after a device timeout";
+    return !c->broken;
+  }
+  auto fail = [&](const char* what) {
+    if (why) *why = std::string("one-shot setup: ") + what;
+    cudaGetLastError();
+    return false;
+  };
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, devices[0]) != cudaSuccess)
+    return fail("SM count");
+  OsContext* c = new OsContext();
+  c->devices.assign(devices, devices + n);
+  c->blocks = sms;
+  const size_t words = size_t(sms) * kMaxRanks * sizeof(unsigned);
+  for (int i = 0; i < n; ++i) {
+    unsigned *ar = nullptr, *de = nullptr;
+    cudaEvent_t ev = nullptr;
+    if (cudaSetDevice(devices[i]) != cudaSuccess || cudaMalloc(&ar, words) != cudaSuccess ||
+        cudaMalloc(&de, words) != cudaSuccess || cudaMemset(ar, 0, words) != cudaSuccess ||
+        cudaMemset(de, 0, words) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {
+      delete c;
+      return fail("arrive/depart tables");
+    }
+    c->arrive.push_back(ar);
+    c->depart.push_back(de);
+    c->done.push_back(ev);
+    c->last.push_back(nullptr);
+  }
+  if (cudaHostAlloc(reinterpret_cast<void**>(&c->status), sizeof(unsigned),
+                    cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
+      cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->status_dev), c->status, 0) != cudaSuccess) {
+    delete c;
+    return fail("status word");
+  }
+  *c->status = 0;
+  g_os.push_back(c);
+  return true;
+}
+
+cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b, const Policy& p,
+                           cudaStream_t s) {
+  std::lock_guard<std::mutex> lk(g_os_mu);
+  OsContext* c = find_os(b.device, b.nranks);
+  if (!c || c->broken) return cudaErrorNotSupported;
+  const int n = b.nranks, r = op.stream.dev;
+  if (c->launched == 0) {
+    if (*static_cast<volatile unsigned*>(c->status) != 0) {
+      c->broken = true;  // a previous call timed out: the tables are no longer in step
+      return cudaErrorLaunchTimeout;
+    }
+    // A new call: its epoch, and whether any rank changed streams.
+    ++c->epoch;
+    c->fence = false;
+    for (int q = 0; q < n; ++q) c->fence = c->fence || (c->last[size_t(q)] && c->last[size_t(q)] != b.stream[q]);
+  }
+  const size_t es = elem_size(plan.desc.dtype);
+  const size_t bytes = plan.desc.bytes;
+  uintptr_t any = reinterpret_cast<uintptr_t>(b.recv[r]);
+  for (int q = 0; q < n; ++q) any |= reinterpret_cast<uintptr_t>(b.send[q]);
+  if (!es || bytes % es || any % 16) return cudaErrorInvalidValue;
+  const bool wide = any % 32 == 0;
+  const int vb = wide ? 32 : 16;
+  const OsFn fn = pick(plan.desc.dtype, n, wide);
+  if (!fn) return cudaErrorInvalidValue;
+  OsArgs a{};
+  for (int q = 0; q < n; ++q) {
+    a.src[q] = b.send[q];
+    a.dev_scalar[q] = b.dev_scalar[q];
+    a.scale[q] = b.fold.scalars[q];
+    a.arrive_peer[q] = c->arrive[size_t(q)];
+    a.depart_peer[q] = c->depart[size_t(q)];
+  }
+  a.dst = b.recv[r];
+  a.arrive_mine = c->arrive[size_t(r)];
+  a.depart_mine = c->depart[size_t(r)];
+  a.nvec = bytes / size_t(vb);
+  a.tail_elems = (bytes - a.nvec * size_t(vb)) / es;
+  a.timeout_ns = p.device_timeout_ns;
+  a.status = c->status_dev;
+  a.epoch = c->epoch;
+  a.skew = p.test_nvls_skew;
+  a.op = int(b.fold.op);
+  a.nranks = n;
+  a.rank = r;
+  // Enough blocks for ~8 16-byte loads per thread, at most one per SM; every
+  // rank uses the same grid (block b pairs with block b everywhere).
+  const size_t per_block = size_t(kThreads) * 16 * 8 / size_t(n);
+  const unsigned blocks =
+      unsigned(std::max<size_t>(1, std::min<size_t>((bytes + per_block - 1) / per_block, size_t(c->blocks))));
+  cudaError_t e = cudaSuccess;
+  if (c->fence)
+    for (int q = 0; q < n && e == cudaSuccess; ++q) e = cudaStreamWaitEvent(s, c->done[size_t(q)], 0);
+  if (e == cudaSuccess) {
+    void* argv[] = {&a};
+    // Cooperative: every block of the grid is resident at once, so a block
+    // waiting for its counterparts never keeps another block of its own
+    // kernel from running.
+    e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(fn), dim3(blocks), dim3(kThreads), argv, 0, s);
+  }
+  if (e == cudaSuccess) e = cudaEventRecord(c->done[size_t(r)], s);
+  c->last[size_t(r)] = s;
+  if (++c->launched == n) c->launched = 0;
+  return e;
+}
+
+unsigned oneshot_status(const int* devices, int n) {
+  std::lock_guard<std::mutex> lk(g_os_mu);
+  OsContext* c = find_os(devices, n);
+  return c && c->status ? *static_cast<volatile unsigned*>(c->status) : 0u;
+}
+
+}  // namespace nb

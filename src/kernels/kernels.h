@@ -37,6 +37,7 @@ struct CopyLaunch {
   size_t len[kMaxRanks] = {};
   int nseg = 0;
   bool local = false;  // every buffer is in the launching GPU's own device memory
+  bool prefer_tma = false;  // a large local copy runs on the TMA bulk engine
 };
 
 struct LaunchShape {

@@ -19,7 +19,8 @@ CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", 
          ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ar_nvls", "allreduce"),
          ("bc_nvls", "broadcast"), ("ag_nvls", "allgather"), ("rs_nvls", "reducescatter"),
          ("ag_push", "allgather"), ("bc_ring", "broadcast"), ("rs_push", "reducescatter"),
-         ("ar_push", "allreduce"), ("ar_hybrid", "allreduce")]
+         ("ar_push", "allreduce"), ("ar_hybrid", "allreduce"), ("ar_oneshot", "allreduce"),
+         ("rs_hybrid", "reducescatter")]
 
 
 def test_baseline_cpu_plumbing_config():

@@ -173,7 +173,9 @@ print(",".join(out), nc.shim.nb_poisoned(), nc.fallbacks(16), nc.fallbacks(17), 
 def test_host_fault_injection(spec, expect):
     """Error policy with host-side injected CUDA errors (nothing faults on the GPU)."""
     need_gpus(1)
-    env = dict(os.environ, NCCL_B200_FAULT=spec)
+    # No init-time tuning: the one-rank plan is then [record, copy kernel, ...],
+    # so op 1 is the kernel launch.
+    env = dict(os.environ, NCCL_B200_FAULT=spec, NCCL_B200_TUNE="0")
     r = subprocess.run([sys.executable, "-c", FAULT_CHILD.format(repo=REPO)], env=env,
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]

@@ -159,7 +159,8 @@ def test_single_local_copy(nbytes, src_off, dst_off):
 
 CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", "allgather"),
          ("bc_pull", "broadcast"), ("bc_scatter", "broadcast"), ("ar_staged", "allreduce"),
-         ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ag_push", "allgather")]
+         ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ag_push", "allgather"),
+         ("ar_oneshot", "allreduce")]
 
 
 @pytest.mark.parametrize("algo,kind", CASES)

@@ -132,3 +132,78 @@ def test_ring_bounded_wait_reports_timeout():
     assert calls[2] == "err1", calls
     assert calls[4] == "ok", calls
     assert seq[2] == "1"
+
+
+ORDER_CHILD = r"""
+import sys, ctypes as C, torch
+sys.path.insert(0, {repo!r})
+from scc26_nccl_shim_b200.parallel.nccl import Nccl, collective
+from scc26_nccl_shim_b200._core import ALGO
+from scc26_nccl_shim_b200.utils.data import exact
+n = {n}
+devs = list(range(n))
+nc = Nccl("interposer")
+cliques = [nc.comm_init_all(devs), nc.comm_init_all(devs)]
+# Two unordered streams per GPU (neither waits on the other).
+streams = [[torch.cuda.Stream(device=d) for d in devs] for _ in range(2)]
+count = (48 << 20) // 4  # 48 MiB per rank: long enough for calls to overlap
+kinds = ["broadcast", "allreduce", "reducescatter"]
+jobs = []
+# (a) two cliques over the same GPUs, (b) one clique on two unordered streams;
+# every call back to back, no host synchronization in between.
+for it in range(6):
+    for mode in ("two_cliques", "two_streams"):
+        comms = cliques[it % 2] if mode == "two_cliques" else cliques[0]
+        ss = streams[it % 2]
+        kind = kinds[it % 3]
+        slots = n if kind == "reducescatter" else 1
+        rc = count // n // 8 * 8 if kind == "reducescatter" else count
+        sends, recvs = [], []
+        for r, d in enumerate(devs):
+            with torch.cuda.stream(ss[r]):
+                sends.append(exact(r, rc * slots, it, 7 + len(jobs), torch.float32, n, f"cuda:{{d}}"))
+                recvs.append(torch.empty(rc, device=f"cuda:{{d}}"))
+        collective(nc, kind, sends, recvs, comms, [s.cuda_stream for s in ss], root=it % n)
+        jobs.append((kind, rc, sends, recvs, it % n))
+for d in devs:
+    torch.cuda.synchronize(d)
+bad = 0
+for kind, rc, sends, recvs, root in jobs:
+    ins = [s.to("cuda:0") for s in sends]
+    for r in range(n):
+        if kind == "broadcast":
+            ref = ins[root]
+        elif kind == "allreduce":
+            ref = ins[0].clone()
+            for x in ins[1:]:
+                ref = ref + x
+        else:
+            ref = ins[0][r * rc:(r + 1) * rc].clone()
+            for x in ins[1:]:
+                ref = ref + x[r * rc:(r + 1) * rc]
+        bad += 0 if torch.equal(recvs[r].to("cuda:0"), ref) else 1
+arr = (C.c_int * n)(*devs)
+st = nc.shim.nb_ring_status(arr, n) | nc.shim.nb_pushred_status(arr, n)
+print("RESULT", bad, st, nc.shim.nb_poisoned(), nc.custom_calls(ALGO["bc_ring"]),
+      nc.custom_calls(ALGO["ar_push"]), nc.custom_calls(ALGO["rs_push"]))
+"""
+
+
+@pytest.mark.parametrize("n", [2, 3])
+def test_gang_calls_ordered_across_streams_and_cliques(n):
+    """The push chain and the push-reduce engine keep scratch, progress words
+    and an epoch per device set. Calls from two cliques over the same GPUs,
+    and calls of one clique on two unordered streams, issued back to back
+    without host synchronization, must not overlap on those engines: every
+    result bit-exact, no wait expired, nothing poisoned."""
+    need_gpus(n)
+    env = dict(os.environ, NCCL_B200_ALGO="bc=ring,ar=push,rs=push", NCCL_B200_TUNE="0",
+               NCCL_B200_FIRST_PASS="0", NCCL_B200_AR_MIN="1K", NCCL_B200_RS_MIN="1K",
+               NCCL_B200_BC_MIN="1K", NCCL_B200_TIMEOUT_MS="5000")
+    r = subprocess.run([sys.executable, "-c", ORDER_CHILD.format(repo=REPO, n=n)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    bad, status, poisoned, ring, arp, rsp = map(int, line[1:])
+    assert (bad, status, poisoned) == (0, 0, 0), line
+    assert ring >= 4 and arp >= 4 and rsp >= 4, line
