@@ -314,9 +314,10 @@ def worker(args) -> int:
 
 
 def nvls_trace(nc, devs, kind, reset_only=False, steps=1):
-    """With NCCL_B200_NVLS_TRACE=1: the NVLS kernels' per-block phase times
-    (mean over blocks, per call) of every rank, to stderr. Read outside the
-    timed region (it synchronizes the devices)."""
+    """With NCCL_B200_NVLS_TRACE=1: the in-kernel-synchronized engines'
+    per-block phase times (mean over blocks, per call) of every rank, to
+    stderr: the NVLS kernels, the push-reduce kernel and the Broadcast push
+    chain. Read outside the timed region (it synchronizes the devices)."""
     import ctypes as C
     if not os.environ.get("NCCL_B200_NVLS_TRACE") or nc.shim is None or \
             not hasattr(nc.shim, "nb_nvls_trace"):
@@ -326,12 +327,23 @@ def nvls_trace(nc, devs, kind, reset_only=False, steps=1):
     for r in range(n):
         out = (C.c_double * 6)()
         blocks = nc.shim.nb_nvls_trace(arr, n, r, out, 1)
-        if reset_only or blocks <= 0:
-            continue
-        ms = [v / 1e6 / steps for v in out]
-        sys.stderr.write(f"nvls_trace {kind} rank={r} blocks={blocks} per_call_ms mover_busy={ms[0]:.3f} "
-                         f"mover_wait={ms[1]:.3f} copier_busy={ms[2]:.3f} copier_wait={ms[3]:.3f} "
-                         f"mover_total={ms[4]:.3f} copier_total={ms[5]:.3f}\n")
+        if not reset_only and blocks > 0:
+            ms = [v / 1e6 / steps for v in out]
+            sys.stderr.write(f"nvls_trace {kind} rank={r} blocks={blocks} per_call_ms mover_busy={ms[0]:.3f} "
+                             f"mover_wait={ms[1]:.3f} copier_busy={ms[2]:.3f} copier_wait={ms[3]:.3f} "
+                             f"mover_total={ms[4]:.3f} copier_total={ms[5]:.3f}\n")
+        out4 = (C.c_double * 4)()
+        blocks = nc.shim.nb_pushred_trace(arr, n, r, out4, 1)
+        if not reset_only and blocks > 0:
+            ms = [v / 1e6 / steps for v in out4]
+            sys.stderr.write(f"pushred_trace {kind} rank={r} blocks={blocks} per_call_ms sender_wait={ms[0]:.3f} "
+                             f"sender_total={ms[1]:.3f} reducer_wait={ms[2]:.3f} reducer_total={ms[3]:.3f}\n")
+        out2 = (C.c_double * 2)()
+        blocks = nc.shim.nb_ring_trace(arr, n, r, out2, 1)
+        if not reset_only and blocks > 0:
+            ms = [v / 1e6 / steps for v in out2]
+            sys.stderr.write(f"ring_trace {kind} rank={r} blocks={blocks} per_call_ms wait={ms[0]:.3f} "
+                             f"total={ms[1]:.3f}\n")
 
 
 def end_to_end(torch, nc, comms, sends, recvs, streams, devs, count, args):

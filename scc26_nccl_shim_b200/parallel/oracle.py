@@ -15,7 +15,8 @@ src/core/calib_model.cc):
   "size": N slots for AllGather/ReduceScatter) is at most the cap
   (NCCL_B200_MAX_BYTES, 8 GiB); the library and the kind are enabled; the
   logical message reaches the kind's threshold (NCCL_B200_{AR,AG,RS,BC}_MIN,
-  32 MiB) and is not empty; a ReduceScatter slot is a multiple of 16 bytes.
+  32 MiB, or, when unset, the crossover with NCCL measured at init and kept
+  in the calibration record) and is not empty; a ReduceScatter slot is a multiple of 16 bytes.
 * Route: a forced route (NCCL_B200_ALGO) when it is valid for the call; else
   the tuned route of the message's size band (tiny, small or large, from a
   calibration cache file) when valid; else the static rule (AllReduce: NVLS
@@ -92,6 +93,7 @@ class Rules:
         g = env.get
         self.enabled = not parse_bool(g("NCCL_B200_DISABLE"))
         self.kind_enabled = {k: parse_bool(g("NCCL_B200_" + v)) is not False for k, v in KIND_ENV.items()}
+        self.min_set = {k: parse_size(g(f"NCCL_B200_{v}_MIN")) is not None for k, v in KEYS.items()}
         self.min_bytes = {k: parse_size(g(f"NCCL_B200_{v}_MIN")) or 32 * MIB for k, v in KEYS.items()}
         self.max_bytes = parse_size(g("NCCL_B200_MAX_BYTES")) or 8 * GIB
         nv = g("NCCL_B200_NVLS", "auto")
@@ -217,6 +219,13 @@ def expected_route(kind: str, dtype: str, op: str, count: int, n: int, *, inplac
                    rules: Rules | None = None, calib: dict | None = None) -> str:
     """"nccl" when the call falls back, else the route that runs it."""
     rules = rules or Rules()
+    engage = int((calib or {}).get(f"engage{KIND_INDEX[kind]}", 0))
+    if engage > 0 and not rules.min_set[kind] and n > 1:
+        # The measured crossover with NCCL lowers an unset threshold.
+        import copy
+        rules = copy.copy(rules)
+        rules.min_bytes = dict(rules.min_bytes)
+        rules.min_bytes[kind] = min(rules.min_bytes[kind], engage * KIB)
     if gate_message(kind, dtype, op, count, n, rules) != "None":
         return "nccl"
     logical = logical_bytes(kind, dtype, count, n)

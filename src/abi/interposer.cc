@@ -28,6 +28,7 @@
 #include "core/plan.h"
 #include "exec/calib.h"
 #include "exec/nvls.h"
+#include "exec/oneshot.h"
 #include "exec/pushred.h"
 #include "kernels/kernels.h"
 #include "exec/ring.h"
@@ -85,10 +86,19 @@ Runtime& rt() {
       std::fprintf(stderr, "[nccl-b200] ignoring malformed NCCL_B200_FAULT=%s\n", x->policy.fault.c_str());
     x->exec.set_policy(x->policy);
     x->exec.set_summary(&x->summary);
+    for (int n = 0; n <= kMaxRanks; ++n) x->eff[n] = x->policy;
     return x;
   }();
   static ExitSummary exit_summary;
   return *r;
+}
+
+void Runtime::refresh_policy(int n) {
+  if (n < 1 || n > kMaxRanks) return;
+  eff[n] = policy;
+  for (int k = 0; k < int(Kind::Count); ++k)
+    if (!policy.min_bytes_set[k] && calib[n].engage_kib[k] > 0)
+      eff[n].min_bytes[k] = std::min(policy.min_bytes[k], size_t(calib[n].engage_kib[k]) << 10);
 }
 
 void* real_symbol(const char* name) {
@@ -182,6 +192,7 @@ void prewarm(const int* devices, int n) {
       calib_save(r.policy.calib_cache, key, c);
     }
     r.calib[n] = c;
+    r.refresh_policy(n);
     if (c.valid) {
       char line[320];
       std::snprintf(line, sizeof line, "routes n=%d allreduce=%s allgather=%s(ce=%d) reducescatter=%s "
@@ -226,6 +237,8 @@ void prewarm(const int* devices, int n) {
 
 namespace {
 
+Outcome run_clique(std::vector<Call>& calls, Reason& reason, bool probe);
+
 // The GroupBackend the group state machine drives in the library.
 class RealBackend final : public GroupBackend {
  public:
@@ -258,8 +271,8 @@ class RealBackend final : public GroupBackend {
            n.CommUserRank(comm, &c.desc.rank) == ncclSuccess &&
            n.CommCount(comm, &c.desc.nranks) == ncclSuccess;
   }
-  const Policy& policy() override { return rt().policy; }
-  Outcome run(std::vector<Call>& calls, Reason& reason) override;
+  const Policy& policy(int nranks) override { return rt().policy_for(nranks); }
+  Outcome run(std::vector<Call>& calls, Reason& reason) override { return run_clique(calls, reason, false); }
 };
 
 RealBackend g_backend;
@@ -290,7 +303,10 @@ bool runtime_checks(Runtime& r, const std::vector<Call>& calls, const CliqueInfo
   return true;
 }
 
-Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
+// Gate, check, plan and execute one clique set. `probe`: a measurement at
+// init (measure_crossover), which counts nothing in the summary and leaves
+// the first-pass rule alone.
+Outcome run_clique(std::vector<Call>& calls, Reason& reason, bool probe) {
   Runtime& r = rt();
   std::lock_guard<std::mutex> lk(r.exec_mu);
   if (!r.poisoned && tma_copy_status() != 0) {
@@ -303,7 +319,7 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
   CliqueState st;
   st.poisoned = r.poisoned;
   st.nccl_supported = r.nccl_supported;
-  st.first_pass_done = r.first_pass_done;
+  st.first_pass_done = r.first_pass_done || probe;
   std::vector<void*> comms;
   std::vector<CallDesc> descs;
   for (const Call& c : calls) {
@@ -327,9 +343,9 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
       for (int k = 0; k < int(Kind::Count); ++k)
         st.preferred[k] = tuned_route(r.calib[info.nranks], k, logical_bytes(descs[0]));
   }
-  const CliqueDecision d = gate_clique(descs, st, r.policy);
+  const CliqueDecision d = gate_clique(descs, st, r.policy_for(int(descs.size())));
   reason = d.reason;
-  if (d.reason == Reason::FirstPass) r.first_pass_done = true;
+  if (d.reason == Reason::FirstPass && !probe) r.first_pass_done = true;
   if (d.algo == Algo::Fallback) return Outcome::Fallback;
   reason = Reason::RuntimeUnsupported;
   if (!runtime_checks(r, calls, info)) return Outcome::Fallback;
@@ -388,7 +404,8 @@ Outcome RealBackend::run(std::vector<Call>& calls, Reason& reason) {
     return Outcome::Error;
   }
   if (status == ExecStatus::Ok) {
-    r.summary.count_custom(plan.algo, logical_bytes(descs[0]), n, plan.sm_bytes, plan.ce_bytes,
+    if (!probe)
+      r.summary.count_custom(plan.algo, logical_bytes(descs[0]), n, plan.sm_bytes, plan.ce_bytes,
                            plan.host_bytes);
     return Outcome::Handled;
   }
@@ -426,6 +443,30 @@ Call make_call(Kind kind, const void* sendbuff, void* recvbuff, size_t count, nc
   c.desc.recv = reinterpret_cast<uintptr_t>(recvbuff);
   c.desc.root = root;
   return c;
+}
+
+// Device time (max over GPUs, ms per call) of `reps` back-to-back calls of fn.
+template <typename Fn>
+double time_calls(const int* devices, int n, cudaStream_t* streams, cudaEvent_t* e0, cudaEvent_t* e1,
+                  int reps, Fn fn) {
+  for (int i = 0; i < n; ++i) {
+    cudaSetDevice(devices[i]);
+    cudaEventRecord(e0[i], streams[i]);
+  }
+  for (int k = 0; k < reps; ++k)
+    if (!fn()) return -1;
+  double worst = 0;
+  for (int i = 0; i < n; ++i) {
+    cudaSetDevice(devices[i]);
+    cudaEventRecord(e1[i], streams[i]);
+  }
+  for (int i = 0; i < n; ++i) {
+    float ms = 0;
+    if (cudaEventSynchronize(e1[i]) != cudaSuccess || cudaEventElapsedTime(&ms, e0[i], e1[i]) != cudaSuccess)
+      return -1;
+    worst = std::max(worst, double(ms));
+  }
+  return worst / reps;
 }
 
 bool blocking_configuration(const ncclConfig_t* config) {
@@ -512,9 +553,124 @@ void register_initializations() {
   int caller = -1;
   if (r.cliques.lookup(by_rank[0], &info) && cudaGetDevice(&caller) == cudaSuccess) {
     prewarm(info.devices, n);
+    measure_crossover(reinterpret_cast<void* const*>(by_rank), info.devices, n);
     cudaSetDevice(caller);
   }
 }
+
+}  // namespace
+
+void measure_crossover(void* const* comms_by_rank, const int* devices, int n) {
+  Runtime& r = rt();
+  if (n < 2 || n > kMaxRanks || !r.policy.tune || r.crossover_tried[n] || !r.calib[n].valid || r.poisoned)
+    return;
+  r.crossover_tried[n] = true;
+  CalibResult& cal = r.calib[n];
+  bool cached = false;
+  for (int k = 0; k < int(Kind::Count); ++k) cached = cached || cal.engage_kib[k] > 0;
+  if (cached) {  // loaded with the calibration
+    r.refresh_policy(n);
+    return;
+  }
+  static const size_t kLadder[] = {64 << 10, 256 << 10, 1 << 20, 4 << 20, 16 << 20};
+  constexpr int kSteps = int(sizeof(kLadder) / sizeof(kLadder[0]));
+  const size_t top = kLadder[kSteps - 1];
+  std::vector<void*> send(size_t(n), nullptr), recv(size_t(n), nullptr);
+  std::vector<cudaStream_t> streams(size_t(n), nullptr);
+  std::vector<cudaEvent_t> e0(size_t(n), nullptr), e1(size_t(n), nullptr);
+  bool ok = true;
+  for (int i = 0; i < n && ok; ++i)
+    ok = cudaSetDevice(devices[i]) == cudaSuccess && cudaMalloc(&send[size_t(i)], top) == cudaSuccess &&
+         cudaMalloc(&recv[size_t(i)], top) == cudaSuccess && cudaMemset(send[size_t(i)], 0, top) == cudaSuccess &&
+         cudaStreamCreateWithFlags(&streams[size_t(i)], cudaStreamNonBlocking) == cudaSuccess &&
+         cudaEventCreate(&e0[size_t(i)]) == cudaSuccess && cudaEventCreate(&e1[size_t(i)]) == cudaSuccess;
+  const RealNccl& nccl = r.real;
+  for (int k = 0; ok && k < int(Kind::Count); ++k) {
+    if (r.policy.min_bytes_set[k]) continue;
+    const Kind kind = Kind(k);
+    const bool slots = kind == Kind::AllGather || kind == Kind::ReduceScatter;
+    double ours[kSteps], base[kSteps];
+    int measured = 0;
+    for (int j = 0; j < kSteps && kLadder[j] < r.policy.min_bytes[k]; ++j, ++measured) {
+      const size_t logical = kLadder[j];
+      const size_t count = (slots ? logical / size_t(n) : logical) / 4;
+      auto custom = [&]() {
+        std::vector<Call> calls;
+        for (int q = 0; q < n; ++q) {
+          Call c = make_call(kind, send[size_t(q)], recv[size_t(q)], count, ncclFloat, ncclSum, 0,
+                             static_cast<ncclComm_t>(comms_by_rank[q]), streams[size_t(q)]);
+          c.desc.device = devices[q];
+          c.desc.rank = q;
+          c.desc.nranks = n;
+          calls.push_back(c);
+        }
+        Reason why = Reason::None;
+        return run_clique(calls, why, true) == Outcome::Handled;
+      };
+      auto stock = [&]() {
+        if (nccl.GroupStart() != ncclSuccess) return false;
+        bool good = true;
+        for (int q = 0; q < n; ++q) {
+          const auto comm = static_cast<ncclComm_t>(comms_by_rank[q]);
+          void* sb = send[size_t(q)];
+          void* rb = recv[size_t(q)];
+          const cudaStream_t st = streams[size_t(q)];
+          ncclResult_t res;
+          switch (kind) {
+            case Kind::AllGather: res = nccl.AllGather(sb, rb, count, ncclFloat, comm, st); break;
+            case Kind::ReduceScatter: res = nccl.ReduceScatter(sb, rb, count, ncclFloat, ncclSum, comm, st); break;
+            case Kind::Broadcast: res = nccl.Broadcast(sb, rb, count, ncclFloat, 0, comm, st); break;
+            default: res = nccl.AllReduce(sb, rb, count, ncclFloat, ncclSum, comm, st); break;
+          }
+          good = good && res == ncclSuccess;
+        }
+        return nccl.GroupEnd() == ncclSuccess && good;
+      };
+      // Warm both (NCCL connects lazily per algorithm), then time 10 calls each.
+      ours[j] = time_calls(devices, n, streams.data(), e0.data(), e1.data(), 3, custom);
+      base[j] = time_calls(devices, n, streams.data(), e0.data(), e1.data(), 3, stock);
+      ours[j] = time_calls(devices, n, streams.data(), e0.data(), e1.data(), 10, custom);
+      base[j] = time_calls(devices, n, streams.data(), e0.data(), e1.data(), 10, stock);
+      if (ours[j] < 0 || base[j] < 0) {
+        ok = false;
+        break;
+      }
+    }
+    if (!ok || measured == 0) break;
+    // The smallest ladder size from which the routes win at every larger
+    // measured size (the threshold itself always engages).
+    int from = measured;
+    while (from > 0 && ours[from - 1] <= base[from - 1]) --from;
+    std::string line = std::string("crossover n=") + std::to_string(n) + " " + kind_name(kind) + ":";
+    for (int j = 0; j < measured; ++j) {
+      char cell[96];
+      std::snprintf(cell, sizeof cell, " %zuKiB ours=%.1fus nccl=%.1fus", kLadder[j] >> 10, ours[j] * 1e3,
+                    base[j] * 1e3);
+      line += cell;
+    }
+    if (from < measured) {
+      cal.engage_kib[k] = int(kLadder[from] >> 10);
+      line += " -> engage from " + std::to_string(kLadder[from] >> 10) + " KiB";
+    } else {
+      line += " -> keep the threshold";
+    }
+    r.summary.note(line);
+  }
+  for (int i = 0; i < n; ++i) {
+    if (cudaSetDevice(devices[i]) != cudaSuccess) continue;
+    cudaDeviceSynchronize();
+    if (send[size_t(i)]) cudaFree(send[size_t(i)]);
+    if (recv[size_t(i)]) cudaFree(recv[size_t(i)]);
+    if (streams[size_t(i)]) cudaStreamDestroy(streams[size_t(i)]);
+    if (e0[size_t(i)]) cudaEventDestroy(e0[size_t(i)]);
+    if (e1[size_t(i)]) cudaEventDestroy(e1[size_t(i)]);
+  }
+  cudaGetLastError();
+  r.refresh_policy(n);
+  if (!r.policy.calib_cache.empty()) calib_save(r.policy.calib_cache, calib_cache_key(devices, n), cal);
+}
+
+namespace {
 
 int force_passthrough(bool initialization = false) {
   return g_machine.force_passthrough(g_group, initialization);
@@ -582,7 +738,13 @@ ncclResult_t ncclCommInitAll(ncclComm_t* comms, int ndev, const int* devlist) {
   ++g_init_all_depth;
   const ncclResult_t res = r.real.CommInitAll(comms, ndev, devlist);
   --g_init_all_depth;
-  if (res == ncclSuccess && clique && restored && comms) register_clique(comms, ndev);
+  if (res == ncclSuccess && clique && restored && comms && register_clique(comms, ndev)) {
+    int caller = -1;
+    if (cudaGetDevice(&caller) == cudaSuccess) {
+      measure_crossover(reinterpret_cast<void* const*>(comms), devs, ndev);
+      restored = cudaSetDevice(caller) == cudaSuccess;
+    }
+  }
   if (res == ncclSuccess && !restored) return ncclUnhandledCudaError;
   return res;
 }
@@ -782,8 +944,15 @@ int nb_nvls_supported(const int* devices, int n) { return nvls_supported(devices
 unsigned nb_nvls_status(const int* devices, int n) { return nvls_status(devices, n); }
 unsigned nb_ring_status(const int* devices, int n) { return ring_status(devices, n); }
 unsigned nb_pushred_status(const int* devices, int n) { return pushred_status(devices, n); }
+unsigned nb_oneshot_status(const int* devices, int n) { return oneshot_status(devices, n); }
 int nb_nvls_trace(const int* devices, int n, int rank, double* out6, int reset) {
   return nvls_trace_read(devices, n, rank, out6, reset != 0);
+}
+int nb_pushred_trace(const int* devices, int n, int rank, double* out4, int reset) {
+  return pushred_trace_read(devices, n, rank, out4, reset != 0);
+}
+int nb_ring_trace(const int* devices, int n, int rank, double* out2, int reset) {
+  return ring_trace_read(devices, n, rank, out2, reset != 0);
 }
 
 // The tuned route of a collective kind on cliques of n ranks (-1 untuned).

@@ -52,6 +52,12 @@ struct Runtime {
   // prewarm of a clique of that size, or loaded from the cache).
   CalibResult calib[kMaxRanks + 1];
   bool calib_tried[kMaxRanks + 1] = {};
+  bool crossover_tried[kMaxRanks + 1] = {};
+  // The policy in force per clique size: `policy` with the thresholds the
+  // environment left unset replaced by the measured crossover with NCCL.
+  Policy eff[kMaxRanks + 1];
+  const Policy& policy_for(int n) const { return n >= 1 && n <= kMaxRanks ? eff[n] : policy; }
+  void refresh_policy(int n);
 };
 
 // Time every candidate route on the clique's GPUs at `bytes` and record the
@@ -63,6 +69,10 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out);
 void tune_single(int device, size_t bytes, CalibResult* out);
 
 Runtime& rt();
+// After the communicators of a clique exist: time the tuned routes against
+// libnccl on a size ladder below the thresholds and lower each kind's
+// threshold to the size from which the routes win (interposer.cc).
+void measure_crossover(void* const* comms_by_rank, const int* devices, int n);
 // Resolve the real libnccl once (dlsym RTLD_NEXT, then the loaded
 // libnccl.so.2, then NCCL_B200_REAL_NCCL or libnccl.so.2 by name); aborts
 // with a message if a required symbol is missing.

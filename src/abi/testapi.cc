@@ -43,6 +43,7 @@ int nb_emu_copy(const void* const* srcs, void* const* dsts, const uint64_t* lens
   CopyLaunch c;
   c.nseg = nseg;
   c.local = true;  // virtual ranks: every buffer is on the current GPU
+  c.prefer_tma = rt().policy.local_copy_tma;
   size_t total = 0;
   for (int i = 0; i < nseg && i < kMaxRanks; ++i) {
     c.src[i] = srcs[i];

@@ -161,10 +161,11 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
   const bool nvls = r.policy.nvls != NvlsMode::Off && nvls_supported(devices, n);
   // Two tuning sizes: the large one (the policy's) and a small one; the
   // small choice serves messages below their geometric mean.
-  // A third, tiny size picks among the SM routes for small messages.
+  // A third, tiny size (1 MiB) picks among the SM routes for small messages,
+  // where launch and synchronization latency outweigh the bytes.
   const size_t unit = size_t(n) * 256;
   const size_t small_bytes = std::max(unit, (size_t(64) << 20) / unit * unit);
-  const size_t tiny_bytes = std::max(unit, (size_t(4) << 20) / unit * unit);
+  const size_t tiny_bytes = std::max(unit, (size_t(1) << 20) / unit * unit);
   const bool two_sizes = bytes >= 4 * small_bytes;
   for (int pass = 0; pass < (two_sizes ? 3 : 1); ++pass) {
     const size_t size = pass == 0 ? bytes : pass == 1 ? small_bytes : tiny_bytes;

@@ -109,9 +109,9 @@ std::string calib_to_json(const CalibResult& c, const std::string& key) {
   for (int k = 0; k < 4; ++k) {
     std::snprintf(buf, sizeof buf,
                   ", \"tpref%d\": %d, \"split%d\": %d, \"sblocks%d\": %d, \"ssplit%d\": %d, "
-                  "\"ssblocks%d\": %d",
+                  "\"ssblocks%d\": %d, \"engage%d\": %d",
                   k, c.tiny_pref[k], k, c.split_ppm[k], k, c.split_blocks[k], k, c.small_split_ppm[k], k,
-                  c.small_split_blocks[k]);
+                  c.small_split_blocks[k], k, c.engage_kib[k]);
     s += buf;
   }
   return s + "}\n";
@@ -166,6 +166,7 @@ bool calib_from_json(const std::string& text, const std::string& key, CalibResul
       if (json_number(text, ("sblocks" + K).c_str(), &v)) c.split_blocks[k] = int(v);
       if (json_number(text, ("ssplit" + K).c_str(), &v)) c.small_split_ppm[k] = int(v);
       if (json_number(text, ("ssblocks" + K).c_str(), &v)) c.small_split_blocks[k] = int(v);
+      if (json_number(text, ("engage" + K).c_str(), &v)) c.engage_kib[k] = int(v);
     }
   }
   c.valid = true;

@@ -53,6 +53,10 @@ struct CalibResult {
   // pipelines, no copy-engine or host shares): used below tiny_below_kib.
   int tiny_pref[4] = {0, 0, 0, 0};
   int tiny_below_kib = 0;
+  // Measured crossover with NCCL (after the communicators exist): the
+  // smallest logical size, in KiB, from which the tuned routes were faster
+  // at every size of the ladder up to the policy threshold (0 = not measured).
+  int engage_kib[4] = {0, 0, 0, 0};
 };
 
 // Whether a message of `logical` bytes takes the small-size choice.

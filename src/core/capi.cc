@@ -449,7 +449,7 @@ class FakeBackend final : public GroupBackend {
     c.desc.nranks = n_;
     return true;
   }
-  const Policy& policy() override { return policy_; }
+  const Policy& policy(int) override { return policy_; }
   Outcome run(std::vector<Call>& calls, Reason& reason) override {
     // Like the real clique gate: one call per rank, all of one kind.
     unsigned ranks = 0;

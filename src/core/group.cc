@@ -47,7 +47,7 @@ Reason GroupMachine::decide_receive(const GroupState& g, Call& c) {
   const bool extends = size_t(c.desc.nranks) > g.pending.size() &&
                        (!head || c.desc.nranks == head->desc.nranks);
   if (!extends) return Reason::GroupShape;
-  return gate_call(c.desc, b_.policy());
+  return gate_call(c.desc, b_.policy(c.desc.nranks));
 }
 
 // The effects of the model's Flush: pending calls, then `arriving` (when
@@ -82,7 +82,7 @@ bool GroupMachine::decide_end(const GroupState& g) const {
 // Outside any group there is nothing to buffer: a one-rank clique that
 // passes the call gate runs at once, everything else goes to libnccl.
 int GroupMachine::ungrouped(Call& c) {
-  if (!b_.query(c) || c.desc.nranks != 1 || gate_call(c.desc, b_.policy()) != Reason::None)
+  if (!b_.query(c) || c.desc.nranks != 1 || gate_call(c.desc, b_.policy(1)) != Reason::None)
     return b_.forward(c, Reason::NotGrouped);
   std::vector<Call> single{c};
   Reason why = Reason::NotGrouped;

@@ -73,7 +73,9 @@ class GroupBackend {
   virtual int forward(const Call& c, Reason reason) = 0;
   // Fill desc.device / rank / nranks from the communicator.
   virtual bool query(Call& c) = 0;
-  virtual const Policy& policy() = 0;
+  // The routing policy in force for cliques of `nranks` (thresholds may be
+  // the measured crossover with NCCL for that size).
+  virtual const Policy& policy(int nranks) = 0;
   // Gate, plan and execute a complete clique set.
   virtual Outcome run(std::vector<Call>& calls, Reason& reason) = 0;
 };

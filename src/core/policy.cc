@@ -87,7 +87,10 @@ Policy policy_from_env(const EnvLookup& env) {
                             "NCCL_B200_BC_MIN"};
   for (size_t k = 0; k < size_t(Kind::Count); ++k) {
     if (parse_bool(env(kind_keys[k]), &b)) p.kind_enabled[k] = b;
-    if (parse_size(env(min_keys[k]), &z)) p.min_bytes[k] = z;
+    if (parse_size(env(min_keys[k]), &z)) {
+      p.min_bytes[k] = z;
+      p.min_bytes_set[k] = true;
+    }
   }
   if (parse_size(env("NCCL_B200_MAX_BYTES"), &z)) p.max_message_bytes = z;
   if (parse_bool(env("NCCL_B200_FIRST_PASS"), &b)) p.first_pass = b;

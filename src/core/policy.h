@@ -23,6 +23,9 @@ struct Policy {
   bool kind_enabled[size_t(Kind::Count)] = {true, true, true, true};
   // Logical-size thresholds (nccl-tests "size": N slots for AG/RS).
   size_t min_bytes[size_t(Kind::Count)] = {32 * kMiB, 32 * kMiB, 32 * kMiB, 32 * kMiB};
+  // Set when the environment gave the threshold; otherwise the threshold of
+  // a clique size may be lowered to the measured crossover with NCCL.
+  bool min_bytes_set[size_t(Kind::Count)] = {false, false, false, false};
   size_t max_message_bytes = size_t(8) << 30;  // enforced logical message cap
   bool first_pass = true;           // first eligible clique call runs on NCCL
   NvlsMode nvls = NvlsMode::Auto;

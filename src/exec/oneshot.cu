@@ -356,11 +356,12 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
   a.op = int(b.fold.op);
   a.nranks = n;
   a.rank = r;
-  // Enough blocks for ~8 16-byte loads per thread, at most one per SM; every
-  // rank uses the same grid (block b pairs with block b everywhere).
-  const size_t per_block = size_t(kThreads) * 16 * 8 / size_t(n);
+  // One block per 8 KiB of output, at least 8 and at most one per SM: the
+  // peers' inputs come over NVLink, and each SM sustains only a share of the
+  // link rate, so even a 1 MiB message is spread over 128 SMs. Every rank
+  // uses the same grid (block b pairs with block b everywhere).
   const unsigned blocks =
-      unsigned(std::max<size_t>(1, std::min<size_t>((bytes + per_block - 1) / per_block, size_t(c->blocks))));
+      unsigned(std::min<size_t>(std::max<size_t>(8, (bytes + 8191) / 8192), size_t(c->blocks)));
   cudaError_t e = cudaSuccess;
   if (c->fence)
     for (int q = 0; q < n && e == cudaSuccess; ++q) e = cudaStreamWaitEvent(s, c->done[size_t(q)], 0);

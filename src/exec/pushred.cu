@@ -61,6 +61,9 @@ struct PrArgs {
   unsigned base, skew;
   unsigned rounds;
   int nranks, rank, op, allreduce, senders;  // senders: threads of the sender group
+  // Optional phase timing (NCCL_B200_NVLS_TRACE): per block, ns accumulated
+  // over calls: {sender waiting, sender total, reducer waiting, reducer total}.
+  unsigned long long* trace;
 };
 
 __device__ __forceinline__ unsigned long long timer_ns() {
@@ -137,6 +140,20 @@ __global__ void __launch_bounds__(512, 1) pushred_kernel(const __grid_constant__
   const unsigned nt = sender ? a.senders : blockDim.x - a.senders;
   const int gid = sender ? 1 : 2;
   volatile int* abort = &abort_flag;
+  // Phase timing, kept by each group's leader.
+  const unsigned long long t_start = a.trace && t == 0 ? timer_ns() : 0;
+  unsigned long long waited = 0;
+  auto timed_wait = [&](const unsigned* const* w, int c, unsigned v) {
+    const unsigned long long w0 = a.trace ? timer_ns() : 0;
+    leader_wait(a, w, c, v, abort);
+    if (a.trace) waited += timer_ns() - w0;
+  };
+  auto trace_out = [&](int slot) {
+    if (!a.trace || t != 0) return;
+    unsigned long long* rec = a.trace + 4ull * blockIdx.x + slot;
+    atomicAdd(rec, waited);
+    atomicAdd(rec + 1, timer_ns() - t_start);
+  };
   if (sender) {
     for (unsigned j = 0; j < a.rounds; ++j) {
       const unsigned long long k = (unsigned long long)j * gridDim.x + blockIdx.x;
@@ -146,7 +163,7 @@ __global__ void __launch_bounds__(512, 1) pushred_kernel(const __grid_constant__
           const unsigned* w[kMaxRanks];
           int c = 0;
           for (int i = 1; i < N; ++i) w[c++] = a.consumed[r] + flag_idx((r + i) % N);
-          leader_wait(a, w, c, a.base + j - kDepth + 1, abort);
+          timed_wait(w, c, a.base + j - kDepth + 1);
         }
         bar(gid, nt);
         if (*abort) return;
@@ -169,6 +186,7 @@ __global__ void __launch_bounds__(512, 1) pushred_kernel(const __grid_constant__
         for (int i = 1; i < N; ++i) release(a.filled[(r + i) % N] + flag_idx(r), a.base + j + 1);
       }
     }
+    trace_out(0);
     return;
   }
   // Reducer group.
@@ -184,7 +202,7 @@ __global__ void __launch_bounds__(512, 1) pushred_kernel(const __grid_constant__
       int c = 0;
       for (int q = 0; q < N; ++q)
         if (q != r) w[c++] = a.filled[r] + flag_idx(q);
-      leader_wait(a, w, c, a.base + j + 1, abort);
+      timed_wait(w, c, a.base + j + 1);
     }
     bar(gid, nt);
     if (*abort) return;
@@ -235,6 +253,7 @@ __global__ void __launch_bounds__(512, 1) pushred_kernel(const __grid_constant__
         if (q != r) release(a.consumed[q] + flag_idx(r), a.base + j + 1);
     }
   }
+  trace_out(2);
 }
 
 template <typename T>
@@ -264,6 +283,7 @@ struct PrContext {
   std::vector<int> devices;
   std::vector<char*> scratch;
   std::vector<unsigned*> filled, consumed;
+  std::vector<unsigned long long*> trace;  // per device: blocks x 4 phase-time records
   unsigned* status = nullptr;
   unsigned* status_dev = nullptr;
   unsigned long long epoch = 0;
@@ -318,9 +338,16 @@ bool pushred_ensure(const int* devices, int n, std::string* why) {
       delete c;
       return fail("scratch and progress words");
     }
+    unsigned long long* tr = nullptr;
+    if (cudaMalloc(&tr, size_t(sms) * 4 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(tr, 0, size_t(sms) * 4 * sizeof(unsigned long long)) != cudaSuccess) {
+      delete c;
+      return fail("trace records");
+    }
     c->scratch.push_back(sc);
     c->filled.push_back(f);
     c->consumed.push_back(u);
+    c->trace.push_back(tr);
   }
   if (cudaHostAlloc(reinterpret_cast<void**>(&c->status), sizeof(unsigned),
                     cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
@@ -379,6 +406,7 @@ cudaError_t pushred_launch(const PlanOp& op, const Plan& plan, const Binding& b,
   a.op = int(plan.desc.op);
   a.allreduce = ar ? 1 : 0;
   a.senders = 256;
+  a.trace = p.nvls_trace ? c->trace[size_t(r)] : nullptr;
   void* argv[] = {&a};
   const cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(unsigned(c->blocks)), dim3(512), argv, 0, s);
   if (++c->launched == n) {
@@ -392,6 +420,31 @@ unsigned pushred_status(const int* devices, int n) {
   std::lock_guard<std::mutex> lk(g_pr_mu);
   PrContext* c = find_pr(devices, n);
   return c && c->status ? *static_cast<volatile unsigned*>(c->status) : 0u;
+}
+
+int pushred_trace_read(const int* devices, int n, int rank, double out[4], bool reset) {
+  std::lock_guard<std::mutex> lk(g_pr_mu);
+  PrContext* c = find_pr(devices, n);
+  if (!c || rank < 0 || rank >= n) return -1;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(devices[rank]) != cudaSuccess) return -1;
+  std::vector<unsigned long long> rec(size_t(c->blocks) * 4);
+  const size_t bytes = rec.size() * sizeof(unsigned long long);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(rec.data(), c->trace[size_t(rank)], bytes, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && reset) e = cudaMemset(c->trace[size_t(rank)], 0, bytes);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return -1;
+  int ran = 0;
+  double sum[4] = {};
+  for (int b = 0; b < c->blocks; ++b) {
+    const unsigned long long* r = &rec[size_t(b) * 4];
+    if (!(r[1] | r[3])) continue;
+    ++ran;
+    for (int k = 0; k < 4; ++k) sum[k] += double(r[k]);
+  }
+  for (int k = 0; k < 4; ++k) out[k] = ran ? sum[k] / double(ran) : 0.0;  // mean ns per block
+  return ran;
 }
 
 }  // namespace nb

@@ -22,5 +22,9 @@ cudaError_t pushred_launch(const PlanOp& op, const Plan& plan, const Binding& b,
                            cudaStream_t s);
 // Nonzero once a bounded wait expired.
 unsigned pushred_status(const int* devices, int n);
+// With NCCL_B200_NVLS_TRACE=1: mean per-block ns since the last reset of rank
+// `rank`'s kernels, {sender waiting, sender total, reducer waiting, reducer
+// total}; returns the blocks that ran, -1 on error.
+int pushred_trace_read(const int* devices, int n, int rank, double out[4], bool reset);
 
 }  // namespace nb

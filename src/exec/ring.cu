@@ -49,6 +49,9 @@ struct RingArgs {
   unsigned* status;         // mapped host word: nonzero = a wait expired
   unsigned base;            // epoch before this call
   unsigned skew;            // added to wait targets (bounded-wait test only)
+  // Optional phase timing (NCCL_B200_NVLS_TRACE): per block, ns accumulated
+  // over calls: {waiting for the predecessor, total}.
+  unsigned long long* trace;
 };
 
 __device__ __forceinline__ unsigned long long gtimer() {
@@ -136,6 +139,8 @@ __global__ void __launch_bounds__(512, 1) bc_ring_kernel(const __grid_constant__
   __syncthreads();
   const unsigned long long step = a.chunk * gridDim.x;
   const unsigned steps = unsigned((a.bytes + step - 1) / step);
+  const unsigned long long t_start = a.trace && threadIdx.x == 0 ? gtimer() : 0;
+  unsigned long long waited = 0;
   for (unsigned k = 0; k < steps; ++k) {
     const unsigned long long off = k * step + a.chunk * blockIdx.x;
     const unsigned long long len = off < a.bytes ? min(a.chunk, a.bytes - off) : 0;
@@ -151,6 +156,7 @@ __global__ void __launch_bounds__(512, 1) bc_ring_kernel(const __grid_constant__
             break;
           }
         }
+        if (a.trace) waited += gtimer() - t0;
       }
       __syncthreads();
       if (abort_flag) return;
@@ -162,11 +168,16 @@ __global__ void __launch_bounds__(512, 1) bc_ring_kernel(const __grid_constant__
       st_rel(a.post + blockIdx.x, a.base + k + 1);
     }
   }
+  if (a.trace && threadIdx.x == 0) {
+    atomicAdd(a.trace + 2ull * blockIdx.x, waited);
+    atomicAdd(a.trace + 2ull * blockIdx.x + 1, gtimer() - t_start);
+  }
 }
 
 struct RingContext {
   std::vector<int> devices;
   std::vector<unsigned*> flags;  // per device: `blocks` progress words
+  std::vector<unsigned long long*> trace;  // per device: blocks x 2 phase-time records
   unsigned* status = nullptr;
   unsigned* status_dev = nullptr;
   unsigned long long epoch = 0;
@@ -214,7 +225,14 @@ bool ring_ensure(const int* devices, int n, std::string* why) {
       delete c;
       return fail("progress words");
     }
+    unsigned long long* tr = nullptr;
+    if (cudaMalloc(&tr, size_t(sms) * 2 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(tr, 0, size_t(sms) * 2 * sizeof(unsigned long long)) != cudaSuccess) {
+      delete c;
+      return fail("trace records");
+    }
     c->flags.push_back(f);
+    c->trace.push_back(tr);
   }
   if (cudaHostAlloc(reinterpret_cast<void**>(&c->status), sizeof(unsigned),
                     cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
@@ -256,6 +274,7 @@ cudaError_t ring_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
     a.status = c->status_dev;
     a.base = unsigned(c->epoch);
     a.skew = p.test_nvls_skew;
+    a.trace = p.nvls_trace ? c->trace[size_t(r)] : nullptr;
     bc_ring_kernel<<<dim3(unsigned(c->blocks)), dim3(512), 0, s>>>(a);
     e = cudaGetLastError();
   }
@@ -271,6 +290,32 @@ unsigned ring_status(const int* devices, int n) {
   std::lock_guard<std::mutex> lk(g_ring_mu);
   RingContext* c = find_ring(devices, n);
   return c && c->status ? *static_cast<volatile unsigned*>(c->status) : 0u;
+}
+
+int ring_trace_read(const int* devices, int n, int rank, double out[2], bool reset) {
+  std::lock_guard<std::mutex> lk(g_ring_mu);
+  RingContext* c = find_ring(devices, n);
+  if (!c || rank < 0 || rank >= n) return -1;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(devices[rank]) != cudaSuccess) return -1;
+  std::vector<unsigned long long> rec(size_t(c->blocks) * 2);
+  const size_t bytes = rec.size() * sizeof(unsigned long long);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(rec.data(), c->trace[size_t(rank)], bytes, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && reset) e = cudaMemset(c->trace[size_t(rank)], 0, bytes);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return -1;
+  int ran = 0;
+  double sum[2] = {};
+  for (int b = 0; b < c->blocks; ++b) {
+    if (!rec[size_t(b) * 2 + 1]) continue;
+    ++ran;
+    sum[0] += double(rec[size_t(b) * 2]);
+    sum[1] += double(rec[size_t(b) * 2 + 1]);
+  }
+  out[0] = ran ? sum[0] / ran : 0.0;
+  out[1] = ran ? sum[1] / ran : 0.0;
+  return ran;
 }
 
 }  // namespace nb

@@ -18,5 +18,9 @@ cudaError_t ring_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
                         cudaStream_t s);
 // Nonzero once a bounded wait expired.
 unsigned ring_status(const int* devices, int n);
+// With NCCL_B200_NVLS_TRACE=1: mean per-block ns since the last reset of rank
+// `rank`'s kernel, {waiting for the predecessor, total}; returns the blocks
+// that ran (0 for the last rank of the chain, which runs no kernel).
+int ring_trace_read(const int* devices, int n, int rank, double out[2], bool reset);
 
 }  // namespace nb

@@ -159,14 +159,16 @@ def test_single_local_copy(nbytes, src_off, dst_off):
 
 CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", "allgather"),
          ("bc_pull", "broadcast"), ("bc_scatter", "broadcast"), ("ar_staged", "allreduce"),
-         ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ag_push", "allgather"),
-         ("ar_oneshot", "allreduce")]
+         ("rs_staged", "reducescatter"), ("bc_chain", "broadcast"), ("ag_push", "allgather")]
 
 
 @pytest.mark.parametrize("algo,kind", CASES)
 @pytest.mark.parametrize("n", [2, 3, 4, 8])
 @pytest.mark.parametrize("inplace", [False, True])
 def test_virtual_rank_plans(algo, kind, n, inplace):
+    # (The gang engines -- NVLS, push chain, push-reduce, one-shot -- wait for
+    # their counterparts on other GPUs inside the kernel; the virtual-rank
+    # runner refuses them. Their GPU tests run on real cliques.)
     need_gpus(1)
     if algo == "bc_scatter" and n < 3:
         pytest.skip("scatter broadcast needs 3+ ranks")

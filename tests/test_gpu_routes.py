@@ -183,27 +183,113 @@ for kind, rc, sends, recvs, root in jobs:
                 ref = ref + x[r * rc:(r + 1) * rc]
         bad += 0 if torch.equal(recvs[r].to("cuda:0"), ref) else 1
 arr = (C.c_int * n)(*devs)
-st = nc.shim.nb_ring_status(arr, n) | nc.shim.nb_pushred_status(arr, n)
+st = nc.shim.nb_ring_status(arr, n) | nc.shim.nb_pushred_status(arr, n) | nc.shim.nb_oneshot_status(arr, n)
 print("RESULT", bad, st, nc.shim.nb_poisoned(), nc.custom_calls(ALGO["bc_ring"]),
-      nc.custom_calls(ALGO["ar_push"]), nc.custom_calls(ALGO["rs_push"]))
+      nc.custom_calls(ALGO["ar_push"]), nc.custom_calls(ALGO["rs_push"]), nc.custom_calls(ALGO["ar_oneshot"]))
 """
 
 
+@pytest.mark.parametrize("algo", ["bc=ring,ar=push,rs=push", "ar=oneshot"])
 @pytest.mark.parametrize("n", [2, 3])
-def test_gang_calls_ordered_across_streams_and_cliques(n):
+def test_gang_calls_ordered_across_streams_and_cliques(n, algo):
     """The push chain and the push-reduce engine keep scratch, progress words
     and an epoch per device set. Calls from two cliques over the same GPUs,
     and calls of one clique on two unordered streams, issued back to back
     without host synchronization, must not overlap on those engines: every
     result bit-exact, no wait expired, nothing poisoned."""
     need_gpus(n)
-    env = dict(os.environ, NCCL_B200_ALGO="bc=ring,ar=push,rs=push", NCCL_B200_TUNE="0",
+    env = dict(os.environ, NCCL_B200_ALGO=algo, NCCL_B200_TUNE="0",
                NCCL_B200_FIRST_PASS="0", NCCL_B200_AR_MIN="1K", NCCL_B200_RS_MIN="1K",
                NCCL_B200_BC_MIN="1K", NCCL_B200_TIMEOUT_MS="5000")
     r = subprocess.run([sys.executable, "-c", ORDER_CHILD.format(repo=REPO, n=n)], env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
-    bad, status, poisoned, ring, arp, rsp = map(int, line[1:])
+    bad, status, poisoned, ring, arp, rsp, one = map(int, line[1:])
     assert (bad, status, poisoned) == (0, 0, 0), line
-    assert ring >= 4 and arp >= 4 and rsp >= 4, line
+    if "oneshot" in algo:
+        assert one >= 4, line
+    else:
+        assert ring >= 4 and arp >= 4 and rsp >= 4, line
+
+
+OS_CHILD = r"""
+import sys, torch
+sys.path.insert(0, {repo!r}); sys.path.insert(0, {repo!r} + "/tests")
+from scc26_nccl_shim_b200.parallel.nccl import Nccl
+from scc26_nccl_shim_b200._core import ALGO
+from test_gpu_abi import run_kind
+n = {n}
+devs = list(range(n))
+nc = Nccl("interposer")
+comms = nc.comm_init_all(devs)
+for c in (1, 7, 4096, 65536 + 3, (1 << 20) // 4, (8 << 20) // 4 + 5, (48 << 20) // 4):
+    run_kind(nc, "allreduce", comms, devs, c)
+for dt in (torch.bfloat16, torch.float16):
+    run_kind(nc, "allreduce", comms, devs, (1 << 20) + 9, dtype=dt)
+for op in ("avg", "max", "min", "prod"):
+    run_kind(nc, "allreduce", comms, devs, (2 << 20) // 4 + 1, op=op)
+run_kind(nc, "allreduce", comms, devs, (4 << 20) // 4, inplace=True)  # planned as two-shot
+print("RESULT", nc.custom_calls(ALGO["ar_oneshot"]), nc.custom_calls(ALGO["ar_twoshot"]))
+for c in comms:
+    nc.comm_destroy(c)
+"""
+
+
+@pytest.mark.parametrize("n", [2, 3, 4, 8])
+def test_forced_oneshot(n):
+    """The low-latency one-shot AllReduce (in-kernel arrive/depart barriers)
+    from 4 bytes up, odd tails, 16-bit types and every op, bit-exact against
+    a torch fp32 fold in rank order; in place it runs the two-shot plan."""
+    need_gpus(n)
+    env = dict(os.environ, NCCL_B200_ALGO="ar=oneshot", NCCL_B200_TUNE="0", NCCL_B200_FIRST_PASS="0",
+               NCCL_B200_AR_MIN="1")
+    r = subprocess.run([sys.executable, "-c", OS_CHILD.format(repo=REPO, n=n)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    assert int(line[1]) >= 13 and int(line[2]) >= 1, line
+
+
+OS_TIMEOUT_CHILD = r"""
+import sys, ctypes as C, torch
+sys.path.insert(0, {repo!r})
+from scc26_nccl_shim_b200.parallel.nccl import Nccl, collective, NcclError
+nc = Nccl("interposer")
+devs = [0, 1]
+arr = (C.c_int * 2)(*devs)
+comms = nc.comm_init_all(devs)
+xs = [torch.full((1 << 20,), float(d + 1), device=f"cuda:{{d}}") for d in devs]
+ys = [torch.empty_like(x) for x in xs]
+s = [torch.cuda.current_stream(d).cuda_stream for d in devs]
+out = []
+for i in range(3):
+    try:
+        collective(nc, "allreduce", xs, ys, comms, s)
+        for d in devs: torch.cuda.synchronize(d)
+        out.append("ok" if all(torch.equal(y, torch.full_like(y, 3.0)) for y in ys) else "stale")
+    except NcclError as e:
+        for d in devs: torch.cuda.synchronize(d)
+        out.append("err%d" % e.code)
+    out.append("s%d" % nc.shim.nb_oneshot_status(arr, 2))
+print("RESULT", ",".join(out), nc.shim.nb_poisoned())
+"""
+
+
+def test_oneshot_bounded_wait_reports_timeout():
+    """With a barrier target nothing reaches, every block gives up after
+    200 ms and sets the status word; the next call reports
+    ncclUnhandledCudaError and poisons the custom paths; the call after runs
+    on NCCL. No GPU faults."""
+    need_gpus(2)
+    env = dict(os.environ, NCCL_B200_ALGO="ar=oneshot", NCCL_B200_TUNE="0", NCCL_B200_FIRST_PASS="0",
+               NCCL_B200_AR_MIN="1K", NCCL_B200_TEST_NVLS_SKEW="1000", NCCL_B200_TIMEOUT_MS="200")
+    r = subprocess.run([sys.executable, "-c", OS_TIMEOUT_CHILD.format(repo=REPO)], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    seq = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
+    calls = seq[1].split(",")
+    assert calls[1] == "s1", calls
+    assert calls[2] == "err1", calls
+    assert calls[4] == "ok", calls
+    assert seq[2] == "1"

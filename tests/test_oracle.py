@@ -87,3 +87,15 @@ def test_tuned_bands_from_a_cache_record():
     assert oracle.tuned_route(rec, "allreduce", 1 << 20) == "ar_oneshot"
     assert oracle.expected_route("allreduce", "float32", "sum", (1 << 20) // 4, 4, nvls=True,
                                  rules=oracle.Rules({"NCCL_B200_AR_MIN": "512K"}), calib=rec) == "ar_oneshot"
+
+
+def test_measured_crossover_lowers_unset_thresholds_only():
+    rec = {"pref0": 1, "engage0": 256}
+    small = (512 << 10) // 4
+    assert oracle.expected_route("allreduce", "float32", "sum", small, 2, calib=rec,
+                                 rules=oracle.Rules({})) == "ar_twoshot"
+    assert oracle.expected_route("allreduce", "float32", "sum", (128 << 10) // 4, 2, calib=rec,
+                                 rules=oracle.Rules({})) == "nccl"
+    # An explicit threshold wins over the measurement.
+    assert oracle.expected_route("allreduce", "float32", "sum", small, 2, calib=rec,
+                                 rules=oracle.Rules({"NCCL_B200_AR_MIN": "32M"})) == "nccl"
