@@ -265,6 +265,19 @@ class RealBackend final : public GroupBackend {
     }
   }
   bool query(Call& c) override {
+    // A registered clique member answers from the registry (its device, rank
+    // and size were checked with libnccl when the clique was registered);
+    // any other communicator asks libnccl.
+    CliqueInfo info;
+    if (rt().cliques.lookup(c.comm, &info)) {
+      for (int q = 0; q < info.nranks; ++q)
+        if (info.comms[q] == c.comm) {
+          c.desc.device = info.devices[q];
+          c.desc.rank = q;
+          c.desc.nranks = info.nranks;
+          return true;
+        }
+    }
     const RealNccl& n = rt().real;
     const auto comm = static_cast<ncclComm_t>(c.comm);
     return n.CommCuDevice(comm, &c.desc.device) == ncclSuccess &&
@@ -343,7 +356,13 @@ Outcome run_clique(std::vector<Call>& calls, Reason& reason, bool probe) {
       for (int k = 0; k < int(Kind::Count); ++k)
         st.preferred[k] = tuned_route(r.calib[info.nranks], k, logical_bytes(descs[0]));
   }
-  const CliqueDecision d = gate_clique(descs, st, r.policy_for(int(descs.size())));
+  // A probe measures sizes below the thresholds: the gate applies none.
+  Policy unthresholded;
+  if (probe) {
+    unthresholded = r.policy_for(int(descs.size()));
+    for (size_t& m : unthresholded.min_bytes) m = 0;
+  }
+  const CliqueDecision d = gate_clique(descs, st, probe ? unthresholded : r.policy_for(int(descs.size())));
   reason = d.reason;
   if (d.reason == Reason::FirstPass && !probe) r.first_pass_done = true;
   if (d.algo == Algo::Fallback) return Outcome::Fallback;

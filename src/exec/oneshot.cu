@@ -4,10 +4,10 @@
 // One kernel per rank, launched on the caller's own stream with nothing
 // around it. Block b of every rank's kernel:
 //   1. arrives: stores the call's epoch into word (b, r) of every peer's
-//      arrive table (P2P st.release.sys) -- this rank's stream has reached
-//      the call, so its whole input is ready;
-//   2. waits until every peer's block b arrived here (ld.acquire.sys polls
-//      of this GPU's own table);
+//      arrive table (P2P stores after a system-scope release fence) -- this
+//      rank's stream has reached the call, so its whole input is ready;
+//   2. waits until every peer's block b arrived here (relaxed polls of this
+//      GPU's own table, then one acquire fence);
 //   3. folds its share of the message (grid-stride 16/32-byte vectors) from
 //      all N inputs in rank order -- its own from HBM, the peers' over
 //      NVLink -- with fp32 accumulation, and stores only this rank's output;
@@ -75,31 +75,34 @@ __device__ __forceinline__ unsigned long long gtimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
+__device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
   unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_rel(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // Thread 0 publishes this block's step to every rank, then waits (bounded)
 // for every rank's block with the same index; the block then proceeds. False
-// when a wait expired.
+// when a wait expired. One release fence orders everything before the
+// barrier (this rank's input, written before the kernel; at departure, the
+// block's loads of the peers' inputs, joined by the CTA barrier) before the
+// relaxed flag stores; the waits poll with relaxed loads and take one
+// acquire fence once every flag is seen, so the reads after the barrier see
+// what the peers published.
 __device__ bool block_barrier(const OsArgs& a, unsigned* const* peer_tables, const unsigned* mine,
                               volatile int* abort_flag) {
   if (threadIdx.x == 0) {
-    // Everything this block did before (its loads of peer inputs) is ordered
-    // before the release stores.
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     for (int q = 0; q < a.nranks; ++q)
-      st_rel(peer_tables[q] + blockIdx.x * unsigned(kMaxRanks) + unsigned(a.rank), a.epoch);
+      st_relaxed(peer_tables[q] + blockIdx.x * unsigned(kMaxRanks) + unsigned(a.rank), a.epoch);
     const unsigned target = a.epoch + a.skew;
     const unsigned long long t0 = gtimer();
     for (int q = 0; q < a.nranks && !*abort_flag; ++q) {
       const unsigned* w = mine + blockIdx.x * unsigned(kMaxRanks) + unsigned(q);
-      while (int(ld_acq(w) - target) < 0) {
+      while (int(ld_relaxed(w) - target) < 0) {
         if (gtimer() - t0 > a.timeout_ns) {
           *reinterpret_cast<volatile unsigned*>(a.status) = 1u;
           __threadfence_system();
@@ -108,6 +111,7 @@ __device__ bool block_barrier(const OsArgs& a, unsigned* const* peer_tables, con
         }
       }
     }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
   }
   __syncthreads();
   return *abort_flag == 0;
@@ -244,7 +248,6 @@ struct OsContext {
   unsigned* status_dev = nullptr;
   unsigned epoch = 0;
   int launched = 0;
-  bool fence = false;  // this call's streams differ from the previous call's
   int blocks = 0;
   bool broken = false;
 };
@@ -322,10 +325,25 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
       c->broken = true;  // a previous call timed out: the tables are no longer in step
       return cudaErrorLaunchTimeout;
     }
-    // A new call: its epoch, and whether any rank changed streams.
+    // A new call: its epoch, and whether any rank changed streams. If one
+    // did, every rank's stream waits for the previous call's kernels on every
+    // GPU -- all these waits are enqueued now, before this call re-records
+    // any of those events.
     ++c->epoch;
-    c->fence = false;
-    for (int q = 0; q < n; ++q) c->fence = c->fence || (c->last[size_t(q)] && c->last[size_t(q)] != b.stream[q]);
+    bool fence = false;
+    for (int q = 0; q < n; ++q) fence = fence || (c->last[size_t(q)] && c->last[size_t(q)] != b.stream[q]);
+    for (int w = 0; fence && w < n; ++w) {
+      cudaError_t e = cudaSetDevice(b.device[w]);
+      for (int q = 0; q < n && e == cudaSuccess; ++q) e = cudaStreamWaitEvent(b.stream[w], c->done[size_t(q)], 0);
+      if (e != cudaSuccess) {
+        cudaSetDevice(b.device[r]);
+        return e;
+      }
+    }
+    if (fence) {
+      const cudaError_t e = cudaSetDevice(b.device[r]);
+      if (e != cudaSuccess) return e;
+    }
   }
   const size_t es = elem_size(plan.desc.dtype);
   const size_t bytes = plan.desc.bytes;
@@ -363,9 +381,7 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
   const unsigned blocks =
       unsigned(std::min<size_t>(std::max<size_t>(8, (bytes + 8191) / 8192), size_t(c->blocks)));
   cudaError_t e = cudaSuccess;
-  if (c->fence)
-    for (int q = 0; q < n && e == cudaSuccess; ++q) e = cudaStreamWaitEvent(s, c->done[size_t(q)], 0);
-  if (e == cudaSuccess) {
+  {
     void* argv[] = {&a};
     // Cooperative: every block of the grid is resident at once, so a block
     // waiting for its counterparts never keeps another block of its own
