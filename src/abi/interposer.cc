@@ -291,27 +291,39 @@ class RealBackend final : public GroupBackend {
 RealBackend g_backend;
 GroupMachine g_machine(g_backend);
 
+// What must hold at run time, per member call, before the clique's own
+// routes may touch its buffers: the communicator reports no asynchronous
+// error (one that does is dropped from the registry), the call's stream
+// belongs to the communicator's GPU, and every buffer the call reads or
+// writes passes the buffer rules for the whole clique.
+enum class MemberCheck { Ok, AsyncError, ForeignStream, Buffer };
+
+MemberCheck check_member(Runtime& r, const Call& c, const CliqueInfo& info) {
+  ncclResult_t async = ncclSuccess;
+  if (r.real.CommGetAsyncError(static_cast<ncclComm_t>(c.comm), &async) != ncclSuccess || async != ncclSuccess)
+    return MemberCheck::AsyncError;
+  const int dev = c.desc.device;
+  int owner = -1;
+  const bool on_device = cudaSetDevice(dev) == cudaSuccess &&
+                         cudaStreamGetDevice(static_cast<cudaStream_t>(c.stream), &owner) == cudaSuccess &&
+                         owner == dev;
+  if (!on_device) {
+    cudaGetLastError();
+    return MemberCheck::ForeignStream;
+  }
+  // A Broadcast non-root's send buffer is never read.
+  const bool reads_send = !(c.desc.kind == Kind::Broadcast && c.desc.rank != c.desc.root);
+  const bool buffers_ok =
+      supported_buffer(c.recvbuff, recv_extent(c.desc), dev, info.devices, info.nranks) &&
+      (!reads_send || supported_buffer(c.sendbuff, send_extent(c.desc), dev, info.devices, info.nranks));
+  return buffers_ok ? MemberCheck::Ok : MemberCheck::Buffer;
+}
+
 bool runtime_checks(Runtime& r, const std::vector<Call>& calls, const CliqueInfo& info) {
   for (const Call& c : calls) {
-    ncclResult_t async = ncclSuccess;
-    if (r.real.CommGetAsyncError(static_cast<ncclComm_t>(c.comm), &async) != ncclSuccess ||
-        async != ncclSuccess) {
-      r.cliques.forget(c.comm);
-      return false;
-    }
-    const int dev = c.desc.device;
-    int stream_dev = -1;
-    if (cudaSetDevice(dev) != cudaSuccess ||
-        cudaStreamGetDevice(static_cast<cudaStream_t>(c.stream), &stream_dev) != cudaSuccess ||
-        stream_dev != dev) {
-      cudaGetLastError();
-      return false;
-    }
-    if (!supported_buffer(c.recvbuff, recv_extent(c.desc), dev, info.devices, info.nranks)) return false;
-    const bool bcast_nonroot = c.desc.kind == Kind::Broadcast && c.desc.rank != c.desc.root;
-    if (!bcast_nonroot &&
-        !supported_buffer(c.sendbuff, send_extent(c.desc), dev, info.devices, info.nranks))
-      return false;
+    const MemberCheck m = check_member(r, c, info);
+    if (m == MemberCheck::AsyncError) r.cliques.forget(c.comm);
+    if (m != MemberCheck::Ok) return false;
   }
   return true;
 }
@@ -488,15 +500,24 @@ double time_calls(const int* devices, int n, cudaStream_t* streams, cudaEvent_t*
   return worst / reps;
 }
 
+// The interposer runs a clique's call synchronously inside the application's
+// call and replays it on libnccl when it falls back, which is only the same
+// contract for blocking communicators. A communicator blocks unless the
+// environment or its ncclConfig_t says otherwise; a config is trusted only
+// when it is large enough to hold the field, carries the initializer's magic
+// number, and comes from a libnccl version whose layout is known here.
 bool blocking_configuration(const ncclConfig_t* config) {
-  const char* env = std::getenv("NCCL_COMM_BLOCKING");
-  if (env && std::strcmp(env, "1") != 0) return false;
-  if (!config) return true;
+  if (const char* env = std::getenv("NCCL_COMM_BLOCKING")) {
+    if (std::strcmp(env, "1") != 0) return false;
+  }
+  if (config == nullptr) return true;
   const Policy& p = rt().policy;
-  return config->size >= offsetof(ncclConfig_t, blocking) + sizeof(config->blocking) &&
-         config->magic == 0xcafebeef && int(config->version) >= p.min_nccl_version &&
-         int(config->version) <= p.max_nccl_version &&
-         (config->blocking == 1 || config->blocking == NCCL_CONFIG_UNDEF_INT);
+  const size_t needed = offsetof(ncclConfig_t, blocking) + sizeof(config->blocking);
+  const int version = int(config->version);
+  const bool readable = config->size >= needed && config->magic == 0xcafebeef;
+  const bool known_layout = version >= p.min_nccl_version && version <= p.max_nccl_version;
+  const bool blocks = config->blocking == NCCL_CONFIG_UNDEF_INT || config->blocking == 1;
+  return readable && known_layout && blocks;
 }
 
 bool distinct_devices(const int* devs, int n) {
@@ -552,7 +573,8 @@ void note_initialization(ncclResult_t result, ncclComm_t* output, int nranks, nc
     g_group.init_only = false;
     return;
   }
-  // Grouped init may defer writing *output until the outer native GroupEnd.
+  // Inside a group, libnccl fills *output only when the outermost group ends:
+  // keep where it will land and register the clique then.
   PendingInit p;
   p.output = reinterpret_cast<void**>(output);
   std::memcpy(p.id, id.internal, sizeof(p.id));

@@ -28,14 +28,13 @@ struct Candidate {
   int depth;
   int split_ppm = 0;     // hybrid routes: the switch's share (per 10000)
   int split_blocks = 0;  // and its blocks per GPU
+  int nvls_shape = 0;    // NVLS routes: packed kernel shape (pack_nvls_shape)
 };
 
-// Hybrid splits tried per kind. AllReduce: the NVLS AllReduce is limited by
-// the switch below the link rate, so a P2P two-shot share on the remaining
-// SMs can use the links' spare capacity. ReduceScatter: NVLS reads every
-// byte of a GPU once more than the P2P pulls do, so its share is smaller.
-constexpr int kArSplits[][2] = {{6000, 74}, {7000, 96}, {7800, 110}, {8500, 120}};
-constexpr int kRsSplits[][2] = {{2500, 48}, {4000, 74}, {5500, 96}};
+// NVLS AllReduce kernel shapes tried (movers per block, requests in flight per
+// mover, round MiB): the switch side bounds the kernel, so more requests in
+// flight and smaller rounds (a shorter pipeline fill and drain) may pay.
+constexpr int kNvlsShapes[][3] = {{0, 0, 0}, {608, 4, 0}, {608, 8, 0}, {512, 8, 128}, {608, 8, 64}};
 
 // Every candidate route of a kind; a host-lane variant is added wherever the
 // rate model (measured PCIe, NVLink and fold rates) predicts a host share.
@@ -91,15 +90,13 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
         add(Algo::ArStaged, 0, 128, 2);
         add(Algo::ArStaged, 0, 256, 2);
       }
-      if (nvls && n >= 2) v.push_back({Algo::ArNvls, 0, 0, 0, 0});
-      if (nvls && n >= 4)
-        for (const auto& sp : kArSplits) v.push_back({Algo::ArHybrid, 0, 0, 0, 0, sp[0], sp[1]});
+      if (nvls && n >= 2)
+        for (const auto& sh : kNvlsShapes)
+          v.push_back({Algo::ArNvls, 0, 0, 0, 0, 0, 0, pack_nvls_shape(sh[0], sh[1], sh[2])});
       v.push_back({Algo::ArPush, 0, 0, 0, 0});
       break;
     case Kind::ReduceScatter:
       if (nvls && n >= 2) v.push_back({Algo::RsNvls, 0, 0, 0, 0});
-      if (nvls && n >= 4)
-        for (const auto& sp : kRsSplits) v.push_back({Algo::RsHybrid, 0, 0, 0, 0, sp[0], sp[1]});
       add(Algo::RsPull, 0);
       v.push_back({Algo::RsPush, 0, 0, 0, 0});
       if (small) {
@@ -200,6 +197,7 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
         s.stage_depth = c.depth;
         s.split_ppm = c.split_ppm;
         s.split_blocks = c.split_blocks;
+        unpack_nvls_shape(c.nvls_shape, &s);
         Plan plan;
         build_plan(c.algo, d, r.policy, s, plan);
         std::string why;
@@ -242,9 +240,10 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
         const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? size : d.bytes;
         std::snprintf(line, sizeof line,
                       "tune %s n=%d bytes=%zu %s ce_ppm=%d host_ppm=%d piece_mib=%d depth=%d split=%d/%d "
-                      "busbw_gbs=%.1f",
+                      "nvls_shape=%d busbw_gbs=%.1f",
                       kind_name(kind), n, logical, algo_name(c.algo), c.ce_ppm, c.host_ppm, c.piece_mib,
-                      c.depth, c.split_ppm, c.split_blocks, logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
+                      c.depth, c.split_ppm, c.split_blocks, c.nvls_shape,
+                      logical / (ms * 1e-3) / 1e9 * busbw_factor(kind, n));
         r.summary.note(line);
         // An event-ordered chain pays a cross-GPU event wait per piece and hop,
         // so its rate drops as messages outgrow the tuning size (measured at 4
@@ -267,6 +266,7 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
         out->small_depth[kk] = best.depth;
         out->small_split_ppm[kk] = best.split_ppm;
         out->small_split_blocks[kk] = best.split_blocks;
+        out->small_nvls_shape[kk] = best.nvls_shape;
       } else if (best.algo != Algo::Fallback) {
         out->preferred[kk] = int(best.algo);
         out->ce_ppm[kk] = best.ce_ppm;
@@ -275,6 +275,7 @@ void tune_routes(const int* devices, int n, size_t bytes, CalibResult* out) {
         out->stage_depth[kk] = best.depth;
         out->split_ppm[kk] = best.split_ppm;
         out->split_blocks[kk] = best.split_blocks;
+        out->nvls_shape[kk] = best.nvls_shape;
         const size_t logical = (kind == Kind::AllGather || kind == Kind::ReduceScatter) ? size : d.bytes;
         out->route_gbs[kk] = logical / (best_real_ms * 1e-3) / 1e9 * busbw_factor(kind, n);
       }

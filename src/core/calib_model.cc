@@ -69,6 +69,7 @@ Shares shares_from(const CalibResult& c, Algo a, int n, bool small) {
       if (c.small_depth[k] > 0) s.stage_depth = c.small_depth[k];
       if (c.small_split_ppm[k] > 0) s.split_ppm = c.small_split_ppm[k];
       if (c.small_split_blocks[k] > 0) s.split_blocks = c.small_split_blocks[k];
+      if (c.small_nvls_shape[k] > 0) unpack_nvls_shape(c.small_nvls_shape[k], &s);
       continue;
     }
     if (c.preferred[k] != int(a)) continue;
@@ -78,6 +79,7 @@ Shares shares_from(const CalibResult& c, Algo a, int n, bool small) {
     if (c.stage_depth[k] > 0) s.stage_depth = c.stage_depth[k];
     if (c.split_ppm[k] > 0) s.split_ppm = c.split_ppm[k];
     if (c.split_blocks[k] > 0) s.split_blocks = c.split_blocks[k];
+    if (c.nvls_shape[k] > 0) unpack_nvls_shape(c.nvls_shape[k], &s);
   }
   return s;
 }
@@ -109,9 +111,9 @@ std::string calib_to_json(const CalibResult& c, const std::string& key) {
   for (int k = 0; k < 4; ++k) {
     std::snprintf(buf, sizeof buf,
                   ", \"tpref%d\": %d, \"split%d\": %d, \"sblocks%d\": %d, \"ssplit%d\": %d, "
-                  "\"ssblocks%d\": %d, \"engage%d\": %d",
+                  "\"ssblocks%d\": %d, \"engage%d\": %d, \"nvshape%d\": %d, \"snvshape%d\": %d",
                   k, c.tiny_pref[k], k, c.split_ppm[k], k, c.split_blocks[k], k, c.small_split_ppm[k], k,
-                  c.small_split_blocks[k], k, c.engage_kib[k]);
+                  c.small_split_blocks[k], k, c.engage_kib[k], k, c.nvls_shape[k], k, c.small_nvls_shape[k]);
     s += buf;
   }
   return s + "}\n";
@@ -167,6 +169,8 @@ bool calib_from_json(const std::string& text, const std::string& key, CalibResul
       if (json_number(text, ("ssplit" + K).c_str(), &v)) c.small_split_ppm[k] = int(v);
       if (json_number(text, ("ssblocks" + K).c_str(), &v)) c.small_split_blocks[k] = int(v);
       if (json_number(text, ("engage" + K).c_str(), &v)) c.engage_kib[k] = int(v);
+      if (json_number(text, ("nvshape" + K).c_str(), &v)) c.nvls_shape[k] = int(v);
+      if (json_number(text, ("snvshape" + K).c_str(), &v)) c.small_nvls_shape[k] = int(v);
     }
   }
   c.valid = true;

@@ -38,6 +38,7 @@ struct CalibResult {
   double route_gbs[4] = {0, 0, 0, 0};  // busbw of the chosen route at the tuning size
   int split_ppm[4] = {0, 0, 0, 0};     // hybrid routes: the switch's share and blocks
   int split_blocks[4] = {0, 0, 0, 0};
+  int nvls_shape[4] = {0, 0, 0, 0};    // NVLS routes: packed kernel shape (see pack_nvls_shape)
   // The same, tuned at a small size: used for messages below small_below_mib
   // (0 = no small-size choice). Pipelined routes pay a start-up that only
   // large messages amortize, so the best route differs with size.
@@ -48,6 +49,7 @@ struct CalibResult {
   int small_depth[4] = {0, 0, 0, 0};
   int small_split_ppm[4] = {0, 0, 0, 0};
   int small_split_blocks[4] = {0, 0, 0, 0};
+  int small_nvls_shape[4] = {0, 0, 0, 0};
   int small_below_mib = 0;
   // A third band for small messages, tuned among the SM routes only (no
   // pipelines, no copy-engine or host shares): used below tiny_below_kib.
@@ -58,6 +60,17 @@ struct CalibResult {
   // at every size of the ladder up to the policy threshold (0 = not measured).
   int engage_kib[4] = {0, 0, 0, 0};
 };
+
+// An NVLS kernel shape in one int: movers (threads) * 100000 + unroll * 10000
+// + round MiB (each part 0 = the policy's).
+inline int pack_nvls_shape(int movers, int unroll, int round_mib) {
+  return movers * 100000 + unroll * 10000 + round_mib;
+}
+inline void unpack_nvls_shape(int v, Shares* s) {
+  s->nvls_movers = v / 100000;
+  s->nvls_unroll = (v / 10000) % 10;
+  s->nvls_round_mib = v % 10000;
+}
 
 // Whether a message of `logical` bytes takes the small-size choice.
 bool small_message(const CalibResult& c, size_t logical);

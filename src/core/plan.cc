@@ -714,13 +714,17 @@ void plan_bc_chain(Builder& b, const CliqueDesc& d, const Shares& s) {
 // switch (multimem.ld_reduce / multimem.st) with bounded in-kernel barriers
 // between pipelined rounds (exec/nvls.cu). The prologue waits make the
 // members of a gang start together, so those barriers wait only for skew.
-void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p) {
+void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p, const Shares& s) {
   const int n = b.n();
   b.prologue();
   for (int r = 0; r < n; ++r) {
     const StreamId as{Strm::Aux, uint8_t(r), 0};
     for (int q = 0; q < n; ++q) b.touch(as, q);
     b.nvls(as, r, d.bytes);
+    PlanOp& op = b.plan().ops.back();
+    op.nvls_movers = uint16_t(std::max(0, s.nvls_movers));
+    op.nvls_unroll = uint8_t(std::max(0, s.nvls_unroll));
+    op.nvls_round = size_t(std::max(0, s.nvls_round_mib)) << 20;
   }
   b.plan().needs.nvls_bytes = p.nvls_round_bytes;
   b.plan().sm_bytes += d.bytes * size_t(n);  // ~S in and S out per GPU via the switch
@@ -878,7 +882,7 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
   switch (algo) {
     case Algo::ArOneShot: plan_ar_oneshot(b, d); break;
     case Algo::ArTwoShot: plan_ar_twoshot(b, d, s); break;
-    case Algo::ArNvls: plan_ar_nvls(b, d, p); break;
+    case Algo::ArNvls: plan_ar_nvls(b, d, p, s); break;
     case Algo::RsPull: plan_rs_pull(b, d, s); break;
     case Algo::AgPull: plan_ag_pull(b, d, s); break;
     case Algo::AgPush: plan_ag_pull(b, d, s, true); break;
@@ -891,7 +895,7 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
     case Algo::ArStaged: plan_staged(b, d, s, true); break;
     case Algo::RsStaged: plan_staged(b, d, s, false); break;
     case Algo::BcChain: plan_bc_chain(b, d, s); break;
-    case Algo::BcNvls: case Algo::AgNvls: case Algo::RsNvls: plan_ar_nvls(b, d, p); break;
+    case Algo::BcNvls: case Algo::AgNvls: case Algo::RsNvls: plan_ar_nvls(b, d, p, s); break;
     default: break;
   }
 }

@@ -99,6 +99,11 @@ struct PlanOp {
   size_t len[kMaxRanks] = {};
   size_t bytes = 0;
   uint16_t grid = 0;  // gang ops: blocks per GPU (0 = one per SM)
+  // NVLS gang ops: the kernel's shape (0 = the policy's): switch-side
+  // threads per block, multimem requests in flight per thread, round bytes.
+  uint16_t nvls_movers = 0;
+  uint8_t nvls_unroll = 0;
+  size_t nvls_round = 0;
 };
 
 // Resources a plan needs; the executor allocates them before submitting.
@@ -125,6 +130,10 @@ struct Shares {
   // blocks per GPU its kernel gets (0 = the policy's).
   int split_ppm = 0;
   int split_blocks = 0;
+  // NVLS routes: the kernel shape (0 = the policy's).
+  int nvls_movers = 0;
+  int nvls_unroll = 0;
+  int nvls_round_mib = 0;
 };
 
 struct Plan {

@@ -908,7 +908,11 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.uc_flags = reinterpret_cast<unsigned*>(a.uc + 3 * c->stride);
   a.mc_flags = reinterpret_cast<unsigned*>(a.mc + 3 * c->stride);
   a.bytes = ar ? range : plan.desc.bytes;
-  a.round = c->round;
+  // A smaller round than the scratch holds (a tuned kernel shape) uses the
+  // same buffers; 32-byte multiples of every slice stay aligned.
+  a.round = op.nvls_round && op.nvls_round < c->round
+                ? std::max<size_t>(op.nvls_round / 32 * 32, size_t(b.nranks) * size_t(c->blocks) * 32)
+                : c->round;
   a.buf_stride = c->stride;
   a.timeout_ns = p.device_timeout_ns;
   a.status = c->status_dev;
@@ -938,11 +942,13 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   // TMA copier: the movers plus one copier warp, with the staging buffers
   // in dynamic shared memory; SM copier: the configured split.
   a.tma = p.nvls_tma && c->tma_ok ? 1 : 0;
-  const int threads = a.tma ? std::min(p.nvls_movers, 608) + 32 : p.nvls_threads;
-  a.movers = a.tma ? threads - 32 : std::min(p.nvls_movers, threads - 128);
+  const int movers = op.nvls_movers ? int(op.nvls_movers) : p.nvls_movers;
+  const int unroll = op.nvls_unroll ? int(op.nvls_unroll) : p.nvls_unroll;
+  const int threads = a.tma ? std::min(movers, 608) + 32 : p.nvls_threads;
+  a.movers = a.tma ? threads - 32 : std::min(movers, threads - 128);
   const size_t smem = a.tma ? kTmaSmem : 0;
   void* argv[] = {&a};
-  const void* fn = pick_kernel(ar, p.nvls_unroll >= 8, a.tma != 0, plan.desc.dtype);
+  const void* fn = pick_kernel(ar, unroll >= 8, a.tma != 0, plan.desc.dtype);
   (void)dev;
   const cudaError_t e =
       cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(unsigned(threads)), argv, smem, s);
