@@ -84,9 +84,18 @@ class Builder {
     op.event = e;
     p_.ops.push_back(op);
   }
-  // `s` is about to touch rank r's buffers: make it wait r's InputReady once.
+  // `s` is about to touch rank r's buffers: make it wait r's InputReady once
+  // (with a hub: the hub's AllReady, once per stream).
   void touch(StreamId s, int r) {
     if (s.kind == Strm::Caller && s.dev == r) return;  // stream order
+    if (hub_) {
+      for (const auto& t : hub_waiters_)
+        if (t == s) return;
+      hub_waiters_.push_back(s);
+      wait(s, {Ev::AllReady, 0, 0, 0});
+      use(s);
+      return;
+    }
     for (const auto& t : touched_)
       if (t.first == s && t.second == r) return;
     touched_.push_back({s, r});
@@ -94,7 +103,7 @@ class Builder {
     use(s);
   }
   void use(StreamId s) {
-    if (s.kind == Strm::Caller || s.kind == Strm::Host) return;
+    if (s.kind == Strm::Caller || s.kind == Strm::Host || s.kind == Strm::Hub) return;
     for (const auto& u : used_)
       if (u == s) return;
     used_.push_back(s);
@@ -165,8 +174,18 @@ class Builder {
     use(s);
   }
 
+  // Every rank records InputReady. From four ranks on, a hub stream on rank
+  // 0's GPU waits for all of them and records AllReady, so a stream that
+  // touches peers waits on one event instead of N - 1: the cross-device
+  // event fans cost O(N) host calls instead of O(N^2).
   void prologue() {
     for (int r = 0; r < n_; ++r) record(input_ready(r), caller(r));
+    if (n_ >= kHubRanks) {
+      hub_ = true;
+      const StreamId h{Strm::Hub, 0, 0};
+      for (int r = 0; r < n_; ++r) wait(h, input_ready(r));
+      record({Ev::AllReady, 0, 0, 0}, h);
+    }
   }
   // Gang engines launched on caller streams share state across calls (see
   // Ev::GangDone): every rank's caller stream first waits for the previous
@@ -187,6 +206,13 @@ class Builder {
         wait(caller(r), done(s));
       }
       record(join_done(r), caller(r));
+    }
+    if (hub_) {
+      const StreamId h{Strm::Hub, 0, 0};
+      for (int r = 0; r < n_; ++r) wait(h, join_done(r));
+      record({Ev::AllJoined, 0, 0, 0}, h);
+      for (int r = 0; r < n_; ++r) wait(caller(r), {Ev::AllJoined, 0, 0, 0});
+      return;
     }
     for (int r = 0; r < n_; ++r)
       for (int q = 0; q < n_; ++q)
@@ -250,6 +276,9 @@ class Builder {
   size_t pieces_ = 0;
   std::vector<std::pair<StreamId, int>> touched_;
   std::vector<StreamId> used_;
+  bool hub_ = false;
+  std::vector<StreamId> hub_waiters_;
+  static constexpr int kHubRanks = 4;
 };
 
 void all_ranks(int n, int* ranks) {

@@ -31,7 +31,9 @@ namespace nb {
 // records and runs the CPU reduction.
 // Copy and Push are two copy-engine streams per GPU (pulls and pushes of a
 // staged route run concurrently on different engines).
-enum class Strm : uint8_t { Caller, Aux, Copy, D2H, H2D, Host, Push, Count };
+// Hub is one stream on rank 0's GPU that gathers the ranks' readiness and
+// completion for cliques of four or more (see Builder::prologue/join).
+enum class Strm : uint8_t { Caller, Aux, Copy, D2H, H2D, Host, Push, Hub, Count };
 struct StreamId {
   Strm kind = Strm::Caller;
   uint8_t dev = 0;
@@ -49,8 +51,10 @@ inline bool operator!=(StreamId a, StreamId b) { return !(a == b); }
 // progress words and an epoch, so the next such call waits for GangDone on
 // every GPU of its clique before it starts (two calls on unordered streams,
 // or from two cliques over the same GPUs, never overlap).
+// AllReady / AllJoined are recorded on the hub once it has waited for every
+// rank's InputReady / Join.
 enum class Ev : uint8_t { InputReady, Join, Phase, Done, D2HDone, H2DDone, HostDone, LaneFree, TempFree,
-                          GangDone, Count };
+                          GangDone, AllReady, AllJoined, Count };
 struct EventId {
   Ev kind = Ev::InputReady;
   uint8_t dev = 0;

@@ -80,9 +80,9 @@ bool Executor::ensure_device(int dev, std::string* why) {
     return false;
   }
   r.sm_count = sms;
-  bool ok = make_stream(r.aux) && make_stream(r.copy) && make_stream(r.push) &&
+  bool ok = make_stream(r.aux) && make_stream(r.copy) && make_stream(r.push) && make_stream(r.hub) &&
             make_event(r.input_ready) && make_event(r.join) && make_event(r.temp_free) &&
-            make_event(r.gang_done);
+            make_event(r.gang_done) && make_event(r.all_ready) && make_event(r.all_joined);
   for (int l = 0; ok && l < kMaxLanes; ++l)
     ok = make_stream(r.d2h[l]) && make_stream(r.h2d[l]) && make_event(r.d2h_done[l]) &&
          make_event(r.h2d_done[l]);
@@ -254,6 +254,7 @@ cudaStream_t Executor::bind_stream(StreamId s, const Binding& b) {
     case Strm::Aux: return r.aux;
     case Strm::Copy: return r.copy;
     case Strm::Push: return r.push;
+    case Strm::Hub: return r.hub;
     case Strm::D2H: return r.d2h[s.lane];
     case Strm::H2D: return r.h2d[s.lane];
     default: return nullptr;
@@ -276,6 +277,8 @@ cudaEvent_t Executor::bind_event(EventId e, const Binding& b) {
     case Ev::Join: return r.join;
     case Ev::TempFree: return r.temp_free;
     case Ev::GangDone: return r.gang_done;
+    case Ev::AllReady: return r.all_ready;
+    case Ev::AllJoined: return r.all_joined;
     case Ev::Phase: return e.index < r.phase.size() ? r.phase[e.index] : nullptr;
     case Ev::Done: return r.done[e.index][e.lane];
     case Ev::D2HDone: return r.d2h_done[e.lane];

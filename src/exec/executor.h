@@ -47,9 +47,10 @@ struct DeviceResources {
   int dev = -1;
   bool ready = false;
   int sm_count = 0;
-  cudaStream_t aux = nullptr, copy = nullptr, push = nullptr;
+  cudaStream_t aux = nullptr, copy = nullptr, push = nullptr, hub = nullptr;
   cudaStream_t d2h[kMaxLanes] = {}, h2d[kMaxLanes] = {};
   cudaEvent_t input_ready = nullptr, join = nullptr, temp_free = nullptr, gang_done = nullptr;
+  cudaEvent_t all_ready = nullptr, all_joined = nullptr;  // recorded on the hub stream
   void* temp = nullptr;  // device scratch of the staged routes
   size_t temp_bytes = 0;
   cudaEvent_t done[size_t(Strm::Count)][kMaxLanes] = {};
