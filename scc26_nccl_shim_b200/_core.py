@@ -18,7 +18,7 @@ ALGO = {"fallback": 0, "ar_twoshot": 1, "ar_nvls": 2, "rs_pull": 3, "ag_pull": 4
         "bc_pull": 5, "bc_scatter": 6, "ar_staged": 7, "rs_staged": 8, "bc_chain": 9,
         "bc_nvls": 10, "ag_nvls": 11, "rs_nvls": 12, "ag_push": 13, "bc_ring": 14,
         "rs_push": 15, "ar_push": 16, "ar_hybrid": 17, "ar_oneshot": 18,
-        "rs_hybrid": 19}
+        "rs_hybrid": 19, "ar_twoshot_ll": 20}
 REASONS = ["None", "NotGrouped", "UnsupportedType", "UnsupportedOp", "NullBuffer",
            "SizeOverflow", "BelowThreshold", "Misaligned", "BadSlot", "PartialOverlap",
            "BadRank", "GroupShape", "NotClique", "Mismatch", "Capturing", "FirstPass",
@@ -66,6 +66,8 @@ def lib() -> C.CDLL:
     L.nb_float_to_bf16.restype = C.c_uint16
     L.nb_bf16_to_float.argtypes = [C.c_uint16]
     L.nb_bf16_to_float.restype = C.c_float
+    L.nb_nvls_ar_round.argtypes = [C.c_uint64, C.c_uint64, C.c_int, C.c_uint,
+                                   C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
     L.nb_policy_value.argtypes = [C.c_char_p, C.c_char_p]
     L.nb_policy_value.restype = C.c_double
     L.nb_shares_from.argtypes = [C.c_double] * 7 + [C.c_int, C.c_int, C.POINTER(C.c_int),
@@ -122,6 +124,18 @@ def plan_simulate(algo, kind, dtype, nranks, count, op="sum", root=0, inplace_ma
                                 root, inplace_mask, host_ppm, ce_ppm, env_spec(env), seed,
                                 data_mode, sc, C.byref(stats), err, 512)
     return rc, err.value.decode(), stats
+
+
+def nvls_ar_rounds(nbytes: int, round_bytes: int, ramp: bool = True) -> list[tuple[int, int]]:
+    """The NVLS AllReduce round schedule: [(base, len), ...]."""
+    b, l = C.c_uint64(), C.c_uint64()
+    n = lib().nb_nvls_ar_round(nbytes, round_bytes, int(ramp), 0, C.byref(b), C.byref(l))
+    assert n >= 0
+    out = []
+    for s in range(n):
+        lib().nb_nvls_ar_round(nbytes, round_bytes, int(ramp), s, C.byref(b), C.byref(l))
+        out.append((b.value, l.value))
+    return out
 
 
 def group_script(script: str, nranks: int, run_result: int = 0) -> list[str]:

@@ -314,10 +314,15 @@ def check_push_reduce(nranks=3, rounds=4, depth=2, skip_consumed_wait=False, onl
 # NvlsAllReduce (progress words of the NVLS AllReduce kernel)
 # --------------------------------------------------------------------------
 
-def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, only=None) -> Result:
-    """State: cs[r], cph[r] (copier step, 0 wait/copy-out, 1 copy-in+publish),
-    ms[r], mph[r] (mover step, 0 wait, 1 read, 2 write+publish), cflag[r],
-    mflag[r], buf[r][b][q] = (round, 0 input | 1 reduced) or None, bad."""
+def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, in_first=True, only=None) -> Result:
+    """State: cs[r], cph[r] (copier step and phase), ms[r], mph[r] (mover
+    step, 0 wait, 1 read, 2 write+publish), cflag[r], mflag[r],
+    buf[r][b][q] = (round, 0 input | 1 reduced) or None, bad.
+
+    Copier step s. `in_first` (the kernel's order): phase 0 copies round s in
+    (A(s)) and publishes s+1; phase 1 waits for every rank's B(s-2) and copies
+    round s-2 out (C(s-2)). Otherwise (the earlier order): phase 0 waits and
+    copies out C(s-2), phase 1 copies in A(s) and publishes s+1."""
     N, R, B = nranks, rounds, bufs
     empty = tuple(tuple(tuple(None for _ in range(N)) for _ in range(B)) for _ in range(N))
     init = (tuple([0] * N), tuple([0] * N), tuple([0] * N), tuple([0] * N),
@@ -330,25 +335,35 @@ def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, only=
         return tuple(tuple(tuple(val if (r in ranks and bb == b and q in slices) else buf[r][bb][q]
                                  for q in range(N)) for bb in range(B)) for r in range(N))
 
+    def copy_out(st, r, s_, nxt_cs, nxt_cph):
+        """C(s-2) after every rank's B(s-2); None while waiting."""
+        cs, cph, ms, mph, cflag, mflag, buf, bad = st
+        if s_ < 2:
+            return (nxt_cs, nxt_cph, ms, mph, cflag, mflag, buf, bad)
+        if not all(mflag[q] >= s_ - 1 for q in range(N)):
+            return None
+        i = s_ - 2
+        wrong = any(buf[r][i % B][q] != (i, 1) for q in range(N))
+        return (nxt_cs, nxt_cph, ms, mph, cflag, mflag, buf, bad or wrong)
+
+    def copy_in(st, r, s_, nxt_cs, nxt_cph):
+        """A(s) into buffer s%B, then publish s+1."""
+        cs, cph, ms, mph, cflag, mflag, buf, bad = st
+        nb = setbuf(buf, {r}, s_ % B, set(range(N)), (s_, 0)) if s_ < R else buf
+        return (nxt_cs, nxt_cph, ms, mph, setv(cflag, r, s_ + 1), mflag, nb, bad)
+
     def actions(st):
         cs, cph, ms, mph, cflag, mflag, buf, bad = st
         for r in range(N):
             s_ = cs[r]
             if s_ < R + 2:
+                first, second = (copy_in, copy_out) if in_first else (copy_out, copy_in)
                 if cph[r] == 0:
-                    if s_ >= 2:
-                        if not all(mflag[q] >= s_ - 1 for q in range(N)):
-                            pass
-                        else:
-                            i = s_ - 2
-                            wrong = any(buf[r][i % B][q] != (i, 1) for q in range(N))
-                            yield (cs, setv(cph, r, 1), ms, mph, cflag, mflag, buf, bad or wrong)
-                    else:
-                        yield (cs, setv(cph, r, 1), ms, mph, cflag, mflag, buf, bad)
+                    nxt = first(st, r, s_, cs, setv(cph, r, 1))
                 else:
-                    nb = setbuf(buf, {r}, s_ % B, set(range(N)), (s_, 0)) if s_ < R else buf
-                    yield (setv(cs, r, s_ + 1), setv(cph, r, 0), ms, mph, setv(cflag, r, s_ + 1), mflag,
-                           nb, bad)
+                    nxt = second(st, r, s_, setv(cs, r, s_ + 1), setv(cph, r, 0))
+                if nxt is not None:
+                    yield nxt
             s_ = ms[r]
             if s_ < R:
                 if mph[r] == 0:
@@ -422,7 +437,7 @@ SPECS = {
     "PushReduceN": (check_push_reduce, {"N": "nranks", "R": "rounds", "D": "depth",
                                         "SkipConsumedWait": "skip_consumed_wait"}),
     "NvlsAllReduceN": (check_nvls_allreduce, {"N": "nranks", "R": "rounds", "B": "bufs",
-                                              "MoverWaitsAll": "mover_waits_all"}),
+                                              "MoverWaitsAll": "mover_waits_all", "InFirst": "in_first"}),
     "BroadcastChainN": (check_broadcast_chain, {"N": "nranks", "S": "steps", "SkipWait": "skip_wait"}),
 }
 

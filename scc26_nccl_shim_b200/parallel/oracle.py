@@ -49,7 +49,8 @@ KIND_INDEX = {"allreduce": 0, "allgather": 1, "reducescatter": 2, "broadcast": 3
 # Route names of the NCCL_B200_ALGO syntax, per kind.
 FORCE_NAMES = {
     "allreduce": {"twoshot": "ar_twoshot", "oneshot": "ar_oneshot", "nvls": "ar_nvls",
-                  "staged": "ar_staged", "push": "ar_push", "hybrid": "ar_hybrid"},
+                  "staged": "ar_staged", "push": "ar_push", "hybrid": "ar_hybrid",
+                  "twoshot_ll": "ar_twoshot_ll"},
     "reducescatter": {"pull": "rs_pull", "staged": "rs_staged", "nvls": "rs_nvls", "push": "rs_push",
                       "hybrid": "rs_hybrid"},
     "allgather": {"pull": "ag_pull", "nvls": "ag_nvls", "push": "ag_push"},
@@ -59,7 +60,7 @@ FORCE_NAMES = {
 SWITCH_ROUTES = {"ar_nvls", "bc_nvls", "ag_nvls", "rs_nvls", "ar_hybrid", "rs_hybrid"}
 ALGO_IDS = ["fallback", "ar_twoshot", "ar_nvls", "rs_pull", "ag_pull", "bc_pull", "bc_scatter",
             "ar_staged", "rs_staged", "bc_chain", "bc_nvls", "ag_nvls", "rs_nvls", "ag_push", "bc_ring",
-            "rs_push", "ar_push", "ar_hybrid", "ar_oneshot", "rs_hybrid"]
+            "rs_push", "ar_push", "ar_hybrid", "ar_oneshot", "rs_hybrid", "ar_twoshot_ll"]
 
 
 def parse_size(s: str | None) -> int | None:
@@ -147,6 +148,7 @@ def valid(route: str, kind: str, n: int, dtype: str, op: str, nvls: bool) -> boo
     table = {
         "ar_twoshot": kind == "allreduce",
         "ar_oneshot": kind == "allreduce" and n >= 2 and dtype in SWITCH_TYPES,
+        "ar_twoshot_ll": kind == "allreduce" and n >= 2 and dtype in SWITCH_TYPES,
         "ar_nvls": kind == "allreduce" and nvls and n >= 2 and dtype in SWITCH_TYPES and switch_op,
         "ar_hybrid": kind == "allreduce" and nvls and n >= 2 and dtype in SWITCH_TYPES and switch_op,
         "ar_staged": kind == "allreduce",
@@ -245,5 +247,5 @@ def expected_route(kind: str, dtype: str, op: str, count: int, n: int, *, inplac
     if route in SWITCH_ROUTES and (not aligned or (op == "premulsum" and not uniform_scalar)):
         route = static_route(kind, n, dtype, op, False, rules)
     if route == "ar_oneshot" and inplace and n > 1:
-        route = "ar_twoshot"
+        route = "ar_twoshot_ll"
     return route

@@ -117,7 +117,8 @@ def standard_cases(n: int, scale: int = 1) -> list[Case]:
 
 def pipeline_cases(n: int, env: dict, sms: int) -> list[Case]:
     """-1/0/+1 vector (32 bytes of fp32) around the edges of the engines'
-    pipelines: the NVLS round (AllReduce message; per-slot part of a round
+    pipelines: the NVLS round (AllReduce message, and the 4R start of the
+    ramped round schedule; per-slot part of a round
     for ReduceScatter/AllGather), the push-reduce round of 256 KiB pieces per
     block (per segment), the push chain's step (chunk x blocks) and the
     host-lane piece. Each case runs on whatever route the environment picks;
@@ -138,6 +139,10 @@ def pipeline_cases(n: int, env: dict, sms: int) -> list[Case]:
                 out.append(Case(f"edge_{name}_{d:+d}", kind, "float32", c))
     add("nvls_round_ar", "allreduce", R)
     add("nvls_round2_ar", "allreduce", 2 * R)
+    # Ramped AllReduce schedule (first and last rounds R/8 .. R/2) from 4R on,
+    # and a partial uniform round between the ramps.
+    add("nvls_ramp_ar", "allreduce", 4 * R)
+    add("nvls_ramp_part_ar", "allreduce", 5 * R + R // 16)
     add("nvls_part_rs", "reducescatter", part)
     add("nvls_part_ag", "allgather", part)
     add("ring_step_bc", "broadcast", step)

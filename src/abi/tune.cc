@@ -32,9 +32,11 @@ struct Candidate {
 };
 
 // NVLS AllReduce kernel shapes tried (movers per block, requests in flight per
-// mover, round MiB): the switch side bounds the kernel, so more requests in
-// flight and smaller rounds (a shorter pipeline fill and drain) may pay.
-constexpr int kNvlsShapes[][3] = {{0, 0, 0}, {608, 4, 0}, {608, 8, 0}, {512, 8, 128}, {608, 8, 64}};
+// mover, round MiB, round schedule): the switch side bounds the kernel, so
+// more requests in flight, smaller rounds and ramped first and last rounds
+// (a shorter pipeline fill and drain) may pay.
+constexpr int kNvlsShapes[][4] = {{0, 0, 0, 0},   {608, 4, 0, 0},  {608, 8, 0, 0},  {512, 8, 128, 0},
+                                  {608, 8, 64, 0}, {0, 0, 0, 2},    {608, 8, 0, 2}};
 
 // Every candidate route of a kind; a host-lane variant is added wherever the
 // rate model (measured PCIe, NVLink and fold rates) predicts a host share.
@@ -48,6 +50,7 @@ std::vector<Candidate> tiny_candidates(Kind k, int n, bool nvls) {
   switch (k) {
     case Kind::AllReduce:
       add(Algo::ArOneShot);
+      add(Algo::ArTwoShotLL);
       add(Algo::ArTwoShot);
       if (nvls) add(Algo::ArNvls);
       break;
@@ -85,6 +88,7 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
   switch (k) {
     case Kind::AllReduce:
       add(Algo::ArTwoShot, 0);
+      v.push_back({Algo::ArTwoShotLL, 0, 0, 0, 0});
       if (small) {
         add(Algo::ArStaged, 0, 64, 3);
         add(Algo::ArStaged, 0, 128, 2);
@@ -92,7 +96,7 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
       }
       if (nvls && n >= 2)
         for (const auto& sh : kNvlsShapes)
-          v.push_back({Algo::ArNvls, 0, 0, 0, 0, 0, 0, pack_nvls_shape(sh[0], sh[1], sh[2])});
+          v.push_back({Algo::ArNvls, 0, 0, 0, 0, 0, 0, pack_nvls_shape(sh[0], sh[1], sh[2], sh[3])});
       v.push_back({Algo::ArPush, 0, 0, 0, 0});
       break;
     case Kind::ReduceScatter:

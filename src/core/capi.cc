@@ -12,6 +12,7 @@
 #include "core/bufclass.h"
 #include "core/calib_model.h"
 #include "core/clique.h"
+#include "core/nvls_sched.h"
 #include "core/exec_loop.h"
 #include "core/fault.h"
 #include "core/gate.h"
@@ -334,6 +335,20 @@ uint16_t nb_float_to_bf16(float f) { return float_to_bf16(f); }
 float nb_bf16_to_float(uint16_t h) { return bf16_to_float(h); }
 
 // Policy field readback for tests: returns the value as a double.
+// The NVLS AllReduce round schedule: the number of rounds, and round s's
+// [base, base + len) when s is below it.
+int nb_nvls_ar_round(uint64_t bytes, uint64_t round, int ramp, unsigned s, uint64_t* base, uint64_t* len) {
+  if (round == 0) return -1;
+  const unsigned n = ar_rounds(bytes, round, ramp);
+  if (s < n) {
+    unsigned long long b = 0, l = 0;
+    ar_round(s, bytes, round, ramp, &b, &l);
+    *base = b;
+    *len = l;
+  }
+  return int(n);
+}
+
 double nb_policy_value(const char* env, const char* field) {
   const Policy p = EnvMap(env).policy();
   const std::string f(field);
@@ -362,6 +377,7 @@ double nb_policy_value(const char* env, const char* field) {
   if (f == "hybrid_nvls_ppm") return p.hybrid_nvls_ppm;
   if (f == "hybrid_blocks") return p.hybrid_blocks;
   if (f == "nvls_tma") return p.nvls_tma;
+  if (f == "nvls_ramp") return p.nvls_ramp;
   if (f == "nvls_trace") return p.nvls_trace;
   if (f == "nvtx") return p.nvtx;
   if (f == "nvls_movers") return p.nvls_movers;

@@ -64,6 +64,7 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
              (op == RedOp::Sum || op == RedOp::Avg || op == RedOp::PreMulSum);
     case Algo::ArOneShot:
+    case Algo::ArTwoShotLL:
       return k == Kind::AllReduce && nranks >= 2 && (t == DType::F32 || t == DType::F16 || t == DType::BF16);
     case Algo::RsPull: return k == Kind::ReduceScatter;
     case Algo::AgPull: return k == Kind::AllGather;

@@ -754,6 +754,7 @@ void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p, const Shares
     op.nvls_movers = uint16_t(std::max(0, s.nvls_movers));
     op.nvls_unroll = uint8_t(std::max(0, s.nvls_unroll));
     op.nvls_round = size_t(std::max(0, s.nvls_round_mib)) << 20;
+    op.nvls_ramp = uint8_t(std::clamp(s.nvls_ramp, 0, 2));
   }
   b.plan().needs.nvls_bytes = p.nvls_round_bytes;
   b.plan().sm_bytes += d.bytes * size_t(n);  // ~S in and S out per GPU via the switch
@@ -873,6 +874,22 @@ void plan_ar_oneshot(Builder& b, const CliqueDesc& d) {
   b.plan().sm_bytes += d.bytes * size_t(n - 1) * size_t(n);
 }
 
+// Low-latency two-shot AllReduce (exec/oneshot.cu, two-shot mode): the same
+// gang kernel per rank on its caller stream and no events; rank r folds
+// slice r from every input and stores it into every rank's output, between
+// the in-kernel arrive and depart barriers. In place is safe: each element
+// of slice r is read and written by the same thread of rank r only.
+void plan_ar_twoshot_ll(Builder& b, const CliqueDesc& d) {
+  const int n = b.n();
+  for (int r = 0; r < n; ++r) {
+    size_t off, len;
+    slice_of(d.bytes, n, r, &off, &len);
+    b.nvls({Strm::Caller, uint8_t(r), 0}, r, len, off);
+  }
+  b.plan().needs.oneshot = true;
+  b.plan().sm_bytes += d.bytes * size_t(2 * (n - 1));
+}
+
 // One rank: every collective except a scaled one (PreMulSum) is a copy of
 // the input into the output: the SM stream copy kernel on the caller stream,
 // beside an optional copy-engine share (the leading ce_ppm of the bytes, on
@@ -906,10 +923,11 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
   }
   bool in_place = false;
   for (int r = 0; r < d.nranks; ++r) in_place = in_place || d.in_place[r];
-  if (algo == Algo::ArOneShot && in_place) algo = Algo::ArTwoShot;
+  if (algo == Algo::ArOneShot && in_place) algo = Algo::ArTwoShotLL;
   b.plan().algo = algo;
   switch (algo) {
     case Algo::ArOneShot: plan_ar_oneshot(b, d); break;
+    case Algo::ArTwoShotLL: plan_ar_twoshot_ll(b, d); break;
     case Algo::ArTwoShot: plan_ar_twoshot(b, d, s); break;
     case Algo::ArNvls: plan_ar_nvls(b, d, p, s); break;
     case Algo::RsPull: plan_rs_pull(b, d, s); break;

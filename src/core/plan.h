@@ -104,9 +104,11 @@ struct PlanOp {
   size_t bytes = 0;
   uint16_t grid = 0;  // gang ops: blocks per GPU (0 = one per SM)
   // NVLS gang ops: the kernel's shape (0 = the policy's): switch-side
-  // threads per block, multimem requests in flight per thread, round bytes.
+  // threads per block, multimem requests in flight per thread, round bytes,
+  // AllReduce round schedule (1 uniform, 2 ramped).
   uint16_t nvls_movers = 0;
   uint8_t nvls_unroll = 0;
+  uint8_t nvls_ramp = 0;
   size_t nvls_round = 0;
 };
 
@@ -138,6 +140,7 @@ struct Shares {
   int nvls_movers = 0;
   int nvls_unroll = 0;
   int nvls_round_mib = 0;
+  int nvls_ramp = 0;  // 0 = the policy's, 1 = uniform rounds, 2 = ramped
 };
 
 struct Plan {

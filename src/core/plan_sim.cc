@@ -240,11 +240,10 @@ std::string check_plan(const Plan& plan, const SimLayout& lay) {
     data_index[size_t(g.gang)] = int(data_nodes.size());
     data_nodes.push_back(g.gang);
     acc.emplace_back();
+    // Every member's range (the low-latency two-shot gives each rank its
+    // own slice; the other gangs repeat one range).
     for (const PlanOp& op : plan.ops)
-      if (op.kind == OpKind::NvlsReduce) {
-        accesses_of(op, lay, plan.desc, acc.back());
-        break;
-      }
+      if (op.kind == OpKind::NvlsReduce) accesses_of(op, lay, plan.desc, acc.back());
   }
   // The reduction kernels issue 16-byte vector accesses: every reduce operand
   // must start on a 16-byte boundary of its (16-byte aligned) buffer.
@@ -354,16 +353,22 @@ std::string simulate_plan(const Plan& plan, const SimLayout& lay, const FoldPara
   for (int v : order) {
     if (v == g.gang) {
       // The whole gang collective for every rank at once (an AllReduce gang
-      // over its ops' range).
+      // over the union of its ops' ranges: one shared range, or one slice
+      // per rank for the low-latency two-shot).
       size_t bytes = plan.desc.bytes, goff = 0;
       const size_t slot = plan.desc.bytes;  // ReduceScatter: the stride between slots
-      if (plan.desc.kind == Kind::AllReduce || plan.desc.kind == Kind::ReduceScatter)
+      if (plan.desc.kind == Kind::AllReduce || plan.desc.kind == Kind::ReduceScatter) {
+        size_t lo = ~size_t(0), hi = 0;
         for (const PlanOp& op : plan.ops)
           if (op.kind == OpKind::NvlsReduce) {
-            bytes = op.bytes;
-            goff = op.src[0].off;
-            break;
+            lo = std::min(lo, op.src[0].off);
+            hi = std::max(hi, op.src[0].off + op.bytes);
           }
+        if (hi > lo) {
+          goff = lo;
+          bytes = hi - lo;
+        }
+      }
       auto send = [&](int q) { return arenas[size_t(q)].data() + lay.send_off[q] + goff; };
       auto recv = [&](int q) { return arenas[size_t(q)].data() + lay.recv_off[q] + goff; };
       switch (plan.desc.kind) {

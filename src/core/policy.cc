@@ -54,6 +54,7 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   if (a == "nccl" || a == "fallback") *algo = Algo::Fallback;
   else if (a == "twoshot" && *kind == Kind::AllReduce) *algo = Algo::ArTwoShot;
   else if (a == "oneshot" && *kind == Kind::AllReduce) *algo = Algo::ArOneShot;
+  else if (a == "twoshot_ll" && *kind == Kind::AllReduce) *algo = Algo::ArTwoShotLL;
   else if (a == "nvls" && *kind == Kind::AllReduce) *algo = Algo::ArNvls;
   else if (a == "pull" && *kind == Kind::ReduceScatter) *algo = Algo::RsPull;
   else if (a == "pull" && *kind == Kind::AllGather) *algo = Algo::AgPull;
@@ -106,6 +107,7 @@ Policy policy_from_env(const EnvLookup& env) {
   if (parse_int(env("NCCL_B200_NVLS_UNROLL"), &i) && (i == 4 || i == 8)) p.nvls_unroll = int(i);
   if (parse_bool(env("NCCL_B200_NVLS_TRACE"), &b)) p.nvls_trace = b;
   if (parse_bool(env("NCCL_B200_NVLS_TMA"), &b)) p.nvls_tma = b;
+  if (parse_bool(env("NCCL_B200_NVLS_RAMP"), &b)) p.nvls_ramp = b;
   if (const char* v = env("NCCL_B200_LOCAL_COPY")) {
     if (std::strcmp(v, "tma") == 0) p.local_copy_tma = true;
     else if (std::strcmp(v, "sm") == 0) p.local_copy_tma = false;

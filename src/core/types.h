@@ -56,6 +56,7 @@ enum class Algo : uint8_t {
   ArHybrid,    // NVLS on part of the SMs for one share, two-shot P2P for the rest
   ArOneShot,   // every rank folds the whole message from all inputs into its own output
   RsHybrid,    // NVLS ReduceScatter on part of the SMs for one share, P2P pulls for the rest
+  ArTwoShotLL, // two-shot in one gang kernel per rank: in-kernel arrive/depart instead of events
   Count
 };
 

@@ -365,7 +365,8 @@ cudaError_t Executor::submit(const PlanOp& op, const Plan& plan, const Binding& 
       launches_.fetch_add(1, std::memory_order_relaxed);
       if (plan.algo == Algo::BcRing) return ring_launch(op, plan, b, policy_, s);
       if (plan.algo == Algo::RsPush || plan.algo == Algo::ArPush) return pushred_launch(op, plan, b, policy_, s);
-      if (plan.algo == Algo::ArOneShot) return oneshot_launch(op, plan, b, policy_, s);
+      if (plan.algo == Algo::ArOneShot || plan.algo == Algo::ArTwoShotLL)
+        return oneshot_launch(op, plan, b, policy_, s);
       return nvls_launch(op, plan, b, policy_, s, dev);
     default:
       return cudaErrorNotSupported;

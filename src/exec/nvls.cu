@@ -30,6 +30,7 @@
 #include <mutex>
 #include <vector>
 
+#include "core/nvls_sched.h"
 #include "exec/nvls.h"
 
 namespace nb {
@@ -55,6 +56,7 @@ struct NvlsArgs {
   int nranks, rank, dtype;
   int scaled;                // multiply the switch's sum by `mul` (Avg, PreMulSum)
   int tma;                   // copier group: TMA bulk pipeline (one warp) instead of SM copies
+  int ramp;                  // AllReduce: ramped first and last rounds (see ar_round)
   float mul;
   int movers;                // threads of a block that work through the switch
   int mode;                  // collective kind (xfer kernel)
@@ -486,12 +488,16 @@ struct Copier {
 
 // AllReduce. Warp specialization: movers reduce through the switch
 // (NVLink-bound), copiers stream rounds in and out of the scratch
-// (HBM-bound). Rounds of R bytes cut into N slices; rank r owns slice r.
-//   copier step s: C(s-2) after every rank's B(s-2); A(s); publish s+1.
+// (HBM-bound). Rounds (ar_round) cut into N slices; rank r owns slice r.
+//   copier step s: A(s); publish s+1; then C(s-2) after every rank's B(s-2).
 //   mover  step s: B(s) after every rank's A(s); publish s+1.
-// A(s) reuses buffer s%3 after every rank's B(s-3) (implied by the wait
-// before C(s-2)); B(s) stores into every rank's buffer s%3 after that rank's
-// A(s), hence after its C(s-3). U: multimem requests in flight per thread.
+// A(s) reuses buffer s%3: every rank's B(s-3) is done (waited for before
+// C(s-3), in the previous step) and so is this rank's C(s-3) (its loads
+// complete before any later store is issued; the SM copier syncs the group).
+// B(s) stores into every rank's buffer s%3 after that rank's A(s), hence
+// after its C(s-3). Copy-in first keeps the copier up to two rounds ahead
+// of the movers: after B(s-2) it has C(s-2) and A(s+1) to do while the
+// movers run B(s-1) and B(s). U: multimem requests in flight per thread.
 template <int U, int DT, bool TMA>
 __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(const __grid_constant__ NvlsArgs a) {
   extern __shared__ __align__(128) unsigned char dsmem[];
@@ -505,13 +511,12 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
   trace_begin(g);
   __syncthreads();
   const int n = a.nranks;
-  const unsigned rounds = unsigned((a.bytes + a.round - 1) / a.round);
+  const unsigned rounds = ar_rounds(a.bytes, a.round, a.ramp);
   if (g.mover) {
     for (unsigned s = 0; s < rounds; ++s) {
       if (!group_wait(a, g, kCopier, a.base + s + 1, -1)) return;
-      const unsigned long long rbase = s * a.round;
-      const unsigned long long rlen = min(a.round, a.bytes - rbase);
-      unsigned long long lo, hi;
+      unsigned long long rbase, rlen, lo, hi;
+      ar_round(s, a.bytes, a.round, a.ramp, &rbase, &rlen);
       portion(rlen, n, a.rank, &lo, &hi);
       char* base = a.mc + (s % 3) * a.buf_stride + lo;
       strided<U>(
@@ -523,22 +528,9 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
   } else {
     Copier<TMA> cp(a, g, dsmem, tma_bar, tma_dst, tma_size);
     for (unsigned s = 0; s < rounds + 2; ++s) {
-      if (s >= 2) {
-        if (!group_wait(a, g, kMover, a.base + s - 1, -1)) break;
-        cp.acquired();
-        const unsigned i = s - 2;
-        const unsigned long long rbase = i * a.round;
-        const unsigned long long rlen = min(a.round, a.bytes - rbase);
-        const char* buf = a.uc + (i % 3) * a.buf_stride;
-        for (int q = 0; q < n; ++q) {
-          unsigned long long lo, hi;
-          portion(rlen, n, q, &lo, &hi);
-          cp.copy(a.recv + rbase + lo, buf + lo, hi - lo);
-        }
-      }
       if (s < rounds) {
-        const unsigned long long rbase = s * a.round;
-        const unsigned long long rlen = min(a.round, a.bytes - rbase);
+        unsigned long long rbase, rlen;
+        ar_round(s, a.bytes, a.round, a.ramp, &rbase, &rlen);
         char* buf = a.uc + (s % 3) * a.buf_stride;
         for (int q = 0; q < n; ++q) {
           unsigned long long lo, hi;
@@ -548,7 +540,24 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
       }
       cp.flush();
       group_publish(a, g, a.base + s + 1);
+      if (s >= 2) {
+        if (!group_wait(a, g, kMover, a.base + s - 1, -1)) break;
+        cp.acquired();
+        const unsigned i = s - 2;
+        unsigned long long rbase, rlen;
+        ar_round(i, a.bytes, a.round, a.ramp, &rbase, &rlen);
+        const char* buf = a.uc + (i % 3) * a.buf_stride;
+        for (int q = 0; q < n; ++q) {
+          unsigned long long lo, hi;
+          portion(rlen, n, q, &lo, &hi);
+          cp.copy(a.recv + rbase + lo, buf + lo, hi - lo);
+        }
+        // The SM copier's threads read C(s-2) and write A(s+1) in different
+        // parts of the same buffer when the rounds differ in length.
+        if (!TMA || !a.tma) group_sync(false, g.nt);
+      }
     }
+    cp.flush();
     cp.finish();
   }
   trace_end(a, g);
@@ -931,8 +940,9 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   // The largest progress value this call publishes (every rank the same):
   // the next call's epoch.
   unsigned long long steps = 0;
+  a.ramp = ar && (op.nvls_ramp ? op.nvls_ramp == 2 : p.nvls_ramp) ? 1 : 0;
   if (ar) {
-    steps = (a.bytes + a.round - 1) / a.round + 2;
+    steps = ar_rounds(a.bytes, a.round, a.ramp) + 2ull;
   } else {
     const bool bc = plan.desc.kind == Kind::Broadcast;
     const unsigned long long part = bc ? a.round : ((a.round / (unsigned long long)b.nranks) & ~31ull);

@@ -1,5 +1,5 @@
-// Low-latency one-shot AllReduce over peer memory, synchronized inside the
-// kernel instead of by cross-device events.
+// Low-latency one-shot and two-shot AllReduce over peer memory, synchronized
+// inside the kernel instead of by cross-device events.
 //
 // One kernel per rank, launched on the caller's own stream with nothing
 // around it. Block b of every rank's kernel:
@@ -8,13 +8,17 @@
 //      rank's stream has reached the call, so its whole input is ready;
 //   2. waits until every peer's block b arrived here (relaxed polls of this
 //      GPU's own table, then one acquire fence);
-//   3. folds its share of the message (grid-stride 16/32-byte vectors) from
+//   3. folds its share of its range (grid-stride 16/32-byte vectors) from
 //      all N inputs in rank order -- its own from HBM, the peers' over
-//      NVLink -- with fp32 accumulation, and stores only this rank's output;
+//      NVLink -- with fp32 accumulation. One-shot: the range is the whole
+//      message and the result goes to this rank's output only. Two-shot:
+//      the range is slice r and the result goes to slice r of every rank's
+//      output (P2P stores), so each GPU moves 2(N-1)/N of the message
+//      instead of N-1 times it;
 //   4. departs: stores the epoch into the peers' depart tables, and waits
 //      until every peer's block b departed, i.e. finished reading this
-//      rank's input; only then may this rank's stream go on (the caller may
-//      overwrite the input).
+//      rank's input and (two-shot) writing this rank's output; only then may
+//      this rank's stream go on (the caller may reuse both buffers).
 // A call thus costs N kernel launches and no event traffic: the two
 // cross-device event fans of an event-ordered plan (every stream waiting on
 // every peer before and after) are what bound small messages otherwise.
@@ -53,8 +57,9 @@ namespace {
 using namespace kfold;
 
 struct OsArgs {
-  const void* src[kMaxRanks];         // every rank's input (peer pointers)
-  void* dst;                          // this rank's output
+  const void* src[kMaxRanks];         // every rank's input at the range (peer pointers)
+  void* dst[kMaxRanks];               // outputs at the range: this rank's (one-shot) or every rank's
+  int ndst;
   const void* dev_scalar[kMaxRanks];  // PreMulSum scalars in device memory, per rank
   double scale[kMaxRanks];            // host PreMulSum scalars, per rank
   unsigned* arrive_mine;              // this GPU's tables: [block][rank]
@@ -197,7 +202,7 @@ __global__ void __launch_bounds__(512) oneshot_kernel(const __grid_constant__ Os
           for (int k = 0; k < NSRC; ++k) part[k] = v[u][k].h[j];
           out.h[j] = fold_vec<T, NSRC>(part, a.op, a.nranks, s);
         }
-        st_vec<VB>(static_cast<char*>(a.dst) + i * VB, out);
+        for (int q = 0; q < a.ndst; ++q) st_vec<VB>(static_cast<char*>(a.dst[q]) + i * VB, out);
       }
     }
   }
@@ -206,7 +211,8 @@ __global__ void __launch_bounds__(512) oneshot_kernel(const __grid_constant__ Os
     A acc = first<T>(static_cast<const T*>(a.src[0])[e], a.op, s[0]);
 #pragma unroll
     for (int k = 1; k < NSRC; ++k) acc = combine<T>(acc, static_cast<const T*>(a.src[k])[e], a.op, s[k]);
-    static_cast<T*>(a.dst)[e] = finish<T>(acc, a.op, a.nranks);
+    const T out = finish<T>(acc, a.op, a.nranks);
+    for (int q = 0; q < a.ndst; ++q) static_cast<T*>(a.dst[q])[e] = out;
   }
   __syncthreads();
   block_barrier(a, a.depart_peer, a.depart_mine, &abort_flag);
@@ -346,9 +352,16 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
     }
   }
   const size_t es = elem_size(plan.desc.dtype);
-  const size_t bytes = plan.desc.bytes;
-  uintptr_t any = reinterpret_cast<uintptr_t>(b.recv[r]);
-  for (int q = 0; q < n; ++q) any |= reinterpret_cast<uintptr_t>(b.send[q]);
+  // One-shot: the whole message into this rank's output. Two-shot: this
+  // rank's slice (the plan op's range) into every rank's output.
+  const bool two = plan.algo == Algo::ArTwoShotLL;
+  const size_t off = two ? op.src[0].off : 0;
+  const size_t bytes = two ? op.bytes : plan.desc.bytes;
+  uintptr_t any = reinterpret_cast<uintptr_t>(b.recv[r]) | off;
+  for (int q = 0; q < n; ++q) {
+    any |= reinterpret_cast<uintptr_t>(b.send[q]);
+    if (two) any |= reinterpret_cast<uintptr_t>(b.recv[q]);
+  }
   if (!es || bytes % es || any % 16) return cudaErrorInvalidValue;
   const bool wide = any % 32 == 0;
   const int vb = wide ? 32 : 16;
@@ -356,13 +369,14 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
   if (!fn) return cudaErrorInvalidValue;
   OsArgs a{};
   for (int q = 0; q < n; ++q) {
-    a.src[q] = b.send[q];
+    a.src[q] = static_cast<const char*>(b.send[q]) + off;
     a.dev_scalar[q] = b.dev_scalar[q];
     a.scale[q] = b.fold.scalars[q];
     a.arrive_peer[q] = c->arrive[size_t(q)];
     a.depart_peer[q] = c->depart[size_t(q)];
   }
-  a.dst = b.recv[r];
+  a.ndst = two ? n : 1;
+  for (int q = 0; q < a.ndst; ++q) a.dst[q] = static_cast<char*>(b.recv[two ? q : r]) + off;
   a.arrive_mine = c->arrive[size_t(r)];
   a.depart_mine = c->depart[size_t(r)];
   a.nvec = bytes / size_t(vb);
@@ -374,12 +388,14 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
   a.op = int(b.fold.op);
   a.nranks = n;
   a.rank = r;
-  // One block per 8 KiB of output, at least 8 and at most one per SM: the
-  // peers' inputs come over NVLink, and each SM sustains only a share of the
-  // link rate, so even a 1 MiB message is spread over 128 SMs. Every rank
-  // uses the same grid (block b pairs with block b everywhere).
+  // One block per 8 KiB of this rank's range, at least 8 and at most one
+  // per SM: the peers' inputs come over NVLink, and each SM sustains only a
+  // share of the link rate, so even a 1 MiB range is spread over 128 SMs.
+  // Every rank uses the same grid (block b pairs with block b everywhere),
+  // so the two-shot grid follows the common slice length, not this rank's.
+  const size_t span = two ? plan.desc.bytes / size_t(n) : plan.desc.bytes;
   const unsigned blocks =
-      unsigned(std::min<size_t>(std::max<size_t>(8, (bytes + 8191) / 8192), size_t(c->blocks)));
+      unsigned(std::min<size_t>(std::max<size_t>(8, (span + 8191) / 8192), size_t(c->blocks)));
   cudaError_t e = cudaSuccess;
   {
     void* argv[] = {&a};

@@ -201,6 +201,8 @@ def test_policy_parsing_of_engine_knobs():
     assert c.policy_value({"NCCL_B200_HYBRID_BLOCKS": "100"}, "hybrid_blocks") == 100
     assert c.policy_value({}, "nvls_tma") == 1
     assert c.policy_value({"NCCL_B200_NVLS_TMA": "0"}, "nvls_tma") == 0
+    assert c.policy_value({}, "nvls_ramp") == 0
+    assert c.policy_value({"NCCL_B200_NVLS_RAMP": "1"}, "nvls_ramp") == 1
     assert c.policy_value({"NCCL_B200_NVLS_TRACE": "1", "NCCL_B200_NVTX": "on"}, "nvls_trace") == 1
     assert c.policy_value({"NCCL_B200_NVTX": "on"}, "nvtx") == 1
     assert c.policy_value({"NCCL_B200_NVLS_MOVERS": "384"}, "nvls_movers") == 384

@@ -20,7 +20,7 @@ CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", 
          ("bc_nvls", "broadcast"), ("ag_nvls", "allgather"), ("rs_nvls", "reducescatter"),
          ("ag_push", "allgather"), ("bc_ring", "broadcast"), ("rs_push", "reducescatter"),
          ("ar_push", "allreduce"), ("ar_hybrid", "allreduce"), ("ar_oneshot", "allreduce"),
-         ("rs_hybrid", "reducescatter")]
+         ("rs_hybrid", "reducescatter"), ("ar_twoshot_ll", "allreduce")]
 
 
 def test_baseline_cpu_plumbing_config():

@@ -185,11 +185,12 @@ for kind, rc, sends, recvs, root in jobs:
 arr = (C.c_int * n)(*devs)
 st = nc.shim.nb_ring_status(arr, n) | nc.shim.nb_pushred_status(arr, n) | nc.shim.nb_oneshot_status(arr, n)
 print("RESULT", bad, st, nc.shim.nb_poisoned(), nc.custom_calls(ALGO["bc_ring"]),
-      nc.custom_calls(ALGO["ar_push"]), nc.custom_calls(ALGO["rs_push"]), nc.custom_calls(ALGO["ar_oneshot"]))
+      nc.custom_calls(ALGO["ar_push"]), nc.custom_calls(ALGO["rs_push"]),
+      nc.custom_calls(ALGO["ar_oneshot"]) + nc.custom_calls(ALGO["ar_twoshot_ll"]))
 """
 
 
-@pytest.mark.parametrize("algo", ["bc=ring,ar=push,rs=push", "ar=oneshot"])
+@pytest.mark.parametrize("algo", ["bc=ring,ar=push,rs=push", "ar=oneshot", "ar=twoshot_ll"])
 @pytest.mark.parametrize("n", [2, 3])
 def test_gang_calls_ordered_across_streams_and_cliques(n, algo):
     """The push chain and the push-reduce engine keep scratch, progress words
@@ -207,7 +208,7 @@ def test_gang_calls_ordered_across_streams_and_cliques(n, algo):
     line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
     bad, status, poisoned, ring, arp, rsp, one = map(int, line[1:])
     assert (bad, status, poisoned) == (0, 0, 0), line
-    if "oneshot" in algo:
+    if "shot" in algo:
         assert one >= 4, line
     else:
         assert ring >= 4 and arp >= 4 and rsp >= 4, line
@@ -229,26 +230,33 @@ for dt in (torch.bfloat16, torch.float16):
     run_kind(nc, "allreduce", comms, devs, (1 << 20) + 9, dtype=dt)
 for op in ("avg", "max", "min", "prod"):
     run_kind(nc, "allreduce", comms, devs, (2 << 20) // 4 + 1, op=op)
-run_kind(nc, "allreduce", comms, devs, (4 << 20) // 4, inplace=True)  # planned as two-shot
-print("RESULT", nc.custom_calls(ALGO["ar_oneshot"]), nc.custom_calls(ALGO["ar_twoshot"]))
+run_kind(nc, "allreduce", comms, devs, (4 << 20) // 4, inplace=True)  # one-shot: planned as two-shot
+print("RESULT", nc.custom_calls(ALGO["ar_oneshot"]), nc.custom_calls(ALGO["ar_twoshot_ll"]))
 for c in comms:
     nc.comm_destroy(c)
 """
 
 
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot_ll"])
 @pytest.mark.parametrize("n", [2, 3, 4, 8])
-def test_forced_oneshot(n):
-    """The low-latency one-shot AllReduce (in-kernel arrive/depart barriers)
-    from 4 bytes up, odd tails, 16-bit types and every op, bit-exact against
-    a torch fp32 fold in rank order; in place it runs the two-shot plan."""
+def test_forced_oneshot(n, algo):
+    """The low-latency one-shot and two-shot AllReduce (in-kernel
+    arrive/depart barriers) from 4 bytes up (slices of a few bytes, empty
+    slices), odd tails, 16-bit types and every op, bit-exact against a torch
+    fp32 fold in rank order; in place the one-shot runs the low-latency
+    two-shot plan."""
     need_gpus(n)
-    env = dict(os.environ, NCCL_B200_ALGO="ar=oneshot", NCCL_B200_TUNE="0", NCCL_B200_FIRST_PASS="0",
+    env = dict(os.environ, NCCL_B200_ALGO="ar=" + algo, NCCL_B200_TUNE="0", NCCL_B200_FIRST_PASS="0",
                NCCL_B200_AR_MIN="1")
     r = subprocess.run([sys.executable, "-c", OS_CHILD.format(repo=REPO, n=n)], env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
-    assert int(line[1]) >= 13 and int(line[2]) >= 1, line
+    one, two = int(line[1]), int(line[2])
+    if algo == "oneshot":
+        assert one >= 13 and two >= 1, line
+    else:
+        assert one == 0 and two >= 14, line
 
 
 OS_TIMEOUT_CHILD = r"""

@@ -89,7 +89,8 @@ def test_stress_ordering_controls(n):
 
 
 GANGS = ["ar=push,rs=push,ag=push,bc=ring", "ar=nvls,rs=nvls,ag=nvls,bc=nvls",
-         "ar=hybrid,rs=hybrid,ag=pull,bc=scatter", "ar=oneshot,rs=pull,ag=pull,bc=pull"]
+         "ar=hybrid,rs=hybrid,ag=pull,bc=scatter", "ar=oneshot,rs=pull,ag=pull,bc=pull",
+         "ar=twoshot_ll,rs=pull,ag=pull,bc=pull"]
 
 
 @pytest.mark.parametrize("algo", GANGS)

@@ -59,13 +59,24 @@ def test_push_reduce_broken_reads_stale(n):
     assert not r.ok and r.violation == "NoStaleRead"
 
 
-@pytest.mark.parametrize("n,rounds,bufs", [(2, 4, 3), (2, 6, 3), (3, 4, 3), (3, 4, 2)])
-def test_nvls_allreduce_holds(n, rounds, bufs):
-    """The NVLS AllReduce's copier/mover progress words, with three round
-    buffers (the kernel's) and with two (also safe: A(s) reuses a buffer only
-    after every rank's B(s-2), which the wait before C(s-2) already needs)."""
-    r = m.check_nvls_allreduce(nranks=n, rounds=rounds, bufs=bufs)
+@pytest.mark.parametrize("n,rounds,bufs,in_first", [(2, 4, 3, True), (2, 6, 3, True), (3, 4, 3, True),
+                                                     (2, 4, 3, False), (3, 4, 3, False), (3, 4, 2, False)])
+def test_nvls_allreduce_holds(n, rounds, bufs, in_first):
+    """The NVLS AllReduce's copier/mover progress words with three round
+    buffers (the kernel's), in the kernel's order (copy-in of round s before
+    copy-out of round s-2) and in the earlier order. The earlier order was
+    also safe with two buffers (A(s) reused a buffer only after every rank's
+    B(s-2), which the wait before C(s-2) already needed)."""
+    r = m.check_nvls_allreduce(nranks=n, rounds=rounds, bufs=bufs, in_first=in_first)
     assert r.ok, (r.violation, r.trace)
+
+
+@pytest.mark.parametrize("n", [2, 3])
+def test_nvls_allreduce_copy_in_first_needs_three_buffers(n):
+    """Copying round s in before round s-2 is out overwrites round s-2's
+    reduced data when there are only two buffers."""
+    r = m.check_nvls_allreduce(nranks=n, rounds=4, bufs=2, in_first=True)
+    assert not r.ok and r.violation == "RoundsInOrder"
 
 
 @pytest.mark.parametrize("n", [2, 3])

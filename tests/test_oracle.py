@@ -75,7 +75,7 @@ def test_oracle_switch_and_inplace_substitutions(n):
         assert got == "nccl" and want in ("ar_twoshot", "rs_pull")
     env = {"NCCL_B200_ALGO": "ar=oneshot", "NCCL_B200_AR_MIN": "1K"}
     assert oracle.expected_route("allreduce", "float32", "sum", 1 << 20, n, inplace=True,
-                                 rules=oracle.Rules(env)) == "ar_twoshot"
+                                 rules=oracle.Rules(env)) == "ar_twoshot_ll"
     assert oracle.expected_route("allreduce", "float32", "sum", 1 << 20, n, inplace=False,
                                  rules=oracle.Rules(env)) == "ar_oneshot"
 

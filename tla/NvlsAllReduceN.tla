@@ -1,9 +1,11 @@
 ---------------------------- MODULE NvlsAllReduceN ----------------------------
 (* One block index of the NVLS AllReduce: N ranks, R rounds, B round       *)
-(* buffers of N slices per rank. Copier of rank r, step s (0..R+1): when    *)
-(* s >= 2 it waits until every mover published s - 1 and copies buffer     *)
-(* (s-2) % B out (CopyOut: every slice must hold round s-2 reduced); when   *)
-(* s < R it copies input round s into buffer s % B; then publishes s + 1.   *)
+(* buffers of N slices per rank. Copier of rank r, step s (0..R+1), two     *)
+(* actions: CopyIn (when s < R, copy input round s into buffer s % B, then  *)
+(* publish s + 1) and CopyOut (when s >= 2, wait until every mover          *)
+(* published s - 1 and copy buffer (s-2) % B out: every slice must hold     *)
+(* round s-2 reduced). With InFirst (the kernel's order) CopyIn comes      *)
+(* first in the step, else CopyOut.                                         *)
 (* Mover of rank r, step s < R: waits until every copier published s + 1   *)
 (* (only its own when not MoverWaitsAll), reads slice r of buffer s % B on  *)
 (* every rank (the switch's ld_reduce: must hold round s input), then       *)
@@ -11,7 +13,7 @@
 (* and publishes s + 1. Reading and writing are separate steps.            *)
 EXTENDS Integers
 
-CONSTANTS N, R, B, MoverWaitsAll
+CONSTANTS N, R, B, MoverWaitsAll, InFirst
 VARIABLES cs, cph, ms, mph, cflag, mflag, buf, bad
 vars == <<cs, cph, ms, mph, cflag, mflag, buf, bad>>
 
@@ -24,18 +26,24 @@ Init == /\ cs = [r \in Ranks |-> 0] /\ cph = [r \in Ranks |-> 0]
         /\ buf = [r \in Ranks |-> [b \in 0..(B - 1) |-> [q \in Ranks |-> Empty]]]
         /\ bad = FALSE
 
+\* The phase of the step each copier action takes, and what follows it.
+OutPhase == IF InFirst THEN 1 ELSE 0
+InPhase == IF InFirst THEN 0 ELSE 1
+
 CopyOut(r) == LET s == cs[r] IN
-              /\ s < R + 2 /\ cph[r] = 0
+              /\ s < R + 2 /\ cph[r] = OutPhase
               /\ s >= 2 => \A q \in Ranks : mflag[q] >= s - 1
               /\ bad' = (bad \/ (s >= 2 /\ \E q \in Ranks : buf[r][(s - 2) % B][q] # <<s - 2, 1>>))
-              /\ cph' = [cph EXCEPT ![r] = 1]
-              /\ UNCHANGED <<cs, ms, mph, cflag, mflag, buf>>
+              /\ IF InFirst THEN cs' = [cs EXCEPT ![r] = s + 1] /\ cph' = [cph EXCEPT ![r] = 0]
+                 ELSE UNCHANGED cs /\ cph' = [cph EXCEPT ![r] = 1]
+              /\ UNCHANGED <<ms, mph, cflag, mflag, buf>>
 
 CopyInPublish(r) == LET s == cs[r] IN
-                    /\ s < R + 2 /\ cph[r] = 1
+                    /\ s < R + 2 /\ cph[r] = InPhase
                     /\ buf' = IF s < R THEN [buf EXCEPT ![r][s % B] = [q \in Ranks |-> <<s, 0>>]]
                               ELSE buf
-                    /\ cs' = [cs EXCEPT ![r] = s + 1] /\ cph' = [cph EXCEPT ![r] = 0]
+                    /\ IF InFirst THEN UNCHANGED cs /\ cph' = [cph EXCEPT ![r] = 1]
+                       ELSE cs' = [cs EXCEPT ![r] = s + 1] /\ cph' = [cph EXCEPT ![r] = 0]
                     /\ cflag' = [cflag EXCEPT ![r] = s + 1]
                     /\ UNCHANGED <<ms, mph, mflag, bad>>
 
