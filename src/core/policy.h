@@ -37,6 +37,7 @@ struct Policy {
   bool nvls_trace = false;          // per-block phase timing in the NVLS kernels
   bool nvls_tma = true;             // NVLS copier: TMA bulk pipeline (else SM copy warps)
   bool nvls_ramp = false;           // NVLS AllReduce: ramped first/last rounds from 4 rounds on
+  bool nvls_strong = true;          // NVLS copier: SM copies with system-scope accesses to the scratch
   bool local_copy_tma = false;      // a large copy within one GPU: TMA bulk copy (else SM stream copy)
   size_t ring_chunk = 256 * 1024;   // Broadcast chain: bytes per block per step
   int hybrid_nvls_ppm = 6000;       // hybrid AllReduce: NVLS share of the message (per 10000)

@@ -57,6 +57,7 @@ struct NvlsArgs {
   int scaled;                // multiply the switch's sum by `mul` (Avg, PreMulSum)
   int tma;                   // copier group: TMA bulk pipeline (one warp) instead of SM copies
   int ramp;                  // AllReduce: ramped first and last rounds (see ar_round)
+  int strong;                // SM copier: strong (system-scope) accesses to the scratch
   float mul;
   int movers;                // threads of a block that work through the switch
   int mode;                  // collective kind (xfer kernel)
@@ -178,6 +179,45 @@ __device__ __forceinline__ void copy16(char* dst, const char* src, unsigned long
     __stcs(d16 + i + nt, b);
   }
   if (i < n16) __stcs(d16 + i, __ldcs(s16 + i));
+}
+
+// copy16 with system-scope relaxed (strong) accesses on one side: `mode` 1
+// loads the source strongly, 2 stores the destination strongly. Used for the
+// scratch side of the SM copier: the scratch is also written and read through
+// the switch, and weak accesses may be served from, or left in, a cache the
+// switch traffic does not see.
+__device__ __forceinline__ void copy16_strong(char* dst, const char* src, unsigned long long bytes, int t,
+                                              int nthreads, int mode) {
+  constexpr int U = 4;
+  const unsigned n16 = unsigned(bytes / 16);
+  const unsigned nt = unsigned(nthreads);
+  auto ld = [&](unsigned i) {
+    uint4 v;
+    const void* p = src + size_t(i) * 16;
+    if (mode == 1)
+      asm volatile("ld.relaxed.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+    else
+      v = __ldcs(reinterpret_cast<const uint4*>(p));
+    return v;
+  };
+  auto st = [&](unsigned i, uint4 v) {
+    void* p = dst + size_t(i) * 16;
+    if (mode == 2)
+      asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                   "r"(v.w) : "memory");
+    else
+      __stcs(reinterpret_cast<uint4*>(p), v);
+  };
+  unsigned i = unsigned(t);
+  for (; i + nt * (U - 1) < n16; i += nt * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = ld(i + u * nt);
+#pragma unroll
+    for (int u = 0; u < U; ++u) st(i + u * nt, v[u]);
+  }
+  for (; i < n16; i += nt) st(i, ld(i));
 }
 
 // Calls st(i, ld(i)) for i = t, t + nt, ... below n, with the U loads of a
@@ -465,9 +505,13 @@ struct Copier {
   __device__ void acquired() {
     if (b.on && g->leader) fence_async_global();
   }
-  __device__ void copy(char* dst, const char* src, unsigned long long bytes) {
+  // `scratch`: 1 when the source is the scratch, 2 when the destination is.
+  __device__ void copy(char* dst, const char* src, unsigned long long bytes, int scratch = 0) {
     if (!b.on) {
-      copy16(dst, src, bytes, g->t, g->nt);
+      if (a->strong && scratch)
+        copy16_strong(dst, src, bytes, g->t, g->nt, scratch);
+      else
+        copy16(dst, src, bytes, g->t, g->nt);
       return;
     }
     if (!g->leader || *g->abort) return;
@@ -528,18 +572,6 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
   } else {
     Copier<TMA> cp(a, g, dsmem, tma_bar, tma_dst, tma_size);
     for (unsigned s = 0; s < rounds + 2; ++s) {
-      if (s < rounds) {
-        unsigned long long rbase, rlen;
-        ar_round(s, a.bytes, a.round, a.ramp, &rbase, &rlen);
-        char* buf = a.uc + (s % 3) * a.buf_stride;
-        for (int q = 0; q < n; ++q) {
-          unsigned long long lo, hi;
-          portion(rlen, n, q, &lo, &hi);
-          cp.copy(buf + lo, a.send + rbase + lo, hi - lo);
-        }
-      }
-      cp.flush();
-      group_publish(a, g, a.base + s + 1);
       if (s >= 2) {
         if (!group_wait(a, g, kMover, a.base + s - 1, -1)) break;
         cp.acquired();
@@ -550,14 +582,22 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
         for (int q = 0; q < n; ++q) {
           unsigned long long lo, hi;
           portion(rlen, n, q, &lo, &hi);
-          cp.copy(a.recv + rbase + lo, buf + lo, hi - lo);
+          cp.copy(a.recv + rbase + lo, buf + lo, hi - lo, 1);
         }
-        // The SM copier's threads read C(s-2) and write A(s+1) in different
-        // parts of the same buffer when the rounds differ in length.
-        if (!TMA || !a.tma) group_sync(false, g.nt);
       }
+      if (s < rounds) {
+        unsigned long long rbase, rlen;
+        ar_round(s, a.bytes, a.round, a.ramp, &rbase, &rlen);
+        char* buf = a.uc + (s % 3) * a.buf_stride;
+        for (int q = 0; q < n; ++q) {
+          unsigned long long lo, hi;
+          portion(rlen, n, q, &lo, &hi);
+          cp.copy(buf + lo, a.send + rbase + lo, hi - lo, 2);
+        }
+      }
+      cp.flush();
+      group_publish(a, g, a.base + s + 1);
     }
-    cp.flush();
     cp.finish();
   }
   trace_end(a, g);
@@ -619,7 +659,7 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_xfer_kernel(const __g
         cp.acquired();
         char* buf = a.uc + (s % 3) * a.buf_stride;
         for (int q = 0; q < n; ++q)
-          cp.copy(buf + q * part + lo, a.send + q * a.slot_stride + s * part + lo, hi - lo);
+          cp.copy(buf + q * part + lo, a.send + q * a.slot_stride + s * part + lo, hi - lo, 2);
         cp.flush();
       }
     } else if (g.mover) {
@@ -636,10 +676,10 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_xfer_kernel(const __g
       cp.acquired();
       const char* buf = a.uc + (s % 3) * a.buf_stride;
       if (bc) {
-        cp.copy(a.recv + s * part + lo, buf + lo, hi - lo);
+        cp.copy(a.recv + s * part + lo, buf + lo, hi - lo, 1);
       } else {
         for (int q = 0; q < n; ++q)
-          cp.copy(a.recv + q * a.slot_stride + s * part + lo, buf + q * part + lo, hi - lo);
+          cp.copy(a.recv + q * a.slot_stride + s * part + lo, buf + q * part + lo, hi - lo, 1);
       }
       cp.flush();
     }
@@ -951,7 +991,8 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   }
   // TMA copier: the movers plus one copier warp, with the staging buffers
   // in dynamic shared memory; SM copier: the configured split.
-  a.tma = p.nvls_tma && c->tma_ok ? 1 : 0;
+  a.strong = p.nvls_strong ? 1 : 0;
+  a.tma = p.nvls_tma && c->tma_ok && !a.strong ? 1 : 0;
   const int movers = op.nvls_movers ? int(op.nvls_movers) : p.nvls_movers;
   const int unroll = op.nvls_unroll ? int(op.nvls_unroll) : p.nvls_unroll;
   const int threads = a.tma ? std::min(movers, 608) + 32 : p.nvls_threads;

@@ -63,10 +63,10 @@ def test_push_reduce_broken_reads_stale(n):
                                                      (2, 4, 3, False), (3, 4, 3, False), (3, 4, 2, False)])
 def test_nvls_allreduce_holds(n, rounds, bufs, in_first):
     """The NVLS AllReduce's copier/mover progress words with three round
-    buffers (the kernel's), in the kernel's order (copy-in of round s before
-    copy-out of round s-2) and in the earlier order. The earlier order was
-    also safe with two buffers (A(s) reused a buffer only after every rank's
-    B(s-2), which the wait before C(s-2) already needed)."""
+    buffers (the kernel's), in the kernel's order (copy-out of round s-2
+    before copy-in of round s) and in the swapped order. The kernel's order
+    is also safe with two buffers (A(s) reuses a buffer only after every
+    rank's B(s-2), which the wait before C(s-2) already needs)."""
     r = m.check_nvls_allreduce(nranks=n, rounds=rounds, bufs=bufs, in_first=in_first)
     assert r.ok, (r.violation, r.trace)
 

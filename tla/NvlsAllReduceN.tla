@@ -4,8 +4,8 @@
 (* actions: CopyIn (when s < R, copy input round s into buffer s % B, then  *)
 (* publish s + 1) and CopyOut (when s >= 2, wait until every mover          *)
 (* published s - 1 and copy buffer (s-2) % B out: every slice must hold     *)
-(* round s-2 reduced). With InFirst (the kernel's order) CopyIn comes      *)
-(* first in the step, else CopyOut.                                         *)
+(* round s-2 reduced). The kernel's order is CopyOut first; with InFirst   *)
+(* CopyIn comes first (an order that holds here but failed on the GPU).     *)
 (* Mover of rank r, step s < R: waits until every copier published s + 1   *)
 (* (only its own when not MoverWaitsAll), reads slice r of buffer s % B on  *)
 (* every rank (the switch's ld_reduce: must hold round s input), then       *)
