@@ -18,7 +18,8 @@ ALGO = {"fallback": 0, "ar_twoshot": 1, "ar_nvls": 2, "rs_pull": 3, "ag_pull": 4
         "bc_pull": 5, "bc_scatter": 6, "ar_staged": 7, "rs_staged": 8, "bc_chain": 9,
         "bc_nvls": 10, "ag_nvls": 11, "rs_nvls": 12, "ag_push": 13, "bc_ring": 14,
         "rs_push": 15, "ar_push": 16, "ar_hybrid": 17, "ar_oneshot": 18,
-        "rs_hybrid": 19, "ar_twoshot_ll": 20}
+        "rs_hybrid": 19, "ar_twoshot_ll": 20,
+        "rs_ll": 21, "ag_ll": 22, "bc_ll": 23}
 REASONS = ["None", "NotGrouped", "UnsupportedType", "UnsupportedOp", "NullBuffer",
            "SizeOverflow", "BelowThreshold", "Misaligned", "BadSlot", "PartialOverlap",
            "BadRank", "GroupShape", "NotClique", "Mismatch", "Capturing", "FirstPass",

@@ -52,15 +52,16 @@ FORCE_NAMES = {
                   "staged": "ar_staged", "push": "ar_push", "hybrid": "ar_hybrid",
                   "twoshot_ll": "ar_twoshot_ll"},
     "reducescatter": {"pull": "rs_pull", "staged": "rs_staged", "nvls": "rs_nvls", "push": "rs_push",
-                      "hybrid": "rs_hybrid"},
-    "allgather": {"pull": "ag_pull", "nvls": "ag_nvls", "push": "ag_push"},
+                      "hybrid": "rs_hybrid", "ll": "rs_ll"},
+    "allgather": {"pull": "ag_pull", "nvls": "ag_nvls", "push": "ag_push", "ll": "ag_ll"},
     "broadcast": {"pull": "bc_pull", "scatter": "bc_scatter", "chain": "bc_chain", "nvls": "bc_nvls",
-                  "ring": "bc_ring"},
+                  "ring": "bc_ring", "ll": "bc_ll"},
 }
 SWITCH_ROUTES = {"ar_nvls", "bc_nvls", "ag_nvls", "rs_nvls", "ar_hybrid", "rs_hybrid"}
 ALGO_IDS = ["fallback", "ar_twoshot", "ar_nvls", "rs_pull", "ag_pull", "bc_pull", "bc_scatter",
             "ar_staged", "rs_staged", "bc_chain", "bc_nvls", "ag_nvls", "rs_nvls", "ag_push", "bc_ring",
-            "rs_push", "ar_push", "ar_hybrid", "ar_oneshot", "rs_hybrid", "ar_twoshot_ll"]
+            "rs_push", "ar_push", "ar_hybrid", "ar_oneshot", "rs_hybrid", "ar_twoshot_ll", "rs_ll",
+            "ag_ll", "bc_ll"]
 
 
 def parse_size(s: str | None) -> int | None:
@@ -149,15 +150,18 @@ def valid(route: str, kind: str, n: int, dtype: str, op: str, nvls: bool) -> boo
         "ar_twoshot": kind == "allreduce",
         "ar_oneshot": kind == "allreduce" and n >= 2 and dtype in SWITCH_TYPES,
         "ar_twoshot_ll": kind == "allreduce" and n >= 2 and dtype in SWITCH_TYPES,
+        "rs_ll": kind == "reducescatter" and n >= 2 and dtype in SWITCH_TYPES,
+        "ag_ll": kind == "allgather" and n >= 2,
+        "bc_ll": kind == "broadcast" and n >= 2,
         "ar_nvls": kind == "allreduce" and nvls and n >= 2 and dtype in SWITCH_TYPES and switch_op,
-        "ar_hybrid": kind == "allreduce" and nvls and n >= 2 and dtype in SWITCH_TYPES and switch_op,
+        "ar_hybrid": False,  # refused by the library (wrong data at 4 GiB, measured)
         "ar_staged": kind == "allreduce",
         "ar_push": kind == "allreduce" and n >= 2 and dtype in SWITCH_TYPES,
         "rs_pull": kind == "reducescatter",
         "rs_staged": kind == "reducescatter",
         "rs_push": kind == "reducescatter" and n >= 2 and dtype in SWITCH_TYPES,
         "rs_nvls": kind == "reducescatter" and nvls and n >= 2 and dtype in SWITCH_TYPES and switch_op,
-        "rs_hybrid": kind == "reducescatter" and nvls and n >= 2 and dtype in SWITCH_TYPES and switch_op,
+        "rs_hybrid": False,
         "ag_pull": kind == "allgather",
         "ag_push": kind == "allgather",
         "ag_nvls": kind == "allgather" and nvls and n >= 2,
@@ -245,6 +249,9 @@ def expected_route(kind: str, dtype: str, op: str, count: int, n: int, *, inplac
     # rank's payload must be 16-byte aligned.
     aligned = aligned and (count * ELEM[dtype]) % 16 == 0
     if route in SWITCH_ROUTES and (not aligned or (op == "premulsum" and not uniform_scalar)):
+        route = static_route(kind, n, dtype, op, False, rules)
+    # So do the low-latency AllGather and Broadcast copies.
+    if route in ("ag_ll", "bc_ll") and not aligned:
         route = static_route(kind, n, dtype, op, False, rules)
     if route == "ar_oneshot" and inplace and n > 1:
         route = "ar_twoshot_ll"

@@ -33,10 +33,11 @@ struct Candidate {
 
 // NVLS AllReduce kernel shapes tried (movers per block, requests in flight per
 // mover, round MiB, round schedule): the switch side bounds the kernel, so
-// more requests in flight, smaller rounds and ramped first and last rounds
-// (a shorter pipeline fill and drain) may pay.
-constexpr int kNvlsShapes[][4] = {{0, 0, 0, 0},   {608, 4, 0, 0},  {608, 8, 0, 0},  {512, 8, 128, 0},
-                                  {608, 8, 64, 0}, {0, 0, 0, 2},    {608, 8, 0, 2}};
+// more requests in flight and ramped first and last rounds (a shorter
+// pipeline fill and drain) may pay. No shape shrinks the round: the scratch
+// holds one buffer per round of the largest message, and smaller rounds
+// would reuse buffers within a call.
+constexpr int kNvlsShapes[][4] = {{0, 0, 0, 0}, {608, 4, 0, 0}, {608, 8, 0, 0}, {0, 0, 0, 2}, {608, 8, 0, 2}};
 
 // Every candidate route of a kind; a host-lane variant is added wherever the
 // rate model (measured PCIe, NVLink and fold rates) predicts a host share.
@@ -55,15 +56,18 @@ std::vector<Candidate> tiny_candidates(Kind k, int n, bool nvls) {
       if (nvls) add(Algo::ArNvls);
       break;
     case Kind::ReduceScatter:
+      add(Algo::RsLL);
       add(Algo::RsPull);
       if (nvls) add(Algo::RsNvls);
       break;
     case Kind::AllGather:
+      add(Algo::AgLL);
       add(Algo::AgPull);
       add(Algo::AgPush);
       if (nvls) add(Algo::AgNvls);
       break;
     case Kind::Broadcast:
+      add(Algo::BcLL);
       add(n >= 3 ? Algo::BcScatter : Algo::BcPull);
       add(Algo::BcRing);
       if (nvls) add(Algo::BcNvls);
@@ -102,6 +106,7 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
     case Kind::ReduceScatter:
       if (nvls && n >= 2) v.push_back({Algo::RsNvls, 0, 0, 0, 0});
       add(Algo::RsPull, 0);
+      v.push_back({Algo::RsLL, 0, 0, 0, 0});
       v.push_back({Algo::RsPush, 0, 0, 0, 0});
       if (small) {
         add(Algo::RsStaged, 0, 64, 3);
@@ -113,6 +118,7 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
       if (nvls && n >= 2) v.push_back({Algo::AgNvls, 0, 0, 0, 0});
       add(Algo::AgPull, 0);
       add(Algo::AgPush, 0);
+      v.push_back({Algo::AgLL, 0, 0, 0, 0});
       if (small) add(Algo::AgPull, 10000);
       break;
     case Kind::Broadcast:
@@ -123,6 +129,7 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
         add(Algo::BcPull, 10000);
       }
       v.push_back({Algo::BcRing, 0, 0, 0, 0});
+      v.push_back({Algo::BcLL, 0, 0, 0, 0});
       if (n >= 3) {
         add(Algo::BcChain, 10000, 64, 0);
         add(Algo::BcChain, 10000, 128, 0);

@@ -57,8 +57,14 @@ Reason gate_call(const CallDesc& c, const Policy& p) {
 bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_available) {
   switch (a) {
     case Algo::ArTwoShot: return k == Kind::AllReduce;
-    case Algo::ArNvls:
     case Algo::ArHybrid:
+    case Algo::RsHybrid:
+      // The hybrid routes (an NVLS gang on part of the SMs beside a P2P
+      // kernel) returned wrong data at 4 GiB on 2, 4 and 8 GPUs and were
+      // slower than NVLS alone where correct: refused, so forcing them takes
+      // the static choice.
+      return false;
+    case Algo::ArNvls:
       // A multicast object needs at least two devices.
       return k == Kind::AllReduce && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
@@ -66,6 +72,10 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
     case Algo::ArOneShot:
     case Algo::ArTwoShotLL:
       return k == Kind::AllReduce && nranks >= 2 && (t == DType::F32 || t == DType::F16 || t == DType::BF16);
+    case Algo::RsLL:
+      return k == Kind::ReduceScatter && nranks >= 2 && (t == DType::F32 || t == DType::F16 || t == DType::BF16);
+    case Algo::AgLL: return k == Kind::AllGather && nranks >= 2;
+    case Algo::BcLL: return k == Kind::Broadcast && nranks >= 2;
     case Algo::RsPull: return k == Kind::ReduceScatter;
     case Algo::AgPull: return k == Kind::AllGather;
     case Algo::BcPull: return k == Kind::Broadcast;
@@ -82,7 +92,6 @@ bool algo_valid(Algo a, Kind k, int nranks, DType t, RedOp op, bool nvls_availab
       return k == (a == Algo::RsPush ? Kind::ReduceScatter : Kind::AllReduce) && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16);
     case Algo::RsNvls:
-    case Algo::RsHybrid:
       return k == Kind::ReduceScatter && nvls_available && nranks >= 2 &&
              (t == DType::F32 || t == DType::F16 || t == DType::BF16) &&
              (op == RedOp::Sum || op == RedOp::Avg || op == RedOp::PreMulSum);
@@ -147,8 +156,10 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
   // The multimem kernels move whole 16-byte vectors only: every buffer and
   // every slot must be 16-byte aligned. They scale the switch's sum once, so
   // a PreMulSum takes them only when every rank passed the same host scalar.
+  // The low-latency AllGather/Broadcast copies also move whole vectors.
   const bool nvls = algo == Algo::ArNvls || algo == Algo::BcNvls || algo == Algo::AgNvls ||
                     algo == Algo::RsNvls || algo == Algo::ArHybrid || algo == Algo::RsHybrid;
+  const bool vec_copy = algo == Algo::AgLL || algo == Algo::BcLL;
   bool aligned = call_bytes(a) % 16 == 0;
   for (const CallDesc& c : calls)
     aligned = aligned && c.recv % 16 == 0 && (c.send % 16 == 0 || (c.kind == Kind::Broadcast && c.rank != c.root));
@@ -156,7 +167,7 @@ CliqueDecision gate_clique(const std::vector<CallDesc>& calls, const CliqueState
   if (a.op == RedOp::PreMulSum)
     for (const CallDesc& c : calls)
       uniform = uniform && c.scalar_residence == 1 && a.scalar_residence == 1 && c.scalar == a.scalar;
-  if (nvls && (!aligned || !uniform)) {
+  if ((nvls && (!aligned || !uniform)) || (vec_copy && !aligned)) {
     const Policy q = [&] {
       Policy x = p;
       x.nvls = NvlsMode::Off;

@@ -890,6 +890,19 @@ void plan_ar_twoshot_ll(Builder& b, const CliqueDesc& d) {
   b.plan().sm_bytes += d.bytes * size_t(2 * (n - 1));
 }
 
+// Low-latency ReduceScatter / AllGather / Broadcast on the one-shot engine:
+// one gang kernel per rank on its caller stream, no events. Rank r folds
+// slot r from every input into its output (ReduceScatter), stores its slot
+// into slot r of every rank's output (AllGather), or copies the root's
+// buffer into its output (Broadcast), between the in-kernel arrive and
+// depart barriers.
+void plan_gang_ll(Builder& b, const CliqueDesc& d) {
+  const int n = b.n();
+  for (int r = 0; r < n; ++r) b.nvls({Strm::Caller, uint8_t(r), 0}, r, d.bytes);
+  b.plan().needs.oneshot = true;
+  b.plan().sm_bytes += d.bytes * size_t(n - 1) * size_t(n);
+}
+
 // One rank: every collective except a scaled one (PreMulSum) is a copy of
 // the input into the output: the SM stream copy kernel on the caller stream,
 // beside an optional copy-engine share (the leading ce_ppm of the bytes, on
@@ -928,6 +941,7 @@ void build_plan(Algo algo, const CliqueDesc& d, const Policy& p, const Shares& s
   switch (algo) {
     case Algo::ArOneShot: plan_ar_oneshot(b, d); break;
     case Algo::ArTwoShotLL: plan_ar_twoshot_ll(b, d); break;
+    case Algo::RsLL: case Algo::AgLL: case Algo::BcLL: plan_gang_ll(b, d); break;
     case Algo::ArTwoShot: plan_ar_twoshot(b, d, s); break;
     case Algo::ArNvls: plan_ar_nvls(b, d, p, s); break;
     case Algo::RsPull: plan_rs_pull(b, d, s); break;

@@ -55,6 +55,9 @@ bool parse_algo(const char* s, Kind* kind, Algo* algo) {
   else if (a == "twoshot" && *kind == Kind::AllReduce) *algo = Algo::ArTwoShot;
   else if (a == "oneshot" && *kind == Kind::AllReduce) *algo = Algo::ArOneShot;
   else if (a == "twoshot_ll" && *kind == Kind::AllReduce) *algo = Algo::ArTwoShotLL;
+  else if (a == "ll" && *kind == Kind::ReduceScatter) *algo = Algo::RsLL;
+  else if (a == "ll" && *kind == Kind::AllGather) *algo = Algo::AgLL;
+  else if (a == "ll" && *kind == Kind::Broadcast) *algo = Algo::BcLL;
   else if (a == "nvls" && *kind == Kind::AllReduce) *algo = Algo::ArNvls;
   else if (a == "pull" && *kind == Kind::ReduceScatter) *algo = Algo::RsPull;
   else if (a == "pull" && *kind == Kind::AllGather) *algo = Algo::AgPull;
@@ -102,6 +105,7 @@ Policy policy_from_env(const EnvLookup& env) {
   }
   if (parse_int(env("NCCL_B200_NVLS_MIN_RANKS"), &i) && i >= 1) p.nvls_min_ranks = int(i);
   if (parse_size(env("NCCL_B200_NVLS_ROUND"), &z) && z >= kMiB) p.nvls_round_bytes = z;
+  if (parse_int(env("NCCL_B200_NVLS_BUFFERS"), &i) && i >= 3 && i <= 65536) p.nvls_buffers = int(i);
   if (parse_int(env("NCCL_B200_NVLS_MOVERS"), &i) && i >= 128 && i <= 736 && i % 32 == 0)
     p.nvls_movers = int(i);
   if (parse_int(env("NCCL_B200_NVLS_UNROLL"), &i) && (i == 4 || i == 8)) p.nvls_unroll = int(i);

@@ -30,7 +30,7 @@ const char* algo_name(Algo a) {
   static const char* names[] = {"fallback", "ar_twoshot", "ar_nvls", "rs_pull", "ag_pull",
                                 "bc_pull", "bc_scatter", "ar_staged", "rs_staged", "bc_chain",
                                 "bc_nvls", "ag_nvls", "rs_nvls", "ag_push", "bc_ring", "rs_push", "ar_push", "ar_hybrid",
-                                "ar_oneshot", "rs_hybrid", "ar_twoshot_ll"};
+                                "ar_oneshot", "rs_hybrid", "ar_twoshot_ll", "rs_ll", "ag_ll", "bc_ll"};
   static_assert(sizeof(names) / sizeof(*names) == size_t(Algo::Count), "algo names");
   return names[size_t(a) < size_t(Algo::Count) ? size_t(a) : 0];
 }

@@ -57,6 +57,9 @@ enum class Algo : uint8_t {
   ArOneShot,   // every rank folds the whole message from all inputs into its own output
   RsHybrid,    // NVLS ReduceScatter on part of the SMs for one share, P2P pulls for the rest
   ArTwoShotLL, // two-shot in one gang kernel per rank: in-kernel arrive/depart instead of events
+  RsLL,        // ReduceScatter fold of slot r in one gang kernel per rank (arrive/depart)
+  AgLL,        // AllGather: each rank stores its slot into every output (arrive/depart)
+  BcLL,        // Broadcast: each rank copies the root's buffer (arrive/depart)
   Count
 };
 

@@ -239,7 +239,14 @@ bool Executor::ensure(const Needs& needs, const int* devices, int n, std::string
   }
   if (needs.lanes > 0 && !ensure_lanes(devices[0], needs.lanes, needs.bounce_bytes, devices, n, why))
     return false;
-  if (needs.nvls_bytes > 0 && !nvls_ensure(devices, n, needs.nvls_bytes, why)) return false;
+  if (needs.nvls_bytes > 0) {
+    // Enough round buffers for the largest message (plus partial rounds), so
+    // that no call reuses one, unless the environment set a number.
+    const int nbuf = policy_.nvls_buffers > 0
+                         ? policy_.nvls_buffers
+                         : int(std::min<size_t>(policy_.max_message_bytes / needs.nvls_bytes + 2, 1 << 16));
+    if (!nvls_ensure(devices, n, needs.nvls_bytes, nbuf, why)) return false;
+  }
   if (needs.ring && !ring_ensure(devices, n, why)) return false;
   if (needs.pushred && !pushred_ensure(devices, n, why)) return false;
   if (needs.oneshot && !oneshot_ensure(devices, n, why)) return false;
@@ -365,7 +372,8 @@ cudaError_t Executor::submit(const PlanOp& op, const Plan& plan, const Binding& 
       launches_.fetch_add(1, std::memory_order_relaxed);
       if (plan.algo == Algo::BcRing) return ring_launch(op, plan, b, policy_, s);
       if (plan.algo == Algo::RsPush || plan.algo == Algo::ArPush) return pushred_launch(op, plan, b, policy_, s);
-      if (plan.algo == Algo::ArOneShot || plan.algo == Algo::ArTwoShotLL)
+      if (plan.algo == Algo::ArOneShot || plan.algo == Algo::ArTwoShotLL || plan.algo == Algo::RsLL ||
+          plan.algo == Algo::AgLL || plan.algo == Algo::BcLL)
         return oneshot_launch(op, plan, b, policy_, s);
       return nvls_launch(op, plan, b, policy_, s, dev);
     default:

@@ -4,7 +4,11 @@
 // Setup (once per device set): one multicast object spans every clique GPU;
 // each GPU binds its own physical scratch (cuMemCreate) into it and maps
 // both a unicast view (its own memory) and a multicast view. The scratch
-// holds three round buffers of R bytes plus progress words per block.
+// holds K round buffers of R bytes (K >= 3) plus progress words per block;
+// round s uses buffer s % K. By default K covers the largest message the
+// interposer takes (8 GiB), so no call reuses a buffer: reuse within a call
+// (K = 3) failed the round-reuse edge stress on the GPU although every wait
+// the protocol needs is in place.
 //
 // Kernels (one per GPU; those launched for one call form a gang): the
 // message is processed in rounds of R bytes. In a block, mover warps work
@@ -49,6 +53,7 @@ struct NvlsArgs {
   unsigned long long bytes;
   unsigned long long round;  // R
   unsigned long long buf_stride;
+  unsigned nbuf;             // K round buffers; round s uses buffer s % K
   unsigned long long timeout_ns;
   unsigned* status;          // mapped host word: nonzero = a wait expired
   unsigned base;             // progress epoch before this call
@@ -562,7 +567,7 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
       unsigned long long rbase, rlen, lo, hi;
       ar_round(s, a.bytes, a.round, a.ramp, &rbase, &rlen);
       portion(rlen, n, a.rank, &lo, &hi);
-      char* base = a.mc + (s % 3) * a.buf_stride + lo;
+      char* base = a.mc + (s % a.nbuf) * a.buf_stride + lo;
       strided<U>(
           unsigned(g.t), unsigned(g.nt), unsigned((hi - lo) / 16),
           [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
@@ -578,7 +583,7 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
         const unsigned i = s - 2;
         unsigned long long rbase, rlen;
         ar_round(i, a.bytes, a.round, a.ramp, &rbase, &rlen);
-        const char* buf = a.uc + (i % 3) * a.buf_stride;
+        const char* buf = a.uc + (i % a.nbuf) * a.buf_stride;
         for (int q = 0; q < n; ++q) {
           unsigned long long lo, hi;
           portion(rlen, n, q, &lo, &hi);
@@ -588,7 +593,7 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
       if (s < rounds) {
         unsigned long long rbase, rlen;
         ar_round(s, a.bytes, a.round, a.ramp, &rbase, &rlen);
-        char* buf = a.uc + (s % 3) * a.buf_stride;
+        char* buf = a.uc + (s % a.nbuf) * a.buf_stride;
         for (int q = 0; q < n; ++q) {
           unsigned long long lo, hi;
           portion(rlen, n, q, &lo, &hi);
@@ -612,15 +617,15 @@ __device__ __forceinline__ void flat_portion(unsigned long long len, unsigned lo
 }
 
 // Broadcast / AllGather / ReduceScatter through the switch, with the same
-// three-buffer scratch, decoupled groups and bounded waits:
+// K-buffer scratch, decoupled groups and bounded waits:
 //  ReduceScatter: copier A(s) copies every slot's part of round s in (after
-//    every rank's B(s-3), the last reader of buffer s%3); mover B(s), after
+//    every rank's B(s-K), the last reader of buffer s%K); mover B(s), after
 //    every rank's A(s), multimem.ld_reduces its own part into its output.
 //  AllGather: mover B(s) multicasts its slot's part of round s into every
-//    rank's buffer (after every rank's C(s-3)); copier C(s), after every
+//    rank's buffer (after every rank's C(s-K)); copier C(s), after every
 //    rank's B(s), copies all parts out.
 //  Broadcast: the root's movers multicast round s (after every rank's
-//    C(s-3)); copiers copy round s out after the root's B(s). The root
+//    C(s-K)); copiers copy round s out after the root's B(s). The root
 //    sends each byte once.
 template <int U, int DT, bool TMA>
 __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_xfer_kernel(const __grid_constant__ NvlsArgs a) {
@@ -648,24 +653,24 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_xfer_kernel(const __g
     if (rs) {
       if (g.mover) {
         if (!group_wait(a, g, kCopier, a.base + s + 1, -1)) return;
-        const char* base = a.mc + (s % 3) * a.buf_stride + a.rank * part + lo;
+        const char* base = a.mc + (s % a.nbuf) * a.buf_stride + a.rank * part + lo;
         uint4* out = reinterpret_cast<uint4*>(a.recv + s * part + lo);
         strided<U>(
             unsigned(g.t), unsigned(g.nt), unsigned((hi - lo) / 16),
             [&](unsigned v) { return ld_reduce(base + size_t(v) * 16, DT); },
             [&](unsigned v, uint4 x) { __stcs(out + v, a.scaled ? scale(x, DT, a.mul) : x); });
       } else {
-        if (s >= 3 && !group_wait(a, g, kMover, a.base + s - 2, -1)) break;
+        if (s >= a.nbuf && !group_wait(a, g, kMover, a.base + s - a.nbuf + 1, -1)) break;
         cp.acquired();
-        char* buf = a.uc + (s % 3) * a.buf_stride;
+        char* buf = a.uc + (s % a.nbuf) * a.buf_stride;
         for (int q = 0; q < n; ++q)
           cp.copy(buf + q * part + lo, a.send + q * a.slot_stride + s * part + lo, hi - lo, 2);
         cp.flush();
       }
     } else if (g.mover) {
       if (bc && a.rank != a.root) break;  // only the root's movers send
-      if (s >= 3 && !group_wait(a, g, kCopier, a.base + s - 2, -1)) return;
-      char* base = a.mc + (s % 3) * a.buf_stride + (bc ? 0 : a.rank * part) + lo;
+      if (s >= a.nbuf && !group_wait(a, g, kCopier, a.base + s - a.nbuf + 1, -1)) return;
+      char* base = a.mc + (s % a.nbuf) * a.buf_stride + (bc ? 0 : a.rank * part) + lo;
       const uint4* in = reinterpret_cast<const uint4*>(a.send + s * part + lo);
       strided<U>(
           unsigned(g.t), unsigned(g.nt), unsigned((hi - lo) / 16),
@@ -674,7 +679,7 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_xfer_kernel(const __g
     } else {
       if (!group_wait(a, g, kMover, a.base + s + 1, bc ? a.root : -1)) break;
       cp.acquired();
-      const char* buf = a.uc + (s % 3) * a.buf_stride;
+      const char* buf = a.uc + (s % a.nbuf) * a.buf_stride;
       if (bc) {
         cp.copy(a.recv + s * part + lo, buf + lo, hi - lo, 1);
       } else {
@@ -769,6 +774,7 @@ struct Context {
   std::vector<int> devices;
   size_t round = 0;       // R
   size_t stride = 0;      // distance between round buffers
+  unsigned nbuf = 3;      // round buffers
   size_t size = 0;        // bytes bound per GPU
   std::vector<char*> uc, mc;
   unsigned* status = nullptr;  // mapped pinned host word
@@ -820,7 +826,7 @@ bool nvls_supported(const int* devices, int n) {
   return ok;
 }
 
-bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why) {
+bool nvls_ensure(const int* devices, int n, size_t round_bytes, int nbuf, std::string* why) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (Context* c = find(devices, n)) {
     if (c->broken) {
@@ -849,7 +855,8 @@ bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why
   CUmulticastObjectProp mprop{};
   mprop.numDevices = unsigned(n);
   mprop.handleTypes = 0;
-  mprop.size = 3 * stride + flags_bytes;
+  const unsigned K = unsigned(std::max(3, nbuf));
+  mprop.size = size_t(K) * stride + flags_bytes;
   size_t mgran = 0;
   if (d.MulticastGetGranularity(&mgran, &mprop, CU_MULTICAST_GRANULARITY_RECOMMENDED) != CUDA_SUCCESS)
     return fail("multicast granularity");
@@ -880,6 +887,7 @@ bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why
   c->devices.assign(devices, devices + n);
   c->round = round;
   c->stride = stride;
+  c->nbuf = K;
   c->size = size;
   c->blocks = blocks;
   for (int i = 0; i < n; ++i) {
@@ -901,7 +909,7 @@ bool nvls_ensure(const int* devices, int n, size_t round_bytes, std::string* why
       return fail("multicast mapping");
     c->uc.push_back(reinterpret_cast<char*>(uc));
     c->mc.push_back(reinterpret_cast<char*>(mv));
-    if (cudaMemset(reinterpret_cast<char*>(uc) + 3 * stride, 0, flags_bytes) != cudaSuccess)
+    if (cudaMemset(reinterpret_cast<char*>(uc) + size_t(K) * stride, 0, flags_bytes) != cudaSuccess)
       return fail("flag init");
     unsigned long long* tr = nullptr;
     const size_t tr_bytes = size_t(blocks) * 8 * sizeof(unsigned long long);
@@ -954,8 +962,9 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.recv = static_cast<char*>(b.recv[r]) + off;
   a.uc = c->uc[size_t(r)];
   a.mc = c->mc[size_t(r)];
-  a.uc_flags = reinterpret_cast<unsigned*>(a.uc + 3 * c->stride);
-  a.mc_flags = reinterpret_cast<unsigned*>(a.mc + 3 * c->stride);
+  a.uc_flags = reinterpret_cast<unsigned*>(a.uc + size_t(c->nbuf) * c->stride);
+  a.mc_flags = reinterpret_cast<unsigned*>(a.mc + size_t(c->nbuf) * c->stride);
+  a.nbuf = c->nbuf;
   a.bytes = ar ? range : plan.desc.bytes;
   // A smaller round than the scratch holds (a tuned kernel shape) uses the
   // same buffers; 32-byte multiples of every slice stay aligned.

@@ -23,8 +23,9 @@ namespace nb {
 // True when every device supports multicast objects and the driver entry
 // points exist. Cheap after the first call per device set.
 bool nvls_supported(const int* devices, int n);
-// Create (or grow) the multicast scratch for this device set.
-bool nvls_ensure(const int* devices, int n, size_t bytes, std::string* why);
+// Create the multicast scratch for this device set: `nbuf` round buffers
+// (at least 3) of `round_bytes` each, fixed at creation.
+bool nvls_ensure(const int* devices, int n, size_t round_bytes, int nbuf, std::string* why);
 cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, const Policy& p,
                         cudaStream_t s, int dev);
 // Device-side status of the last NVLS gang on this device set: 0 ok,

@@ -243,6 +243,11 @@ OsFn pick(DType t, int n, bool wide) {
   }
 }
 
+// Copies (AllGather, Broadcast): one source, moved as 32-bit words by a
+// one-source Sum, which performs no arithmetic (bit patterns, NaNs included,
+// pass unchanged); payloads are whole 16-byte vectors (the gate's rule).
+OsFn pick_copy(bool wide) { return wide ? oneshot_kernel<float, 1, 32> : oneshot_kernel<float, 1, 16>; }
+
 constexpr int kThreads = 512;
 
 struct OsContext {
@@ -351,32 +356,64 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
       if (e != cudaSuccess) return e;
     }
   }
-  const size_t es = elem_size(plan.desc.dtype);
-  // One-shot: the whole message into this rank's output. Two-shot: this
-  // rank's slice (the plan op's range) into every rank's output.
-  const bool two = plan.algo == Algo::ArTwoShotLL;
-  const size_t off = two ? op.src[0].off : 0;
-  const size_t bytes = two ? op.bytes : plan.desc.bytes;
-  uintptr_t any = reinterpret_cast<uintptr_t>(b.recv[r]) | off;
-  for (int q = 0; q < n; ++q) {
-    any |= reinterpret_cast<uintptr_t>(b.send[q]);
-    if (two) any |= reinterpret_cast<uintptr_t>(b.recv[q]);
+  // Per route: this rank's sources (nsrc of them, rank order), its
+  // destinations, and the bytes each moves.
+  //   one-shot AllReduce: every input -> own output, the whole message;
+  //   two-shot AllReduce: slice r of every input -> slice r of every output;
+  //   ReduceScatter:      slot r of every input -> own output;
+  //   AllGather:          own input -> slot r of every output (a copy);
+  //   Broadcast:          the root's input -> own output (a copy).
+  const Algo al = plan.algo;
+  const bool copy = al == Algo::AgLL || al == Algo::BcLL;
+  const size_t es = copy ? sizeof(float) : elem_size(plan.desc.dtype);
+  const size_t msg = plan.desc.bytes;  // AllReduce/Broadcast message, AllGather/ReduceScatter slot
+  const char* src[kMaxRanks] = {};
+  char* dst[kMaxRanks] = {};
+  int nsrc = n, ndst = 1;
+  size_t bytes = msg, span = msg;
+  if (al == Algo::ArTwoShotLL) {
+    const size_t off = op.src[0].off;
+    bytes = op.bytes;
+    span = msg / size_t(n);
+    for (int q = 0; q < n; ++q) {
+      src[q] = static_cast<const char*>(b.send[q]) + off;
+      dst[q] = static_cast<char*>(b.recv[q]) + off;
+    }
+    ndst = n;
+  } else if (al == Algo::RsLL) {
+    for (int q = 0; q < n; ++q) src[q] = static_cast<const char*>(b.send[q]) + size_t(r) * msg;
+    dst[0] = static_cast<char*>(b.recv[r]);
+  } else if (al == Algo::AgLL) {
+    nsrc = 1;
+    src[0] = static_cast<const char*>(b.send[r]);
+    for (int q = 0; q < n; ++q) dst[q] = static_cast<char*>(b.recv[q]) + size_t(r) * msg;
+    ndst = n;
+  } else if (al == Algo::BcLL) {
+    nsrc = 1;
+    src[0] = static_cast<const char*>(b.send[plan.desc.root]);
+    dst[0] = static_cast<char*>(b.recv[r]);
+  } else {
+    for (int q = 0; q < n; ++q) src[q] = static_cast<const char*>(b.send[q]);
+    dst[0] = static_cast<char*>(b.recv[r]);
   }
+  uintptr_t any = 0;
+  for (int q = 0; q < nsrc; ++q) any |= reinterpret_cast<uintptr_t>(src[q]);
+  for (int q = 0; q < ndst; ++q) any |= reinterpret_cast<uintptr_t>(dst[q]);
   if (!es || bytes % es || any % 16) return cudaErrorInvalidValue;
   const bool wide = any % 32 == 0;
   const int vb = wide ? 32 : 16;
-  const OsFn fn = pick(plan.desc.dtype, n, wide);
+  const OsFn fn = copy ? pick_copy(wide) : pick(plan.desc.dtype, n, wide);
   if (!fn) return cudaErrorInvalidValue;
   OsArgs a{};
   for (int q = 0; q < n; ++q) {
-    a.src[q] = static_cast<const char*>(b.send[q]) + off;
-    a.dev_scalar[q] = b.dev_scalar[q];
-    a.scale[q] = b.fold.scalars[q];
+    a.src[q] = src[q];
+    a.dev_scalar[q] = copy ? nullptr : b.dev_scalar[q];
+    a.scale[q] = copy ? 1.0 : b.fold.scalars[q];
     a.arrive_peer[q] = c->arrive[size_t(q)];
     a.depart_peer[q] = c->depart[size_t(q)];
   }
-  a.ndst = two ? n : 1;
-  for (int q = 0; q < a.ndst; ++q) a.dst[q] = static_cast<char*>(b.recv[two ? q : r]) + off;
+  a.ndst = ndst;
+  for (int q = 0; q < ndst; ++q) a.dst[q] = dst[q];
   a.arrive_mine = c->arrive[size_t(r)];
   a.depart_mine = c->depart[size_t(r)];
   a.nvec = bytes / size_t(vb);
@@ -385,7 +422,7 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
   a.status = c->status_dev;
   a.epoch = c->epoch;
   a.skew = p.test_nvls_skew;
-  a.op = int(b.fold.op);
+  a.op = copy ? int(RedOp::Sum) : int(b.fold.op);  // a one-source Sum moves words unchanged
   a.nranks = n;
   a.rank = r;
   // One block per 8 KiB of this rank's range, at least 8 and at most one
@@ -393,7 +430,6 @@ cudaError_t oneshot_launch(const PlanOp& op, const Plan& plan, const Binding& b,
   // share of the link rate, so even a 1 MiB range is spread over 128 SMs.
   // Every rank uses the same grid (block b pairs with block b everywhere),
   // so the two-shot grid follows the common slice length, not this rank's.
-  const size_t span = two ? plan.desc.bytes / size_t(n) : plan.desc.bytes;
   const unsigned blocks =
       unsigned(std::min<size_t>(std::max<size_t>(8, (span + 8191) / 8192), size_t(c->blocks)));
   cudaError_t e = cudaSuccess;

@@ -20,7 +20,8 @@ CASES = [("ar_twoshot", "allreduce"), ("rs_pull", "reducescatter"), ("ag_pull", 
          ("bc_nvls", "broadcast"), ("ag_nvls", "allgather"), ("rs_nvls", "reducescatter"),
          ("ag_push", "allgather"), ("bc_ring", "broadcast"), ("rs_push", "reducescatter"),
          ("ar_push", "allreduce"), ("ar_hybrid", "allreduce"), ("ar_oneshot", "allreduce"),
-         ("rs_hybrid", "reducescatter"), ("ar_twoshot_ll", "allreduce")]
+         ("rs_hybrid", "reducescatter"), ("ar_twoshot_ll", "allreduce"),
+         ("rs_ll", "reducescatter"), ("ag_ll", "allgather"), ("bc_ll", "broadcast")]
 
 
 def test_baseline_cpu_plumbing_config():

@@ -178,10 +178,10 @@ print("RESULT", nc.custom_calls(ALGO["ar_hybrid"]))
 """
 
 
-@pytest.mark.parametrize("n", [2, 4, 8])
-def test_nvls_hybrid_allreduce(n):
-    """The hybrid AllReduce: a leading share through the switch on part of the
-    SMs while the two-shot P2P kernel reduces the rest on the other SMs."""
+@pytest.mark.parametrize("n", [2, 4])
+def test_forced_hybrid_takes_the_static_route(n):
+    """The hybrid routes are refused (wrong data at 4 GiB, measured): forcing
+    ar=hybrid runs the static route and the result is exact."""
     need_gpus(n)
     env = dict(os.environ, NCCL_B200_NVLS="on", NCCL_B200_ALGO="ar=hybrid", NCCL_B200_TUNE="0",
                NCCL_B200_FIRST_PASS="0")
@@ -189,4 +189,4 @@ def test_nvls_hybrid_allreduce(n):
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
-    assert int(line[1]) >= 8, line
+    assert int(line[1]) == 0, line

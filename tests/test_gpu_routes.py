@@ -186,11 +186,12 @@ arr = (C.c_int * n)(*devs)
 st = nc.shim.nb_ring_status(arr, n) | nc.shim.nb_pushred_status(arr, n) | nc.shim.nb_oneshot_status(arr, n)
 print("RESULT", bad, st, nc.shim.nb_poisoned(), nc.custom_calls(ALGO["bc_ring"]),
       nc.custom_calls(ALGO["ar_push"]), nc.custom_calls(ALGO["rs_push"]),
-      nc.custom_calls(ALGO["ar_oneshot"]) + nc.custom_calls(ALGO["ar_twoshot_ll"]))
+      nc.custom_calls(ALGO["ar_oneshot"]) + nc.custom_calls(ALGO["ar_twoshot_ll"]),
+      nc.custom_calls(ALGO["rs_ll"]) + nc.custom_calls(ALGO["bc_ll"]))
 """
 
 
-@pytest.mark.parametrize("algo", ["bc=ring,ar=push,rs=push", "ar=oneshot", "ar=twoshot_ll"])
+@pytest.mark.parametrize("algo", ["bc=ring,ar=push,rs=push", "ar=oneshot", "bc=ll,ar=twoshot_ll,rs=ll"])
 @pytest.mark.parametrize("n", [2, 3])
 def test_gang_calls_ordered_across_streams_and_cliques(n, algo):
     """The push chain and the push-reduce engine keep scratch, progress words
@@ -206,9 +207,11 @@ def test_gang_calls_ordered_across_streams_and_cliques(n, algo):
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("RESULT")][-1].split()
-    bad, status, poisoned, ring, arp, rsp, one = map(int, line[1:])
+    bad, status, poisoned, ring, arp, rsp, one, ll = map(int, line[1:])
     assert (bad, status, poisoned) == (0, 0, 0), line
-    if "shot" in algo:
+    if "ll" in algo:
+        assert one >= 4 and ll >= 8, line
+    elif "shot" in algo:
         assert one >= 4, line
     else:
         assert ring >= 4 and arp >= 4 and rsp >= 4, line

@@ -89,14 +89,14 @@ def test_stress_ordering_controls(n):
 
 
 GANGS = ["ar=push,rs=push,ag=push,bc=ring", "ar=nvls,rs=nvls,ag=nvls,bc=nvls",
-         "ar=hybrid,rs=hybrid,ag=pull,bc=scatter", "ar=oneshot,rs=pull,ag=pull,bc=pull",
-         "ar=twoshot_ll,rs=pull,ag=pull,bc=pull"]
+         "ar=oneshot,rs=pull,ag=pull,bc=scatter",
+         "ar=twoshot_ll,rs=ll,ag=ll,bc=ll"]
 
 
 @pytest.mark.parametrize("algo", GANGS)
 @pytest.mark.parametrize("n", [2, 4, 8])
 def test_stress_gang_routes(algo, n):
-    """The in-kernel-synchronized and hybrid routes under the back-to-back
+    """The in-kernel-synchronized routes under the back-to-back
     harness, with the ordering controls on."""
     need_gpus(n)
     rc, rows, log = run(["--gpus", str(n), "--iters", "3", "--scale", "4", "--no-boundary",
