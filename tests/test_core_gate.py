@@ -202,6 +202,10 @@ def test_policy_parsing_of_engine_knobs():
     assert c.policy_value({}, "nvls_tma") == 1
     assert c.policy_value({"NCCL_B200_NVLS_TMA": "0"}, "nvls_tma") == 0
     assert c.policy_value({}, "nvls_ramp") == 0
+    assert c.policy_value({}, "nvls_strong") == 1
+    assert c.policy_value({}, "nvls_buffers") == 0  # 0: one per round of the largest message
+    assert c.policy_value({"NCCL_B200_NVLS_BUFFERS": "8"}, "nvls_buffers") == 8
+    assert c.policy_value({"NCCL_B200_NVLS_BUFFERS": "2"}, "nvls_buffers") == 0  # at least 3
     assert c.policy_value({"NCCL_B200_NVLS_RAMP": "1"}, "nvls_ramp") == 1
     assert c.policy_value({"NCCL_B200_NVLS_TRACE": "1", "NCCL_B200_NVTX": "on"}, "nvls_trace") == 1
     assert c.policy_value({"NCCL_B200_NVTX": "on"}, "nvtx") == 1
