@@ -33,11 +33,11 @@ struct Candidate {
 
 // NVLS AllReduce kernel shapes tried (movers per block, requests in flight per
 // mover, round MiB, round schedule): the switch side bounds the kernel, so
-// more requests in flight and ramped first and last rounds (a shorter
-// pipeline fill and drain) may pay. No shape shrinks the round: the scratch
+// more requests in flight may pay. No shape shrinks the round: the scratch
 // holds one buffer per round of the largest message, and smaller rounds
-// would reuse buffers within a call.
-constexpr int kNvlsShapes[][4] = {{0, 0, 0, 0}, {608, 4, 0, 0}, {608, 8, 0, 0}, {0, 0, 0, 2}, {608, 8, 0, 2}};
+// would reuse buffers within a call. The ramped schedule (NCCL_B200_NVLS_RAMP)
+// measured no gain on 2 GPUs and is not a candidate.
+constexpr int kNvlsShapes[][4] = {{0, 0, 0, 0}, {608, 4, 0, 0}, {608, 8, 0, 0}};
 
 // Every candidate route of a kind; a host-lane variant is added wherever the
 // rate model (measured PCIe, NVLink and fold rates) predicts a host share.

@@ -37,8 +37,9 @@ struct Policy {
   bool nvls_trace = false;          // per-block phase timing in the NVLS kernels
   bool nvls_tma = true;             // NVLS copier: TMA bulk pipeline (else SM copy warps)
   bool nvls_ramp = false;           // NVLS AllReduce: ramped first/last rounds from 4 rounds on
-  // NVLS round buffers per GPU; by default enough for the largest message
-  // (max_bytes / nvls_round_bytes, at least 3), so no call reuses one.
+  // NVLS round buffers per GPU (at least 3); 0: enough for the largest
+  // message (max_bytes / nvls_round_bytes + 2, + 10 with the ramp), so no
+  // call reuses one.
   int nvls_buffers = 0;
   bool nvls_strong = true;          // NVLS copier: SM copies with system-scope accesses to the scratch
   bool local_copy_tma = false;      // a large copy within one GPU: TMA bulk copy (else SM stream copy)

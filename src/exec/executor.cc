@@ -240,11 +240,13 @@ bool Executor::ensure(const Needs& needs, const int* devices, int n, std::string
   if (needs.lanes > 0 && !ensure_lanes(devices[0], needs.lanes, needs.bounce_bytes, devices, n, why))
     return false;
   if (needs.nvls_bytes > 0) {
-    // Enough round buffers for the largest message (plus partial rounds), so
-    // that no call reuses one, unless the environment set a number.
+    // Enough round buffers for the largest message (plus partial rounds, and
+    // the ramped schedule's eight short rounds when it is on), so that no
+    // call reuses one, unless the environment set a number.
+    const size_t extra = policy_.nvls_ramp ? 10 : 2;
     const int nbuf = policy_.nvls_buffers > 0
                          ? policy_.nvls_buffers
-                         : int(std::min<size_t>(policy_.max_message_bytes / needs.nvls_bytes + 2, 1 << 16));
+                         : int(std::min<size_t>(policy_.max_message_bytes / needs.nvls_bytes + extra, 1 << 16));
     if (!nvls_ensure(devices, n, needs.nvls_bytes, nbuf, why)) return false;
   }
   if (needs.ring && !ring_ensure(devices, n, why)) return false;
