@@ -426,6 +426,52 @@ def check_broadcast_chain(nranks=4, steps=3, skip_wait=False, only=None) -> Resu
 
 
 # --------------------------------------------------------------------------
+# OneShotBarrierN (arrive/depart barriers of the low-latency engine)
+# --------------------------------------------------------------------------
+
+def check_oneshot_barrier(nranks=3, calls=3, two=True, skip_arrive=False, skip_depart=False,
+                          only=None) -> Result:
+    """State: c[r] (call), ph[r] (0 produce, 1 data, 2 depart, 3 leave),
+    arr[r], dep[r] (published epochs), inp[r] (call whose input rank r's
+    buffer holds), out[r][s] (call whose result slice s of rank r's output
+    holds), bad."""
+    N, C = nranks, calls
+    init = (tuple([0] * N), tuple([0] * N), tuple([0] * N), tuple([0] * N), tuple([-1] * N),
+            tuple(tuple([-1] * N) for _ in range(N)), False)
+
+    def setv(t, i, v):
+        return t[:i] + (v,) + t[i + 1:]
+
+    def actions(st):
+        c, ph, arr, dep, inp, out, bad = st
+        for r in range(N):
+            if c[r] >= C:
+                continue
+            k = c[r]
+            if ph[r] == 0:
+                wrong = k > 0 and any(x != k - 1 for x in out[r])
+                yield (c, setv(ph, r, 1), setv(arr, r, k + 1), dep, setv(inp, r, k), out, bad or wrong)
+            elif ph[r] == 1:
+                if skip_arrive or all(a >= k + 1 for a in arr):
+                    wrong = any(x != k for x in inp)
+                    if two:
+                        nout = tuple(setv(out[q], r, k) for q in range(N))
+                    else:
+                        nout = setv(out, r, tuple([k] * N))
+                    yield (c, setv(ph, r, 2), arr, dep, inp, nout, bad or wrong)
+            elif ph[r] == 2:
+                yield (c, setv(ph, r, 3), arr, setv(dep, r, k + 1), inp, out, bad)
+            else:
+                if skip_depart or all(d >= k + 1 for d in dep):
+                    yield (setv(c, r, k + 1), setv(ph, r, 0), arr, dep, inp, out, bad)
+
+    def done(st):
+        return all(x >= C for x in st[0])
+
+    return _bfs(init, actions, [("CallsInStep", lambda st: not st[6])], done=done, only=only)
+
+
+# --------------------------------------------------------------------------
 # The committed TLC configurations drive the checkers
 # --------------------------------------------------------------------------
 
@@ -440,6 +486,8 @@ SPECS = {
     "NvlsAllReduceN": (check_nvls_allreduce, {"N": "nranks", "R": "rounds", "B": "bufs",
                                               "MoverWaitsAll": "mover_waits_all", "InFirst": "in_first"}),
     "BroadcastChainN": (check_broadcast_chain, {"N": "nranks", "S": "steps", "SkipWait": "skip_wait"}),
+    "OneShotBarrierN": (check_oneshot_barrier, {"N": "nranks", "C": "calls", "Two": "two",
+                                                "SkipArrive": "skip_arrive", "SkipDepart": "skip_depart"}),
 }
 
 

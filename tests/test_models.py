@@ -98,12 +98,30 @@ def test_broadcast_chain_broken_forwards_early():
     assert not r.ok and r.violation == "ForwardedArrived"
 
 
+@pytest.mark.parametrize("n,calls,two", [(2, 3, False), (2, 3, True), (3, 3, True), (3, 2, False)])
+def test_oneshot_barrier_holds(n, calls, two):
+    """The low-latency engine's arrive/depart barriers: every rank reads
+    every input of the current call, and every output slice a rank consumes
+    holds the previous call, across consecutive calls, one-shot and
+    two-shot alike; no deadlock."""
+    r = m.check_oneshot_barrier(nranks=n, calls=calls, two=two)
+    assert r.ok, (r.violation, r.trace)
+
+
+@pytest.mark.parametrize("two", [False, True])
+def test_oneshot_barrier_broken_without_either_wait(two):
+    for kw in ({"skip_arrive": True}, {"skip_depart": True}):
+        r = m.check_oneshot_barrier(nranks=2, calls=2, two=two, **kw)
+        assert not r.ok and r.violation == "CallsInStep", (kw, two)
+
+
 def test_tla_sources_present():
     for f in ["GroupFallbackN.tla", "HostLaneReuseN.tla", "GroupFallbackN.cfg",
               "GroupFallbackN-broken.cfg", "HostLaneReuseN.cfg", "HostLaneReuseN-broken.cfg",
               "PushReduceN.tla", "PushReduceN.cfg", "PushReduceN-broken.cfg",
               "NvlsAllReduceN.tla", "NvlsAllReduceN.cfg", "NvlsAllReduceN-broken.cfg",
-              "BroadcastChainN.tla", "BroadcastChainN.cfg", "BroadcastChainN-broken.cfg"]:
+              "BroadcastChainN.tla", "BroadcastChainN.cfg", "BroadcastChainN-broken.cfg",
+              "OneShotBarrierN.tla", "OneShotBarrierN.cfg", "OneShotBarrierN-broken.cfg"]:
         assert os.path.exists(os.path.join(REPO, "tla", f)), f
 
 
