@@ -1,5 +1,9 @@
-// Low-latency one-shot and two-shot AllReduce over peer memory, synchronized
-// inside the kernel instead of by cross-device events.
+// Low-latency collectives over peer memory, synchronized inside the kernel
+// instead of by cross-device events: one-shot and two-shot AllReduce,
+// ReduceScatter (slot r of every input folded into rank r's output),
+// AllGather (rank r's input stored into slot r of every output) and
+// Broadcast (every rank copies the root's input); the last two are
+// one-source copies that move 32-bit words unchanged.
 //
 // One kernel per rank, launched on the caller's own stream with nothing
 // around it. Block b of every rank's kernel:
@@ -9,12 +13,12 @@
 //   2. waits until every peer's block b arrived here (relaxed polls of this
 //      GPU's own table, then one acquire fence);
 //   3. folds its share of its range (grid-stride 16/32-byte vectors) from
-//      all N inputs in rank order -- its own from HBM, the peers' over
+//      its sources in rank order -- its own from HBM, the peers' over
 //      NVLink -- with fp32 accumulation. One-shot: the range is the whole
 //      message and the result goes to this rank's output only. Two-shot:
 //      the range is slice r and the result goes to slice r of every rank's
 //      output (P2P stores), so each GPU moves 2(N-1)/N of the message
-//      instead of N-1 times it;
+//      instead of N-1 times it. The other kinds: see the launch;
 //   4. departs: stores the epoch into the peers' depart tables, and waits
 //      until every peer's block b departed, i.e. finished reading this
 //      rank's input and (two-shot) writing this rank's output; only then may

@@ -25,9 +25,11 @@ EDGES = {"NCCL_B200_NVLS_ROUND": "4M", "NCCL_B200_RING_CHUNK": "32K", "NCCL_B200
 
 
 def run(args, env=None, timeout=900):
+    full = dict(os.environ)
+    full.update(SMALL)
+    full.update(env or {})  # a test's own settings win over the small thresholds
     r = subprocess.run([sys.executable, "-m", "scc26_nccl_shim_b200.parallel.stress", *args],
-                       cwd=REPO, env=dict(os.environ, **SMALL, **(env or {})), capture_output=True, text=True,
-                       timeout=timeout)
+                       cwd=REPO, env=full, capture_output=True, text=True, timeout=timeout)
     rows = [l.split("\t") for l in r.stdout.splitlines() if "\t" in l and not l.startswith("case\t")]
     return r.returncode, rows, r.stdout + r.stderr[-3000:]
 
