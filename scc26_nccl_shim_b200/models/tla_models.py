@@ -314,7 +314,8 @@ def check_push_reduce(nranks=3, rounds=4, depth=2, skip_consumed_wait=False, onl
 # NvlsAllReduce (progress words of the NVLS AllReduce kernel)
 # --------------------------------------------------------------------------
 
-def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, in_first=False, only=None) -> Result:
+def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, in_first=False, ahead=False,
+                         only=None) -> Result:
     """State: cs[r], cph[r] (copier step and phase), ms[r], mph[r] (mover
     step, 0 wait, 1 read, 2 write+publish), cflag[r], mflag[r],
     buf[r][b][q] = (round, 0 input | 1 reduced) or None, bad.
@@ -323,7 +324,10 @@ def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, in_fi
     and copies round s-2 out (C(s-2)); phase 1 copies round s in (A(s)) and
     publishes s+1. With `in_first` the phases swap (copy-in of round s, then
     copy-out of round s-2): an order that holds in this model but failed the
-    pipeline-edge stress on the GPU, so the kernel does not use it."""
+    pipeline-edge stress on the GPU, so the kernel does not use it. With
+    `ahead` (the kernel's NCCL_B200_NVLS_AHEAD, for a buffer per round) the
+    copier copies every round in first (steps 0..R-1), then copies round
+    s - R out at step s >= R after every rank's B(s - R)."""
     N, R, B = nranks, rounds, bufs
     empty = tuple(tuple(tuple(None for _ in range(N)) for _ in range(B)) for _ in range(N))
     init = (tuple([0] * N), tuple([0] * N), tuple([0] * N), tuple([0] * N),
@@ -353,11 +357,28 @@ def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, in_fi
         nb = setbuf(buf, {r}, s_ % B, set(range(N)), (s_, 0)) if s_ < R else buf
         return (nxt_cs, nxt_cph, ms, mph, setv(cflag, r, s_ + 1), mflag, nb, bad)
 
+    def ahead_step(st, r):
+        cs, cph, ms, mph, cflag, mflag, buf, bad = st
+        s_ = cs[r]
+        if s_ < R:  # copy round s in, publish s+1
+            nb = setbuf(buf, {r}, s_ % B, set(range(N)), (s_, 0))
+            return (setv(cs, r, s_ + 1), cph, ms, mph, setv(cflag, r, s_ + 1), mflag, nb, bad)
+        i = s_ - R  # copy round i out after every rank's B(i)
+        if not all(mflag[q] >= i + 1 for q in range(N)):
+            return None
+        wrong = any(buf[r][i % B][q] != (i, 1) for q in range(N))
+        return (setv(cs, r, s_ + 1), cph, ms, mph, cflag, mflag, buf, bad or wrong)
+
     def actions(st):
         cs, cph, ms, mph, cflag, mflag, buf, bad = st
         for r in range(N):
             s_ = cs[r]
-            if s_ < R + 2:
+            if ahead:
+                if s_ < 2 * R:
+                    nxt = ahead_step(st, r)
+                    if nxt is not None:
+                        yield nxt
+            elif s_ < R + 2:
                 first, second = (copy_in, copy_out) if in_first else (copy_out, copy_in)
                 if cph[r] == 0:
                     nxt = first(st, r, s_, cs, setv(cph, r, 1))
@@ -381,7 +402,7 @@ def check_nvls_allreduce(nranks=2, rounds=4, bufs=3, mover_waits_all=True, in_fi
                            nb, bad)
 
     def done(st):
-        return all(x >= R + 2 for x in st[0]) and all(x >= R for x in st[2])
+        return all(x >= (2 * R if ahead else R + 2) for x in st[0]) and all(x >= R for x in st[2])
 
     return _bfs(init, actions, [("RoundsInOrder", lambda st: not st[7])], done=done, only=only)
 

@@ -380,6 +380,7 @@ double nb_policy_value(const char* env, const char* field) {
   if (f == "nvls_ramp") return p.nvls_ramp;
   if (f == "nvls_strong") return p.nvls_strong;
   if (f == "nvls_buffers") return p.nvls_buffers;
+  if (f == "nvls_ahead") return p.nvls_ahead;
   if (f == "nvls_trace") return p.nvls_trace;
   if (f == "nvtx") return p.nvtx;
   if (f == "nvls_movers") return p.nvls_movers;

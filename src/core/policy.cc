@@ -113,6 +113,7 @@ Policy policy_from_env(const EnvLookup& env) {
   if (parse_bool(env("NCCL_B200_NVLS_TMA"), &b)) p.nvls_tma = b;
   if (parse_bool(env("NCCL_B200_NVLS_RAMP"), &b)) p.nvls_ramp = b;
   if (parse_bool(env("NCCL_B200_NVLS_STRONG"), &b)) p.nvls_strong = b;
+  if (parse_bool(env("NCCL_B200_NVLS_AHEAD"), &b)) p.nvls_ahead = b;
   if (const char* v = env("NCCL_B200_LOCAL_COPY")) {
     if (std::strcmp(v, "tma") == 0) p.local_copy_tma = true;
     else if (std::strcmp(v, "sm") == 0) p.local_copy_tma = false;

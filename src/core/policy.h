@@ -41,7 +41,8 @@ struct Policy {
   // message (max_bytes / nvls_round_bytes + 2, + 10 with the ramp), so no
   // call reuses one.
   int nvls_buffers = 0;
-  bool nvls_strong = true;          // NVLS copier: SM copies with system-scope accesses to the scratch
+  bool nvls_strong = true;
+  bool nvls_ahead = false;          // NVLS AllReduce: every copy-in before the copy-outs (needs a buffer per round)          // NVLS copier: SM copies with system-scope accesses to the scratch
   bool local_copy_tma = false;      // a large copy within one GPU: TMA bulk copy (else SM stream copy)
   size_t ring_chunk = 256 * 1024;   // Broadcast chain: bytes per block per step
   int hybrid_nvls_ppm = 6000;       // hybrid AllReduce: NVLS share of the message (per 10000)

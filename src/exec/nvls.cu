@@ -54,6 +54,7 @@ struct NvlsArgs {
   unsigned long long round;  // R
   unsigned long long buf_stride;
   unsigned nbuf;             // K round buffers; round s uses buffer s % K
+  int ahead;                 // AllReduce copier: every copy-in first (only when rounds <= K)
   unsigned long long timeout_ns;
   unsigned* status;          // mapped host word: nonzero = a wait expired
   unsigned base;             // progress epoch before this call
@@ -576,7 +577,35 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
     }
   } else {
     Copier<TMA> cp(a, g, dsmem, tma_bar, tma_dst, tma_size);
-    for (unsigned s = 0; s < rounds + 2; ++s) {
+    // With a buffer per round, copy every round in first (the movers never
+    // wait for a copy-in after the first round), then copy each round out
+    // once every rank's movers finished it.
+    const bool ahead = a.ahead && rounds <= a.nbuf;
+    for (unsigned s = 0; ahead && s < rounds; ++s) {
+      unsigned long long rbase, rlen;
+      ar_round(s, a.bytes, a.round, a.ramp, &rbase, &rlen);
+      char* buf = a.uc + (s % a.nbuf) * a.buf_stride;
+      for (int q = 0; q < n; ++q) {
+        unsigned long long lo, hi;
+        portion(rlen, n, q, &lo, &hi);
+        cp.copy(buf + lo, a.send + rbase + lo, hi - lo, 2);
+      }
+      cp.flush();
+      group_publish(a, g, a.base + s + 1);
+    }
+    for (unsigned s = 0; ahead && s < rounds; ++s) {
+      if (!group_wait(a, g, kMover, a.base + s + 1, -1)) break;
+      cp.acquired();
+      unsigned long long rbase, rlen;
+      ar_round(s, a.bytes, a.round, a.ramp, &rbase, &rlen);
+      const char* buf = a.uc + (s % a.nbuf) * a.buf_stride;
+      for (int q = 0; q < n; ++q) {
+        unsigned long long lo, hi;
+        portion(rlen, n, q, &lo, &hi);
+        cp.copy(a.recv + rbase + lo, buf + lo, hi - lo, 1);
+      }
+    }
+    for (unsigned s = 0; !ahead && s < rounds + 2; ++s) {
       if (s >= 2) {
         if (!group_wait(a, g, kMover, a.base + s - 1, -1)) break;
         cp.acquired();
@@ -603,6 +632,7 @@ __global__ void __launch_bounds__(TMA ? 640 : 768, 1) nvls_allreduce_kernel(cons
       cp.flush();
       group_publish(a, g, a.base + s + 1);
     }
+    cp.flush();
     cp.finish();
   }
   trace_end(a, g);
@@ -965,6 +995,7 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.uc_flags = reinterpret_cast<unsigned*>(a.uc + size_t(c->nbuf) * c->stride);
   a.mc_flags = reinterpret_cast<unsigned*>(a.mc + size_t(c->nbuf) * c->stride);
   a.nbuf = c->nbuf;
+  a.ahead = p.nvls_ahead ? 1 : 0;
   a.bytes = ar ? range : plan.desc.bytes;
   // A smaller round than the scratch holds (a tuned kernel shape) uses the
   // same buffers; 32-byte multiples of every slice stay aligned.

@@ -71,6 +71,16 @@ def test_nvls_allreduce_holds(n, rounds, bufs, in_first):
     assert r.ok, (r.violation, r.trace)
 
 
+@pytest.mark.parametrize("n,rounds", [(2, 4), (3, 3)])
+def test_nvls_allreduce_ahead_with_a_buffer_per_round(n, rounds):
+    """Every copy-in first, then the copy-outs: safe with a buffer per
+    round, and refuted when the buffers are fewer than the rounds."""
+    r = m.check_nvls_allreduce(nranks=n, rounds=rounds, bufs=rounds, ahead=True)
+    assert r.ok, (r.violation, r.trace)
+    r = m.check_nvls_allreduce(nranks=n, rounds=rounds, bufs=rounds - 1, ahead=True)
+    assert not r.ok and r.violation == "RoundsInOrder"
+
+
 @pytest.mark.parametrize("n", [2, 3])
 def test_nvls_allreduce_copy_in_first_needs_three_buffers(n):
     """Copying round s in before round s-2 is out overwrites round s-2's
