@@ -41,6 +41,12 @@ namespace nb {
 
 const char* build_id() { return NB_BUILD_ID; }
 
+// The calibration cache key: the GPUs and driver, and this build, so a cache
+// written by another build (other routes, other kernel shapes) is not used.
+std::string build_cache_key(const int* devices, int n) {
+  return calib_cache_key(devices, n) + "-b" + build_id();
+}
+
 namespace {
 
 struct ExitSummary {
@@ -182,7 +188,7 @@ void prewarm(const int* devices, int n) {
   }
   if (r.policy.calibrate && n > 1 && !r.calib_tried[n]) {
     r.calib_tried[n] = true;
-    const std::string key = calib_cache_key(devices, n);
+    const std::string key = build_cache_key(devices, n);
     CalibResult c;
     if (calib_load(r.policy.calib_cache, key, &c)) {
       r.summary.note("calibration loaded from " + r.policy.calib_cache);
@@ -708,7 +714,7 @@ void measure_crossover(void* const* comms_by_rank, const int* devices, int n) {
   }
   cudaGetLastError();
   r.refresh_policy(n);
-  if (!r.policy.calib_cache.empty()) calib_save(r.policy.calib_cache, calib_cache_key(devices, n), cal);
+  if (!r.policy.calib_cache.empty()) calib_save(r.policy.calib_cache, build_cache_key(devices, n), cal);
 }
 
 namespace {

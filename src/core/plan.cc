@@ -900,7 +900,9 @@ void plan_gang_ll(Builder& b, const CliqueDesc& d) {
   const int n = b.n();
   for (int r = 0; r < n; ++r) b.nvls({Strm::Caller, uint8_t(r), 0}, r, d.bytes);
   b.plan().needs.oneshot = true;
-  b.plan().sm_bytes += d.bytes * size_t(n - 1) * size_t(n);
+  // NVLink bytes: every non-root reads the root's buffer (Broadcast); every
+  // rank moves its slot to or from each peer (AllGather, ReduceScatter).
+  b.plan().sm_bytes += d.bytes * size_t(n - 1) * (d.kind == Kind::Broadcast ? 1 : size_t(n));
 }
 
 // One rank: every collective except a scaled one (PreMulSum) is a copy of

@@ -1021,6 +1021,13 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   // the next call's epoch.
   unsigned long long steps = 0;
   a.ramp = ar && (op.nvls_ramp ? op.nvls_ramp == 2 : p.nvls_ramp) ? 1 : 0;
+  // A shape that would need more rounds than the scratch has buffers (a
+  // smaller round, the ramp) would reuse buffers within the call: take the
+  // scratch's own round, uniform, instead.
+  if (ar && ar_rounds(a.bytes, a.round, a.ramp) > c->nbuf) {
+    a.round = c->round;
+    a.ramp = 0;
+  }
   if (ar) {
     steps = ar_rounds(a.bytes, a.round, a.ramp) + 2ull;
   } else {
