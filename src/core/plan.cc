@@ -782,7 +782,9 @@ void plan_bc_ring(Builder& b, const CliqueDesc& d) {
 // Hybrid AllReduce: the first share of the message through the switch (an
 // NVLS gang on `hybrid_blocks` SMs per GPU, launched first), the rest by the
 // two-shot P2P kernel, which the remaining SMs run at the same time; both
-// shares cross NVLink concurrently. The split point is 4 KiB aligned.
+// shares cross NVLink concurrently. The split point is 4 KiB aligned. The
+// gate refuses the hybrid routes (wrong data at 4 GiB on the GPU, slower
+// than NVLS alone where correct); the planners stay for the plan checks.
 int split_ppm(const Policy& p, const Shares& s) { return s.split_ppm > 0 ? s.split_ppm : p.hybrid_nvls_ppm; }
 uint16_t split_blocks(const Policy& p, const Shares& s) {
   return uint16_t(s.split_blocks > 0 ? s.split_blocks : p.hybrid_blocks);
