@@ -44,6 +44,8 @@ def test_oracle_matches_library_gate(n, nvls):
     envs = [{}, {"NCCL_B200_AR_MIN": "1M", "NCCL_B200_RS_MIN": "64K"},
             {"NCCL_B200_ALGO": "ar=oneshot,rs=push,ag=push,bc=ring", "NCCL_B200_AR_MIN": "4K"},
             {"NCCL_B200_ALGO": "ar=hybrid,rs=hybrid,ag=nvls,bc=nvls"},
+            {"NCCL_B200_ALGO": "ar=twoshot_ll,rs=ll,ag=ll,bc=ll", "NCCL_B200_AR_MIN": "4K",
+             "NCCL_B200_AG_MIN": "4K", "NCCL_B200_RS_MIN": "4K", "NCCL_B200_BC_MIN": "4K"},
             {"NCCL_B200_NVLS": "off"}, {"NCCL_B200_MAX_BYTES": "64M"},
             {"NCCL_B200_ALLGATHER": "0"}, {"NCCL_B200_DISABLE": "1"}]
     counts = [0, 1, 1023, (32 << 20) // 4 - 1, (32 << 20) // 4, (32 << 20) // 4 + 3, (40 << 20) // 4,
@@ -99,3 +101,18 @@ def test_measured_crossover_lowers_unset_thresholds_only():
     # An explicit threshold wins over the measurement.
     assert oracle.expected_route("allreduce", "float32", "sum", small, 2, calib=rec,
                                  rules=oracle.Rules({"NCCL_B200_AR_MIN": "32M"})) == "nccl"
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_oracle_low_latency_copies_need_whole_vectors(n):
+    """The low-latency AllGather/Broadcast copies move whole 16-byte vectors:
+    an odd payload or a misaligned buffer takes the static route, in the
+    library and in the oracle alike."""
+    env = {"NCCL_B200_ALGO": "ag=ll,bc=ll", "NCCL_B200_AG_MIN": "1", "NCCL_B200_BC_MIN": "1"}
+    rules = oracle.Rules(env)
+    for kind in ("allgather", "broadcast"):
+        for count, aligned in (((1 << 20) // 4, True), ((1 << 20) // 4 + 1, True), ((1 << 20) // 4, False)):
+            want = oracle.expected_route(kind, "float32", "sum", count, n, aligned=aligned, rules=rules)
+            got = library_route(kind, "float32", "sum", count, n, env, False, aligned=aligned)
+            assert got == want, (kind, count, aligned, got, want)
+            assert (want in ("ag_ll", "bc_ll")) == (aligned and count % 4 == 0), (kind, count, aligned, want)
