@@ -505,7 +505,8 @@ SPECS = {
     "PushReduceN": (check_push_reduce, {"N": "nranks", "R": "rounds", "D": "depth",
                                         "SkipConsumedWait": "skip_consumed_wait"}),
     "NvlsAllReduceN": (check_nvls_allreduce, {"N": "nranks", "R": "rounds", "B": "bufs",
-                                              "MoverWaitsAll": "mover_waits_all", "InFirst": "in_first"}),
+                                              "MoverWaitsAll": "mover_waits_all", "InFirst": "in_first",
+                                              "Ahead": "ahead"}),
     "BroadcastChainN": (check_broadcast_chain, {"N": "nranks", "S": "steps", "SkipWait": "skip_wait"}),
     "OneShotBarrierN": (check_oneshot_barrier, {"N": "nranks", "C": "calls", "Two": "two",
                                                 "SkipArrive": "skip_arrive", "SkipDepart": "skip_depart"}),
