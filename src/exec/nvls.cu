@@ -20,10 +20,12 @@
 // other group's unrelated work. Every wait is bounded by %globaltimer: on
 // expiry the kernel writes a status word in mapped host memory and returns;
 // the host turns it into ncclUnhandledCudaError and disables the route.
-// The copier group can run as one warp of TMA bulk copies (cp.async.bulk
-// global -> shared on an mbarrier, shared -> global in bulk groups); those
-// copies read and write only this GPU's own memory (the user's buffers and
-// the unicast view of its scratch). No load with cluster multicast is used.
+// By default the copier warps use system-scope loads and stores on the
+// scratch side (ld/st.relaxed.sys); on request (NCCL_B200_NVLS_STRONG=0)
+// the copier group runs as one warp of TMA bulk copies (cp.async.bulk
+// global -> shared on an mbarrier, shared -> global in bulk groups). Either
+// reads and writes only this GPU's own memory (the user's buffers and the
+// unicast view of its scratch). No load with cluster multicast is used.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
