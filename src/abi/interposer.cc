@@ -239,6 +239,14 @@ void prewarm(const int* devices, int n) {
     if (r.summary.enabled()) r.summary.note("prewarm_failed " + why);
   }
   r.exec.drain(devices, n);
+  size_t nv_bytes = 0, nv_round = 0;
+  unsigned nv_bufs = 0;
+  if (r.summary.enabled() && nvls_scratch(devices, n, &nv_bytes, &nv_bufs, &nv_round)) {
+    char line[160];
+    std::snprintf(line, sizeof line, "nvls scratch n=%d: %zu MiB per GPU, %u round buffers of %zu MiB", n,
+                  nv_bytes >> 20, nv_bufs, nv_round >> 20);
+    r.summary.note(line);
+  }
 }
 
 namespace {

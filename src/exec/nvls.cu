@@ -1089,4 +1089,14 @@ unsigned nvls_status(const int* devices, int n) {
   return c && c->status ? *static_cast<volatile unsigned*>(c->status) : 0u;
 }
 
+bool nvls_scratch(const int* devices, int n, size_t* bytes, unsigned* buffers, size_t* round) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Context* c = find(devices, n);
+  if (!c) return false;
+  *bytes = c->size;
+  *buffers = c->nbuf;
+  *round = c->round;
+  return true;
+}
+
 }  // namespace nb

@@ -31,6 +31,9 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
 // Device-side status of the last NVLS gang on this device set: 0 ok,
 // nonzero = a bounded wait expired. Reading it synchronizes nothing.
 unsigned nvls_status(const int* devices, int n);
+// The multicast scratch of this device set, once created: bytes bound per
+// GPU, round buffers and round size. False when there is none.
+bool nvls_scratch(const int* devices, int n, size_t* bytes, unsigned* buffers, size_t* round);
 // Phase timing of one rank's NVLS kernels since the last reset (policy
 // nvls_trace): out = mean over blocks of {mover busy, mover waiting, copier
 // busy, copier waiting, mover total, copier total} in ns. Synchronizes that
