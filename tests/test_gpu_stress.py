@@ -136,3 +136,15 @@ def test_stress_large_size_edges_and_cap(n):
     by = {r[0]: r for r in rows}
     assert by["cap_allreduce_at"][6] != "nccl" and by["cap_allreduce_above"][6] == "nccl", log
     assert by["cap_broadcast_above"][6] == "nccl", log
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_stress_nvls_copy_in_ahead_edges(n):
+    """The NVLS AllReduce with every copy-in first (NCCL_B200_NVLS_AHEAD=1,
+    a scratch buffer per round): every pipeline edge exact."""
+    need_gpus(n)
+    env = dict(EDGES, NCCL_B200_NVLS="on", NCCL_B200_NVLS_AHEAD="1")
+    rc, rows, log = run(["--gpus", str(n), "--iters", "2", "--no-standard", "--no-boundary", "--edges",
+                         "--algo", "ar=nvls", "--filter", "_ar"], env=env)
+    assert rc == 0, log
+    assert rows and all(r[4] == "PASS" for r in rows), log
