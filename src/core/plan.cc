@@ -897,7 +897,9 @@ void plan_ar_twoshot_ll(Builder& b, const CliqueDesc& d) {
 // slot r from every input into its output (ReduceScatter), stores its slot
 // into slot r of every rank's output (AllGather), or copies the root's
 // buffer into its output (Broadcast), between the in-kernel arrive and
-// depart barriers.
+// depart barriers. Counterparts: the reference's event-ordered copy-engine
+// copies of the peer's slot (shim/nccl_collectives_shim.cu:626) and of the
+// root's buffer (:674), for two GPUs.
 void plan_gang_ll(Builder& b, const CliqueDesc& d) {
   const int n = b.n();
   for (int r = 0; r < n; ++r) b.nvls({Strm::Caller, uint8_t(r), 0}, r, d.bytes);
