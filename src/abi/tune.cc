@@ -36,8 +36,11 @@ struct Candidate {
 // more requests in flight may pay. No shape shrinks the round: the scratch
 // holds one buffer per round of the largest message, and smaller rounds
 // would reuse buffers within a call. The ramped schedule (NCCL_B200_NVLS_RAMP)
-// measured no gain on 2 GPUs and is not a candidate.
-constexpr int kNvlsShapes[][4] = {{0, 0, 0, 0}, {608, 4, 0, 0}, {608, 8, 0, 0}};
+// measured no gain on 2 GPUs and is not a candidate. From four ranks the
+// tuning also tries the copier that copies every round in first (the movers
+// then never wait for a copy-in); on 2 GPUs it measured 2 % slower.
+constexpr int kNvlsShapes[][5] = {{0, 0, 0, 0, 0}, {608, 4, 0, 0, 0}, {608, 8, 0, 0, 0}, {0, 0, 0, 0, 2},
+                                  {608, 8, 0, 0, 2}};
 
 // Every candidate route of a kind; a host-lane variant is added wherever the
 // rate model (measured PCIe, NVLink and fold rates) predicts a host share.
@@ -100,7 +103,8 @@ std::vector<Candidate> candidates(Kind k, int n, bool nvls, const CalibResult& r
       }
       if (nvls && n >= 2)
         for (const auto& sh : kNvlsShapes)
-          v.push_back({Algo::ArNvls, 0, 0, 0, 0, 0, 0, pack_nvls_shape(sh[0], sh[1], sh[2], sh[3])});
+          if (sh[4] == 0 || n >= 4)  // copy-in first measured slower on 2 GPUs
+            v.push_back({Algo::ArNvls, 0, 0, 0, 0, 0, 0, pack_nvls_shape(sh[0], sh[1], sh[2], sh[3], sh[4])});
       v.push_back({Algo::ArPush, 0, 0, 0, 0});
       break;
     case Kind::ReduceScatter:

@@ -61,15 +61,18 @@ struct CalibResult {
   int engage_kib[4] = {0, 0, 0, 0};
 };
 
-// An NVLS kernel shape in one int: ramp * 10^9 + movers (threads) * 100000 +
-// unroll * 10000 + round MiB (each part 0 = the policy's; ramp 1 = uniform
-// AllReduce rounds, 2 = ramped first and last rounds).
-inline int pack_nvls_shape(int movers, int unroll, int round_mib, int ramp = 0) {
-  return ramp * 1000000000 + movers * 100000 + unroll * 10000 + round_mib;
+// An NVLS kernel shape in one int: (ramp + 3 * ahead) * 2 * 10^8 + movers
+// (threads, below 2000) * 10^5 + unroll * 10^4 + round MiB. Each part 0 =
+// the policy's; ramp 1 = uniform AllReduce rounds, 2 = ramped first and
+// last rounds; ahead 1 = the copier's usual order, 2 = every copy-in first.
+inline int pack_nvls_shape(int movers, int unroll, int round_mib, int ramp = 0, int ahead = 0) {
+  return (ramp + 3 * ahead) * 200000000 + movers * 100000 + unroll * 10000 + round_mib;
 }
 inline void unpack_nvls_shape(int v, Shares* s) {
-  s->nvls_ramp = v / 1000000000;
-  v %= 1000000000;
+  const int sched = v / 200000000;
+  s->nvls_ramp = sched % 3;
+  s->nvls_ahead = sched / 3;
+  v %= 200000000;
   s->nvls_movers = v / 100000;
   s->nvls_unroll = (v / 10000) % 10;
   s->nvls_round_mib = v % 10000;

@@ -335,6 +335,20 @@ uint16_t nb_float_to_bf16(float f) { return float_to_bf16(f); }
 float nb_bf16_to_float(uint16_t h) { return bf16_to_float(h); }
 
 // Policy field readback for tests: returns the value as a double.
+// Pack an NVLS kernel shape and read it back: out = {movers, unroll,
+// round MiB, ramp, ahead}. Returns the packed value.
+int nb_nvls_shape(int movers, int unroll, int round_mib, int ramp, int ahead, int* out) {
+  const int v = pack_nvls_shape(movers, unroll, round_mib, ramp, ahead);
+  Shares s;
+  unpack_nvls_shape(v, &s);
+  out[0] = s.nvls_movers;
+  out[1] = s.nvls_unroll;
+  out[2] = s.nvls_round_mib;
+  out[3] = s.nvls_ramp;
+  out[4] = s.nvls_ahead;
+  return v;
+}
+
 // The NVLS AllReduce round schedule: the number of rounds, and round s's
 // [base, base + len) when s is below it.
 int nb_nvls_ar_round(uint64_t bytes, uint64_t round, int ramp, unsigned s, uint64_t* base, uint64_t* len) {

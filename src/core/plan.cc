@@ -755,6 +755,7 @@ void plan_ar_nvls(Builder& b, const CliqueDesc& d, const Policy& p, const Shares
     op.nvls_unroll = uint8_t(std::max(0, s.nvls_unroll));
     op.nvls_round = size_t(std::max(0, s.nvls_round_mib)) << 20;
     op.nvls_ramp = uint8_t(std::clamp(s.nvls_ramp, 0, 2));
+    op.nvls_ahead = uint8_t(std::clamp(s.nvls_ahead, 0, 2));
   }
   b.plan().needs.nvls_bytes = p.nvls_round_bytes;
   b.plan().sm_bytes += d.bytes * size_t(n);  // ~S in and S out per GPU via the switch

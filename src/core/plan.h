@@ -109,6 +109,7 @@ struct PlanOp {
   uint16_t nvls_movers = 0;
   uint8_t nvls_unroll = 0;
   uint8_t nvls_ramp = 0;
+  uint8_t nvls_ahead = 0;  // AllReduce copier: 1 usual order, 2 every copy-in first
   size_t nvls_round = 0;
 };
 
@@ -141,6 +142,7 @@ struct Shares {
   int nvls_unroll = 0;
   int nvls_round_mib = 0;
   int nvls_ramp = 0;  // 0 = the policy's, 1 = uniform rounds, 2 = ramped
+  int nvls_ahead = 0;  // 0 = the policy's, 1 = usual copier order, 2 = every copy-in first
 };
 
 struct Plan {

@@ -997,7 +997,7 @@ cudaError_t nvls_launch(const PlanOp& op, const Plan& plan, const Binding& b, co
   a.uc_flags = reinterpret_cast<unsigned*>(a.uc + size_t(c->nbuf) * c->stride);
   a.mc_flags = reinterpret_cast<unsigned*>(a.mc + size_t(c->nbuf) * c->stride);
   a.nbuf = c->nbuf;
-  a.ahead = p.nvls_ahead ? 1 : 0;
+  a.ahead = (op.nvls_ahead ? op.nvls_ahead == 2 : p.nvls_ahead) ? 1 : 0;
   a.bytes = ar ? range : plan.desc.bytes;
   // A smaller round than the scratch holds (a tuned kernel shape) uses the
   // same buffers; 32-byte multiples of every slice stay aligned.

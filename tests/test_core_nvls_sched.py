@@ -32,3 +32,14 @@ def test_ramp_shape():
     # Below 4R the schedule is uniform.
     assert [ln for _, ln in c.nvls_ar_rounds(4 * R - 32, R, True)] == [R, R, R, R - 32]
     assert c.nvls_ar_rounds(8 * R, R, False) == [(i * R, R) for i in range(8)]
+
+
+def test_nvls_shape_packs_and_unpacks():
+    """A tuned NVLS kernel shape travels as one int (calibration cache):
+    every field reads back, and the largest shape stays below INT_MAX."""
+    import ctypes as C
+    L = c.lib()
+    out = (C.c_int * 5)()
+    for shape in [(0, 0, 0, 0, 0), (608, 4, 0, 0, 0), (608, 8, 0, 0, 2), (512, 8, 128, 2, 2), (1999, 9, 9999, 2, 2)]:
+        v = L.nb_nvls_shape(*shape, out)
+        assert 0 <= v < 2 ** 31 - 1 and tuple(out) == shape, (shape, v, tuple(out))
